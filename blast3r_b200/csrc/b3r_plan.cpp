@@ -1,0 +1,567 @@
+// Host planner: builds the static structure of one BA phase (b3r_plan_create).
+//
+// The reference rediscovers this structure on every LM iteration with torch.unique /
+// index_add_ inside its block-matrix algebra (inference/ba_solver.py:854-924, 1063-1071);
+// here it is computed once per phase, on the host, in O(n_obs * mean track length):
+//   * image -> (foc, tau, zcf) typed blocks honouring the enable rules of
+//     GaussNewtonSolver.enable (ba_solver.py:72-108);
+//   * the local (this rank's) eliminated tracks, ordered by (first image, id), with their
+//     observations grouped by track and packed into <=32-observation warp tasks;
+//   * per-image observation chunks for the image-major diagonal pass;
+//   * image-pair segments (from ALL tracks, so every rank shares one S pattern) and this
+//     rank's observation-pair lists bucketed by segment, cut into pair tasks;
+//   * the block-sparse pattern of S (upper block triangle) and every destination offset.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <new>
+#include "b3r_plan.h"
+#include "b3r_status.h"
+
+namespace b3r {
+namespace {
+
+struct TypeMap {
+  int n_true = 0, n_cols = 0;
+  bool zero = false;
+  std::vector<int> col;   // -1: removed
+};
+
+int make_type(int mode, const uint8_t* mask, int n, const char* name, TypeMap& t) {
+  t.n_true = n;
+  t.col.assign(n, 0);
+  if (mode == B3R_ENABLE_ALL || mode == B3R_ENABLE_ZERO) {
+    std::iota(t.col.begin(), t.col.end(), 0);
+    t.n_cols = n;
+    t.zero = (mode == B3R_ENABLE_ZERO);
+    return B3R_OK;
+  }
+  B3R_REQUIRE(mode == B3R_ENABLE_MASK, "bad enable mode %d for %s", mode, name);
+  B3R_REQUIRE(mask != nullptr, "mask for %s is NULL", name);
+  int c = 0;
+  for (int j = 0; j < n; ++j) t.col[j] = mask[j] ? c++ : -1;
+  if (c == 0) {   // every column removed: the reference falls back to ZerosMat (ba_solver.py:92-93)
+    std::iota(t.col.begin(), t.col.end(), 0);
+    t.n_cols = n;
+    t.zero = true;
+  } else {
+    t.n_cols = c;
+  }
+  return B3R_OK;
+}
+
+inline int round4(int x) { return (x + 3) & ~3; }
+
+}  // namespace
+
+// Host-side intermediate of the planner (kept out of the public struct).
+struct PlanBuild {
+  const b3r_plan_desc* d;
+  std::vector<int> img_of;                 // [n_obs]
+  TypeMap K, P, Z, X;
+  int nb = 0;
+  std::vector<int> img_bk, img_sc, img_node, img_cam;
+  std::vector<int> bsize, boff;
+  // all eliminated tracks (global), grouped
+  std::vector<int> all_ptr, all_obs;       // CSR over track id
+  std::vector<char> elim;                  // [n_tracks]
+  std::vector<char> obs_live;              // [n_obs] observation touches an active block
+  // local side
+  std::vector<int> loc_tracks, trk_col, perm_t, trk_t, img_t, pt_task, kof;
+  std::vector<int> c1_obs, c1_k, c1_chunk, c1_img;
+  // segments (global)
+  std::vector<int> seg_row_ptr, seg_col;   // CSR over row image
+  std::vector<int64_t> seg_cnt;
+  std::vector<int2> pairs;
+  std::vector<int64_t> task_pb;
+  std::vector<int> task_seg;
+  // pattern
+  std::vector<int> row_ptr, col_idx, val_off;
+  std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
+  int64_t nnz = 0;
+};
+
+static int build_maps(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int I = d.n_imgs;
+  B3R_REQUIRE(I >= 1 && d.n_cams >= 1 && d.n_nodes >= 1 && d.n_tracks >= 0 && d.n_obs >= 0,
+              "bad sizes");
+  B3R_REQUIRE(d.C >= 1 && d.C <= 32, "C=%d out of range [1, 32]", d.C);
+  B3R_REQUIRE(d.n_obs < (int64_t(1) << 31), "n_obs must be < 2^31 per plan");
+  B3R_REQUIRE(d.infos != nullptr && (d.n_obs == 0 || d.pids != nullptr), "NULL infos/pids");
+  B3R_REQUIRE(d.track_begin >= 0 && d.track_begin <= d.track_end && d.track_end <= d.n_tracks,
+              "bad track range [%d, %d)", d.track_begin, d.track_end);
+  const int32_t* cum = d.infos;
+  const int32_t* node = d.infos + I;
+  const int32_t* cam = d.infos + 2 * I;
+  int64_t prev = 0;
+  for (int i = 0; i < I; ++i) {
+    B3R_REQUIRE(cum[i] >= prev, "infos[0] must be non-decreasing (image %d)", i);
+    B3R_REQUIRE(node[i] >= 0 && node[i] < d.n_nodes, "node id %d of image %d out of range", node[i], i);
+    B3R_REQUIRE(cam[i] >= 0 && cam[i] < d.n_cams, "cam id %d of image %d out of range", cam[i], i);
+    prev = cum[i];
+  }
+  B3R_REQUIRE(prev == d.n_obs, "infos[0][-1]=%lld must equal n_obs=%lld", (long long)prev,
+              (long long)d.n_obs);
+  B.img_of.resize(d.n_obs);
+  int64_t o = 0;
+  for (int i = 0; i < I; ++i)
+    for (; o < cum[i]; ++o) B.img_of[o] = i;
+  for (int64_t j = 0; j < d.n_obs; ++j)
+    B3R_REQUIRE(d.pids[j] >= 0 && d.pids[j] < d.n_tracks, "pid %d of observation %lld out of range",
+                d.pids[j], (long long)j);
+
+  B3R_TRY(make_type(d.mode_K, d.mask_K, d.n_cams, "K", B.K));
+  B3R_TRY(make_type(d.mode_P, d.mask_P, d.n_nodes, "P", B.P));
+  B3R_TRY(make_type(d.mode_Z, d.mask_Z, d.n_imgs, "Z", B.Z));
+  B3R_TRY(make_type(d.mode_X, d.mask_X, d.n_tracks, "X", B.X));
+  const int nbK = B.K.n_cols, nbP = B.P.n_cols, nbZ = B.Z.n_cols;
+  B.nb = nbK + nbP + nbZ;
+  B.bsize.resize(B.nb);
+  B.boff.resize(B.nb);
+  int off = 0;
+  for (int p = 0; p < B.nb; ++p) {
+    B.bsize[p] = p < nbK ? 2 : (p < nbK + nbP ? 6 : d.C);
+    B.boff[p] = off;
+    off += B.bsize[p];
+  }
+  B.img_bk.assign(3 * I, -1);
+  B.img_sc.assign(3 * I, -1);
+  B.img_node.assign(node, node + I);
+  B.img_cam.assign(cam, cam + I);
+  for (int i = 0; i < I; ++i) {
+    int bk = (!B.K.zero && B.K.col[cam[i]] >= 0) ? B.K.col[cam[i]] : -1;
+    int bp = (!B.P.zero && B.P.col[node[i]] >= 0) ? nbK + B.P.col[node[i]] : -1;
+    int bz = (!B.Z.zero && B.Z.col[i] >= 0) ? nbK + nbP + B.Z.col[i] : -1;
+    B.img_bk[3 * i] = bk; B.img_bk[3 * i + 1] = bp; B.img_bk[3 * i + 2] = bz;
+    B.img_sc[3 * i] = bk >= 0 ? B.boff[bk] : -1;
+    B.img_sc[3 * i + 1] = bp >= 0 ? B.boff[bp] : -1;
+    B.img_sc[3 * i + 2] = bz >= 0 ? B.boff[bz] : -1;
+  }
+  return B3R_OK;
+}
+
+static inline bool img_live(const PlanBuild& B, int i) {
+  return B.img_bk[3 * i] >= 0 || B.img_bk[3 * i + 1] >= 0 || B.img_bk[3 * i + 2] >= 0;
+}
+
+static int build_tracks(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int T = d.n_tracks;
+  B.elim.assign(T, 0);
+  if (!B.X.zero)
+    for (int t = 0; t < T; ++t) B.elim[t] = B.X.col[t] >= 0;
+  B.obs_live.resize(d.n_obs);
+  for (int64_t o = 0; o < d.n_obs; ++o) B.obs_live[o] = img_live(B, B.img_of[o]);
+  // CSR of observations per eliminated track (all tracks; stable in o)
+  B.all_ptr.assign(T + 1, 0);
+  for (int64_t o = 0; o < d.n_obs; ++o)
+    if (B.elim[d.pids[o]]) B.all_ptr[d.pids[o] + 1]++;
+  for (int t = 0; t < T; ++t) B.all_ptr[t + 1] += B.all_ptr[t];
+  B.all_obs.resize(B.all_ptr[T]);
+  {
+    std::vector<int> fill(B.all_ptr.begin(), B.all_ptr.end() - 1);
+    for (int64_t o = 0; o < d.n_obs; ++o)
+      if (B.elim[d.pids[o]]) B.all_obs[fill[d.pids[o]]++] = (int)o;
+  }
+  // local tracks: eliminated, owned, non-empty; ordered by (first image, id)
+  for (int t = d.track_begin; t < d.track_end; ++t)
+    if (B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) B.loc_tracks.push_back(t);
+  std::stable_sort(B.loc_tracks.begin(), B.loc_tracks.end(), [&](int a, int b) {
+    return B.img_of[B.all_obs[B.all_ptr[a]]] < B.img_of[B.all_obs[B.all_ptr[b]]];
+  });
+  const int nT = (int)B.loc_tracks.size();
+  B.trk_col.resize(nT);
+  for (int tl = 0; tl < nT; ++tl) B.trk_col[tl] = B.X.col[B.loc_tracks[tl]];
+  int64_t n_loc = 0;
+  for (int t : B.loc_tracks) n_loc += B.all_ptr[t + 1] - B.all_ptr[t];
+  B.perm_t.resize(n_loc);
+  B.trk_t.resize(n_loc);
+  B.img_t.resize(n_loc);
+  B.kof.assign(d.n_obs, -1);
+  // Point tasks: whole tracks packed greedily into <= 32 observations (one warp); a track
+  // longer than 32 gets a task of its own, which the kernels process in rounds.
+  B.trk_ptr.assign(nT + 1, 0);
+  for (int tl = 0; tl < nT; ++tl)
+    B.trk_ptr[tl + 1] = B.trk_ptr[tl] + (B.all_ptr[B.loc_tracks[tl] + 1] - B.all_ptr[B.loc_tracks[tl]]);
+  int64_t k = 0;
+  int cur = 0;          // observations in the open task
+  bool open = false, open_long = false;
+  for (int tl = 0; tl < nT; ++tl) {
+    const int t = B.loc_tracks[tl];
+    const int L = B.all_ptr[t + 1] - B.all_ptr[t];
+    if (open && (open_long || L > kPointTask || cur + L > kPointTask)) open = false;
+    if (!open) {
+      B.pt_task.push_back((int)k);
+      open = true;
+      open_long = false;
+      cur = 0;
+    }
+    for (int j = B.all_ptr[t]; j < B.all_ptr[t + 1]; ++j) {
+      const int o = B.all_obs[j];
+      B.perm_t[k] = o;
+      B.trk_t[k] = tl;
+      B.img_t[k] = B.img_of[o];
+      B.kof[o] = (int)k;
+      ++k;
+    }
+    cur += L;
+    open_long = L > kPointTask;
+  }
+  if (nT > 0) B.pt_task.push_back((int)k);
+  // image-major chunks over the observations this rank owns (pid in the track range)
+  int last_img = -1, in_chunk = 0;
+  for (int64_t o = 0; o < d.n_obs; ++o) {
+    const int t = d.pids[o];
+    if (t < d.track_begin || t >= d.track_end || !B.obs_live[o]) continue;
+    const int i = B.img_of[o];
+    if (i != last_img || in_chunk == kDiagChunk) {
+      B.c1_chunk.push_back((int)B.c1_obs.size());
+      B.c1_img.push_back(i);
+      last_img = i;
+      in_chunk = 0;
+    }
+    B.c1_obs.push_back((int)o);
+    B.c1_k.push_back(B.kof[o]);
+    ++in_chunk;
+  }
+  B.c1_chunk.push_back((int)B.c1_obs.size());
+  return B3R_OK;
+}
+
+}  // namespace b3r
+
+namespace b3r {
+
+// Segments: for each row image i, the sorted partner images i' >= i sharing an eliminated
+// track (over ALL tracks).  For i' == i the segment only exists when a track has two
+// live observations in image i.
+static int build_segments(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int I = d.n_imgs;
+  B.seg_row_ptr.assign(I + 1, 0);
+  std::vector<int> stamp(I, -1), partners;
+  const int32_t* cum = d.infos;
+  for (int i = 0; i < I; ++i) {
+    partners.clear();
+    const int64_t o0 = i ? cum[i - 1] : 0, o1 = cum[i];
+    for (int64_t o = o0; o < o1; ++o) {
+      const int t = d.pids[o];
+      if (!B.elim[t] || !B.obs_live[o]) continue;
+      for (int j = B.all_ptr[t]; j < B.all_ptr[t + 1]; ++j) {
+        const int o2 = B.all_obs[j];
+        if (o2 <= o || !B.obs_live[o2]) continue;   // o2 > o  =>  img(o2) >= i
+        const int i2 = B.img_of[o2];
+        if (stamp[i2] != i) { stamp[i2] = i; partners.push_back(i2); }
+      }
+    }
+    std::sort(partners.begin(), partners.end());
+    B.seg_col.insert(B.seg_col.end(), partners.begin(), partners.end());
+    B.seg_row_ptr[i + 1] = (int)B.seg_col.size();
+  }
+  return B3R_OK;
+}
+
+static inline int64_t seg_lookup(const PlanBuild& B, int i, int i2) {
+  const int* a = B.seg_col.data() + B.seg_row_ptr[i];
+  const int* e = B.seg_col.data() + B.seg_row_ptr[i + 1];
+  const int* p = std::lower_bound(a, e, i2);
+  return (p != e && *p == i2) ? (int64_t)(p - B.seg_col.data()) : -1;
+}
+
+// This rank's observation pairs, bucketed by segment (stable in local track order), and
+// the pair tasks.
+static int build_pairs(PlanBuild& B) {
+  const int64_t S = (int64_t)B.seg_col.size();
+  B.seg_cnt.assign(S + 1, 0);
+  auto for_pairs = [&](auto&& fn) {
+    int64_t k0 = 0;
+    for (size_t tl = 0; tl < B.loc_tracks.size(); ++tl) {
+      const int t = B.loc_tracks[tl];
+      const int L = B.all_ptr[t + 1] - B.all_ptr[t];
+      for (int a = 0; a < L; ++a) {
+        const int ka = (int)(k0 + a);
+        const int oa = B.perm_t[ka];
+        if (!B.obs_live[oa]) continue;
+        for (int b = a + 1; b < L; ++b) {
+          const int kb = (int)(k0 + b);
+          const int ob = B.perm_t[kb];
+          if (!B.obs_live[ob]) continue;
+          fn(seg_lookup(B, B.img_of[oa], B.img_of[ob]), ka, kb);
+        }
+      }
+      k0 += L;
+    }
+  };
+  int bad = 0;
+  for_pairs([&](int64_t s, int, int) { if (s < 0) ++bad; else B.seg_cnt[s + 1]++; });
+  B3R_REQUIRE(bad == 0, "internal: %d pairs without a segment", bad);
+  for (int64_t s = 0; s < S; ++s) B.seg_cnt[s + 1] += B.seg_cnt[s];
+  const int64_t P = B.seg_cnt[S];
+  try {
+    B.pairs.resize(P);
+  } catch (const std::bad_alloc&) {
+    return fail(B3R_E_NOMEM, "cannot allocate %lld observation pairs", (long long)P);
+  }
+  {
+    std::vector<int64_t> fill(B.seg_cnt.begin(), B.seg_cnt.end() - 1);
+    for_pairs([&](int64_t s, int ka, int kb) { B.pairs[fill[s]++] = make_int2(ka, kb); });
+  }
+  for (int64_t s = 0; s < S; ++s)
+    for (int64_t p = B.seg_cnt[s]; p < B.seg_cnt[s + 1]; p += kPairTask) {
+      B.task_pb.push_back(p);
+      B.task_seg.push_back((int)s);
+    }
+  B.task_pb.push_back(P);
+  return B3R_OK;
+}
+
+static inline int pat_lookup(const PlanBuild& B, int p, int q) {
+  const int* a = B.col_idx.data() + B.row_ptr[p];
+  const int* e = B.col_idx.data() + B.row_ptr[p + 1];
+  const int* it = std::lower_bound(a, e, q);
+  if (it == e || *it != q) return -1;
+  return B.val_off[it - B.col_idx.data()];
+}
+
+static int build_pattern(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int I = d.n_imgs, nb = B.nb;
+  std::vector<uint64_t> keys;
+  keys.reserve((size_t)nb + 6 * I + 9 * B.seg_col.size());
+  auto add = [&](int p, int q) {
+    if (p < 0 || q < 0) return;
+    if (p > q) std::swap(p, q);
+    keys.push_back((uint64_t)p * (uint64_t)nb + (uint64_t)q);
+  };
+  for (int p = 0; p < nb; ++p) add(p, p);
+  const int32_t* cum = d.infos;
+  for (int i = 0; i < I; ++i) {
+    const int64_t n_i = cum[i] - (i ? cum[i - 1] : 0);
+    if (n_i == 0) continue;
+    for (int a = 0; a < 3; ++a)
+      for (int b = a; b < 3; ++b) add(B.img_bk[3 * i + a], B.img_bk[3 * i + b]);
+  }
+  for (int i = 0; i < I; ++i)
+    for (int s = B.seg_row_ptr[i]; s < B.seg_row_ptr[i + 1]; ++s) {
+      const int i2 = B.seg_col[s];
+      for (int a = 0; a < 3; ++a)
+        for (int b = 0; b < 3; ++b) add(B.img_bk[3 * i + a], B.img_bk[3 * i2 + b]);
+    }
+  std::sort(keys.begin(), keys.end());
+  keys.erase(std::unique(keys.begin(), keys.end()), keys.end());
+  B.row_ptr.assign(nb + 1, 0);
+  B.col_idx.resize(keys.size());
+  B.val_off.resize(keys.size());
+  int64_t v = 0;
+  for (size_t j = 0; j < keys.size(); ++j) {
+    const int p = (int)(keys[j] / nb), q = (int)(keys[j] % nb);
+    B.row_ptr[p + 1]++;
+    B.col_idx[j] = q;
+    B3R_REQUIRE(v < (int64_t(1) << 31), "S has more than 2^31 values");
+    B.val_off[j] = (int)v;
+    v += (int64_t)B.bsize[p] * B.bsize[q];
+  }
+  for (int p = 0; p < nb; ++p) B.row_ptr[p + 1] += B.row_ptr[p];
+  B.nnz = v;
+  B.blk_row.resize(keys.size());
+  for (int p = 0; p < nb; ++p)
+    for (int j = B.row_ptr[p]; j < B.row_ptr[p + 1]; ++j) B.blk_row[j] = p;
+  // destinations of every segment's 9 sub-blocks
+  const int64_t S = (int64_t)B.seg_col.size();
+  B.seg_dst.assign(9 * S, -1);
+  B.seg_mode.assign(S, 0);
+  for (int i = 0; i < I; ++i)
+    for (int s = B.seg_row_ptr[i]; s < B.seg_row_ptr[i + 1]; ++s) {
+      const int i2 = B.seg_col[s];
+      int mode = 0;
+      for (int a = 0; a < 3; ++a)
+        for (int b = 0; b < 3; ++b) {
+          const int p = B.img_bk[3 * i + a], q = B.img_bk[3 * i2 + b];
+          int m = kModeNone, off = -1;
+          if (p >= 0 && q >= 0) {
+            if (p < q) { m = kModeDirect; off = pat_lookup(B, p, q); }
+            else if (p > q) { m = kModeTrans; off = pat_lookup(B, q, p); }
+            else { m = kModeSym; off = pat_lookup(B, p, p); }
+            B3R_REQUIRE(off >= 0, "internal: segment block (%d,%d) missing from pattern", p, q);
+          }
+          B.seg_dst[9 * s + 3 * a + b] = off;
+          mode |= m << (2 * (3 * a + b));
+        }
+      B.seg_mode[s] = mode;
+    }
+  // each image's own diagonal-segment destinations: (f,f),(f,t),(f,z),(t,t),(t,z),(z,z)
+  static const int AB[6][2] = {{0, 0}, {0, 1}, {0, 2}, {1, 1}, {1, 2}, {2, 2}};
+  B.img_dst.assign(6 * I, -1);
+  for (int i = 0; i < I; ++i)
+    for (int j = 0; j < 6; ++j) {
+      const int p = B.img_bk[3 * i + AB[j][0]], q = B.img_bk[3 * i + AB[j][1]];
+      if (p >= 0 && q >= 0) B.img_dst[6 * i + j] = pat_lookup(B, p, q);
+    }
+  // diagonal scalar positions
+  const int ncp = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
+  B.sdiag_pos.resize(ncp);
+  for (int p = 0; p < nb; ++p) {
+    const int base = pat_lookup(B, p, p), bs = B.bsize[p];
+    for (int r = 0; r < bs; ++r) B.sdiag_pos[B.boff[p] + r] = base + r * bs + r;
+  }
+  return B3R_OK;
+}
+
+}  // namespace b3r
+
+namespace b3r {
+namespace {
+
+// Packs host arrays into one device allocation (256-byte aligned pieces).
+struct Arena {
+  struct Item { const void* src; size_t bytes; void** dst; size_t off; };
+  std::vector<Item> items;
+  size_t total = 0;
+  template <typename T>
+  void add(const std::vector<T>& v, const T** dst) { add_raw(v.data(), v.size() * sizeof(T), (void**)dst); }
+  template <typename T>
+  void add_mut(size_t count, T** dst) { add_raw(nullptr, count * sizeof(T), (void**)dst); }
+  void add_raw(const void* src, size_t bytes, void** dst) {
+    items.push_back({src, bytes, dst, total});
+    total += (bytes + 255) & ~size_t(255);
+  }
+  int upload(void** base) {
+    if (total == 0) total = 256;
+    B3R_TRY(check_cuda(cudaMalloc(base, total), "plan cudaMalloc"));
+    for (auto& it : items) {
+      char* p = (char*)*base + it.off;
+      *it.dst = p;
+      if (it.src && it.bytes)
+        B3R_TRY(check_cuda(cudaMemcpy(p, it.src, it.bytes, cudaMemcpyHostToDevice), "plan upload"));
+    }
+    return B3R_OK;
+  }
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace b3r
+
+using namespace b3r;
+
+extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
+  B3R_REQUIRE(out != nullptr && desc != nullptr, "NULL argument");
+  *out = nullptr;
+  PlanBuild B;
+  B.d = desc;
+  try {
+    B3R_TRY(build_maps(B));
+    B3R_TRY(build_tracks(B));
+    B3R_TRY(build_segments(B));
+    B3R_TRY(build_pairs(B));
+    B3R_TRY(build_pattern(B));
+  } catch (const std::bad_alloc&) {
+    return fail(B3R_E_NOMEM, "host allocation failed while planning");
+  }
+  const bool host_only = desc->device < 0;   // planning only: pattern/info queries, no kernels
+  int prev_dev = 0;
+  if (!host_only) {
+    B3R_TRY(check_cuda(cudaGetDevice(&prev_dev), "cudaGetDevice"));
+    B3R_TRY(check_cuda(cudaSetDevice(desc->device), "cudaSetDevice"));
+  }
+  b3r_plan* P = new (std::nothrow) b3r_plan();
+  if (!P) return fail(B3R_E_NOMEM, "plan allocation failed");
+  P->device = desc->device;
+  DevPlan& d = P->d;
+  std::memset(&d, 0, sizeof(d));
+  d.n_imgs = desc->n_imgs; d.n_cams = desc->n_cams; d.n_nodes = desc->n_nodes;
+  d.n_tracks = desc->n_tracks; d.C = desc->C; d.n_obs = desc->n_obs;
+  d.R = round4(27 + desc->C);
+  d.nbK = B.K.n_cols; d.nbP = B.P.n_cols; d.nbZ = B.Z.n_cols; d.nb = B.nb;
+  d.off_P = 2 * d.nbK; d.off_Z = d.off_P + 6 * d.nbP;
+  d.n_cam_params = d.off_Z + desc->C * d.nbZ;
+  d.zeroK = B.K.zero; d.zeroP = B.P.zero; d.zeroZ = B.Z.zero; d.zeroX = B.X.zero;
+  d.n_loc = (int64_t)B.perm_t.size();
+  d.nT_loc = (int)B.loc_tracks.size();
+  d.n_pt_tasks = B.pt_task.empty() ? 0 : (int)B.pt_task.size() - 1;
+  d.n_c1 = (int64_t)B.c1_obs.size();
+  d.n_c1_chunks = (int)B.c1_img.size();
+  d.n_seg = (int64_t)B.seg_col.size();
+  d.n_pairs = (int64_t)B.pairs.size();
+  d.n_tasks = (int64_t)B.task_seg.size();
+  d.nnzb = (int64_t)B.col_idx.size();
+  d.nnz = B.nnz;
+
+  Arena A;
+  A.add(B.img_bk, &d.img_bk); A.add(B.img_sc, &d.img_sc); A.add(B.img_dst, &d.img_dst);
+  A.add(B.img_node, &d.img_node); A.add(B.img_cam, &d.img_cam);
+  A.add(B.perm_t, &d.perm_t); A.add(B.trk_t, &d.trk_t); A.add(B.img_t, &d.img_t);
+  A.add(B.loc_tracks, &d.trk_gid); A.add(B.trk_col, &d.trk_col); A.add(B.pt_task, &d.pt_task);
+  A.add_mut<float2>(d.n_loc, &d.t_pix); A.add_mut<float2>(d.n_loc, &d.t_std);
+  A.add_mut<float>((size_t)d.n_loc * desc->C, &d.t_dep);
+  A.add(B.c1_obs, &d.c1_obs); A.add(B.c1_k, &d.c1_k); A.add(B.c1_chunk, &d.c1_chunk);
+  A.add(B.c1_img, &d.c1_img);
+  A.add(B.seg_dst, &d.seg_dst); A.add(B.seg_mode, &d.seg_mode);
+  A.add(B.pairs, &d.pairs); A.add(B.task_pb, &d.task_pb); A.add(B.task_seg, &d.task_seg);
+  A.add(B.row_ptr, &d.row_ptr); A.add(B.col_idx, &d.col_idx); A.add(B.val_off, &d.val_off);
+  A.add(B.bsize, &d.bsize); A.add(B.boff, &d.boff); A.add(B.sdiag_pos, &d.sdiag_pos);
+  A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);
+  if (!host_only) {
+    int rc = A.upload(&P->dev_mem);
+    cudaSetDevice(prev_dev);
+    if (rc != B3R_OK) { if (P->dev_mem) cudaFree(P->dev_mem); delete P; return rc; }
+    P->dev_bytes = A.total;
+  }
+
+  // workspace layout: image records | track records | elimination records | staged r/w
+  P->ws_img = 0;
+  P->ws_trec = align256(P->ws_img + sizeof(float) * kImgRecFloats * (size_t)d.n_imgs);
+  P->ws_rec = align256(P->ws_trec + sizeof(float) * 24 * (size_t)d.nT_loc);
+  P->ws_rw = align256(P->ws_rec + sizeof(float) * (size_t)d.R * (size_t)d.n_loc);
+  P->ws_misc = align256(P->ws_rw + sizeof(float) * 6 * (size_t)d.n_loc);
+  const size_t ws_total = P->ws_misc + 256;
+
+  P->pat.row_ptr = std::move(B.row_ptr); P->pat.col_idx = std::move(B.col_idx);
+  P->pat.val_off = std::move(B.val_off); P->pat.bsize = std::move(B.bsize);
+  P->pat.boff = std::move(B.boff);
+  b3r_plan_info& I = P->info;
+  std::memset(&I, 0, sizeof(I));
+  I.n_obs = desc->n_obs; I.n_obs_local = d.n_loc; I.n_tracks_local = d.nT_loc;
+  I.n_blocks = d.nb; I.n_cam_params = d.n_cam_params; I.n_points = B.X.n_cols;
+  I.nnzb = d.nnzb; I.nnz = d.nnz; I.n_pairs = d.n_pairs; I.n_segments = d.n_seg;
+  I.n_pair_tasks = d.n_tasks; I.n_point_tasks = d.n_pt_tasks; I.n_diag_chunks = d.n_c1_chunks;
+  I.workspace_bytes = (int64_t)ws_total;
+  I.nb_K = d.nbK; I.nb_P = d.nbP; I.nb_Z = d.nbZ; I.off_P = d.off_P; I.off_Z = d.off_Z;
+  I.record_floats = d.R;
+  *out = P;
+  return B3R_OK;
+}
+
+extern "C" int b3r_plan_destroy(b3r_plan* plan) {
+  if (!plan) return B3R_OK;
+  cudaError_t e = cudaSuccess;
+  if (plan->dev_mem) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(plan->device);
+    e = cudaFree(plan->dev_mem);
+    cudaSetDevice(prev);
+  }
+  delete plan;
+  return check_cuda(e, "b3r_plan_destroy");
+}
+
+extern "C" int b3r_plan_get_info(const b3r_plan* plan, b3r_plan_info* info) {
+  B3R_REQUIRE(plan && info, "NULL argument");
+  *info = plan->info;
+  return B3R_OK;
+}
+
+extern "C" int b3r_plan_get_pattern(const b3r_plan* plan, int32_t* row_ptr, int32_t* col_idx,
+                                    int64_t* val_off, int32_t* block_size, int32_t* block_off) {
+  B3R_REQUIRE(plan != nullptr, "NULL plan");
+  const HostPattern& p = plan->pat;
+  if (row_ptr) std::copy(p.row_ptr.begin(), p.row_ptr.end(), row_ptr);
+  if (col_idx) std::copy(p.col_idx.begin(), p.col_idx.end(), col_idx);
+  if (val_off) for (size_t j = 0; j < p.val_off.size(); ++j) val_off[j] = p.val_off[j];
+  if (block_size) std::copy(p.bsize.begin(), p.bsize.end(), block_size);
+  if (block_off) std::copy(p.boff.begin(), p.boff.end(), block_off);
+  return B3R_OK;
+}

@@ -1,0 +1,102 @@
+// Internal plan: the static structure of one BA phase, built on the host once
+// (b3r_plan.cpp) and read by the fused linearization kernels (b3r_schur.cu).
+//
+// Index spaces
+//   o  image-sorted observation index (the reference layout, tracks.py:853-860)
+//   k  local observation index: observations of this rank's eliminated tracks, grouped
+//      by track, tracks ordered by (first image, track id) so that tracks seen by the
+//      same images are close in memory
+//   tl local track index (0 .. nT_loc-1), in that order
+//   p  typed parameter block: foc blocks [0, nbK), tau blocks [nbK, nbK+nbP), zcf blocks
+//      [nbK+nbP, nb), the column order of the reference solver (ba_solver.py:119, 229)
+//   s  segment: an ordered image pair (i <= i') that shares at least one eliminated track
+#pragma once
+#include <cstdint>
+#include <vector>
+#include <cuda_runtime.h>
+#include "../../include/b3r.h"
+
+namespace b3r {
+
+constexpr int kPairTask = 512;     // max observation pairs per pair task
+constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal chunk
+constexpr int kPointTask = 32;     // max observations per point task (one warp)
+constexpr int kImgRecFloats = 32;  // floats per per-image camera record
+
+// sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
+constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
+
+struct DevPlan {
+  int n_imgs, n_cams, n_nodes, n_tracks, C, R;   // R = floats per elimination record
+  int64_t n_obs;
+  int nbK, nbP, nbZ, nb, n_cam_params, off_P, off_Z;
+  int zeroK, zeroP, zeroZ, zeroX;
+
+  const int* img_bk;      // [n_imgs*3] active block of (foc, tau, zcf) per image, -1 if none
+  const int* img_sc;      // [n_imgs*3] scalar offset of those blocks, -1 if none
+  const int* img_dst;     // [n_imgs*6] value offset of the image's own (f,f),(f,t),(f,z),(t,t),(t,z),(z,z)
+  const int* img_node;    // [n_imgs]
+  const int* img_cam;     // [n_imgs]
+
+  // track-major side (eliminated tracks of this rank)
+  int64_t n_loc;
+  int nT_loc;
+  const int* perm_t;      // [n_loc] o of local observation k
+  const int* trk_t;       // [n_loc] tl of local observation k
+  const int* img_t;       // [n_loc] image of local observation k
+  const int* trk_gid;     // [nT_loc] global track id
+  const int* trk_col;     // [nT_loc] point column of the track in the delta vector
+  int n_pt_tasks;
+  const int* pt_task;     // [n_pt_tasks+1] first k of each point task
+  float2* t_pix;          // [n_loc] staged pix2d
+  float2* t_std;          // [n_loc] staged pix2d_std
+  float* t_dep;           // [C][n_loc] staged pix2d_dep (channel-major)
+
+  // image-major side (observations owned by this rank)
+  int64_t n_c1;
+  const int* c1_obs;      // [n_c1] o
+  const int* c1_k;        // [n_c1] k, -1 if the track is not eliminated
+  int n_c1_chunks;
+  const int* c1_chunk;    // [n_c1_chunks+1]
+  const int* c1_img;      // [n_c1_chunks]
+
+  // segments and their pair lists
+  int64_t n_seg, n_pairs, n_tasks;
+  const int* seg_dst;     // [n_seg*9] value offset of each (a,b) sub-block, -1 none
+  const int* seg_mode;    // [n_seg] 2 bits per sub-block (a*3+b)
+  const int2* pairs;      // [n_pairs] (k_row, k_col)
+  const int64_t* task_pb; // [n_tasks+1]
+  const int* task_seg;    // [n_tasks]
+
+  // S pattern
+  int64_t nnzb, nnz;
+  const int* row_ptr;     // [nb+1]
+  const int* col_idx;     // [nnzb]
+  const int* val_off;     // [nnzb]
+  const int* bsize;       // [nb]
+  const int* boff;        // [nb]
+  const int* sdiag_pos;   // [n_cam_params] position of each diagonal scalar in S_vals
+  const int* blk_row;     // [nnzb] block row of each stored block
+  const int* trk_ptr;     // [nT_loc+1] first k of each local track
+};
+
+struct HostPattern {
+  std::vector<int> row_ptr, col_idx, val_off, bsize, boff;
+};
+
+}  // namespace b3r
+
+struct b3r_plan {
+  b3r::DevPlan d;
+  b3r::HostPattern pat;
+  b3r_plan_info info;
+  int device = 0;
+  void* dev_mem = nullptr;
+  size_t dev_bytes = 0;
+  // workspace layout (byte offsets): image records | track records (24 floats: Hpp, g_p,
+  // then Cholesky factor and L^-1 g_p) | elimination records | staged r/w | misc scalars
+  size_t ws_img = 0, ws_trec = 0, ws_rec = 0, ws_rw = 0, ws_misc = 0;
+  int64_t n_pairs_total = 0;
+  bool staged = false;
+  const void* staged_src[3] = {nullptr, nullptr, nullptr};
+};

@@ -1,0 +1,991 @@
+// Part 2 of the C ABI: the fused per-LM-iteration linearization and Schur assembly.
+//
+// Replaces, for one LM iteration, GaussNewtonSolver.compute_jacobians + solve_delta up to
+// its PCG (naver/blast3r src/blast3r/inference/ba_solver.py:34-188).  J is never written
+// to memory.  Passes (one launch each, all on the caller's stream):
+//   prep      per-image camera records (one 128-byte line per image)
+//   points    track-major, one warp per <=32-observation task: per-track Hpp and g_p by a
+//             segmented warp scan, and the max |diag(Hpp)| for adaptive damping
+//   eliminate track-major: damped guarded 3x3 Cholesky Hpp = L L^T (sfm_jacobian_rigs.cu
+//             :578-617), z = L^-1 g_p, and per observation the elimination record
+//             Y = L^-1 Hpc in reduced form (3 x [f0 f1 tau0..5 zscale]) + its depth channels
+//   diag      image-major: per observation Hcc - Y^T Y and g_c - Y^T z expanded to the
+//             typed blocks of its image, reduced per image chunk in registers, one atomic
+//             per value per chunk; also diag(Hcc) for the damping and preconditioner
+//   pairs     segment-major: for every image pair (i, i') the sum over shared tracks of
+//             -Y_o^T Y_o' accumulated in registers over up to 512 observation pairs,
+//             records staged through shared memory, one atomic per value per task
+//   finalize  per-type adaptive damping of diag(S) (ba_solver.py:510-517, 572-582) and
+//             the Jacobi preconditioner of the reference's PCG (ba_solver.py:191-192)
+#include <algorithm>
+#include <cstring>
+#include "b3r_common.cuh"
+#include "b3r_plan.h"
+#include "b3r_status.h"
+
+namespace b3r {
+namespace {
+
+// Per-call state passed by value to the kernels.
+struct Ctx {
+  DevPlan d;
+  LinOpts o;
+  const float* K; const float* P_rig2c; int64_t P_stride; const float* P_w2rig;
+  const float* z_coefs; const float* pts3d;
+  const float* pix2d; const float* pix2d_std; const float* pix2d_dep; const int* pids;
+  const float* res; int64_t rs_n, rs_c;
+  const float* wpt; int64_t ws_n, ws_c; int w_cols;
+  float* img_rec;     // [n_imgs*32]
+  float* trec;        // [nT_loc*24]
+  float* rec;         // [n_loc*R]
+  float* t_rw;        // [6][n_loc] staged residual (0..2) and weight (3..5), general path
+  float* misc;        // [64]: 4..6 per-type max |diag A|
+  float* hpp_max;     // [1] max |diag(Hpp)| (caller-visible, all-reduced across ranks)
+  int no_grad_f_from_rz, optim_Z0, optim_Z_1st_cam;
+  float dampen;
+  int adaptive;
+};
+
+// ------------------------------------------------------------------------------------
+// small kernels
+// ------------------------------------------------------------------------------------
+__global__ void k_prep_images(Ctx c) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= c.d.n_imgs) return;
+  const int node = c.d.img_node[i], cam = c.d.img_cam[i];
+  const float* Prw = c.P_w2rig + (int64_t)node * 16;
+  const float* Pcr = c.P_rig2c + (int64_t)cam * c.P_stride;
+  const float* Kc = c.K + (int64_t)cam * 9;
+  float* r = c.img_rec + (int64_t)i * kImgRec;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+#pragma unroll
+    for (int b = 0; b < 3; ++b) { r[3 * a + b] = Prw[4 * a + b]; r[12 + 3 * a + b] = Pcr[4 * a + b]; }
+    r[9 + a] = Prw[4 * a + 3];
+    r[21 + a] = Pcr[4 * a + 3];
+  }
+  r[24] = Kc[0]; r[25] = Kc[4]; r[26] = Kc[2]; r[27] = Kc[5];
+  r[28] = r[29] = r[30] = r[31] = 0.f;
+}
+
+__global__ void k_stage_obs(DevPlan d, const float* __restrict__ pix2d, const float* __restrict__ std_,
+                            const float* __restrict__ dep) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= d.n_loc) return;
+  const int64_t o = d.perm_t[k];
+  if (pix2d) d.t_pix[k] = make_float2(pix2d[2 * o], pix2d[2 * o + 1]);
+  d.t_std[k] = make_float2(std_[2 * o], std_[2 * o + 1]);
+  for (int ch = 0; ch < d.C; ++ch) d.t_dep[(int64_t)ch * d.n_loc + k] = dep[o * d.C + ch];
+}
+
+__global__ void k_stage_rw(Ctx c) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= c.d.n_loc) return;
+  const int64_t o = c.d.perm_t[k], n = c.d.n_loc;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    c.t_rw[j * n + k] = c.res[o * c.rs_n + j * c.rs_c];
+    c.t_rw[(3 + j) * n + k] = c.wpt[o * c.ws_n + (c.w_cols == 1 ? 0 : j) * c.ws_c];
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// per-observation view used by every pass
+// ------------------------------------------------------------------------------------
+// Reduced camera-side Jacobian of one observation, rows scaled by sqrt(W):
+//   columns 0,1 focal (fx, fy), 2..7 tau, 8 "z scale" (the depth-coefficient columns are
+//   zs * dep_c in the depth row only, so they are carried as one column and expanded
+//   with the depth channels when written out).
+template <int CT>
+struct ObsView {
+  bool valid;
+  float Jpw[9];     // sqrt(W) * d r / d X        (3x3 row-major)
+  float Jp[9];      // d r / d X (unscaled, for g_p = J_p^T W r)
+  float Jcw[27];    // sqrt(W) * reduced camera J (3x9 row-major)
+  float Wr[3];      // W * r
+  float Jc2[27];    // unscaled reduced camera J (for g = J^T W r)
+  float dep[CT];    // depth channels as used by J (optim_Z0 / optim_Z_1st_cam applied)
+};
+
+// Masks of the image's blocks: bit 0 foc, 1 tau, 2 zcf active.
+__device__ __forceinline__ int image_mask(const DevPlan& d, int img) {
+  return (d.img_bk[3 * img] >= 0 ? 1 : 0) | (d.img_bk[3 * img + 1] >= 0 ? 2 : 0) |
+         (d.img_bk[3 * img + 2] >= 0 ? 4 : 0);
+}
+
+template <int CT>
+__device__ __forceinline__ void make_view(const Ctx& c, const ObsLin& L, float r0, float r1, float r2,
+                                          float w0, float w1, float w2, const float* dep_raw, int64_t o,
+                                          int mask, ObsView<CT>& V) {
+  V.valid = L.valid;
+  const float r[3] = {r0, r1, r2};
+  const float w[3] = {w0, w1, w2};
+  float sW[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float W = clampw(w[i], c.o.clamp_lo, c.o.clamp_hi);
+    V.Wr[i] = W * r[i];
+    sW[i] = sqrtf(W);
+  }
+  const bool mf = mask & 1, mt = mask & 2, mz = mask & 4;
+  const float jkf = c.no_grad_f_from_rz ? 0.f : L.Jkf;
+  float J[27];
+  J[0] = mf ? L.Jf0 : 0.f; J[1] = 0.f;
+  J[9] = 0.f;              J[10] = mf ? L.Jf1 : 0.f;
+  J[18] = mf ? jkf : 0.f;  J[19] = mf ? jkf : 0.f;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int t = 0; t < 6; ++t) J[9 * i + 2 + t] = mt ? L.Jt[6 * i + t] : 0.f;
+  }
+  J[8] = 0.f; J[17] = 0.f; J[26] = mz ? L.zs : 0.f;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+#pragma unroll
+    for (int a = 0; a < 9; ++a) { V.Jc2[9 * i + a] = J[9 * i + a]; V.Jcw[9 * i + a] = J[9 * i + a] * sW[i]; }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) { V.Jp[3 * i + j] = L.Jp[3 * i + j]; V.Jpw[3 * i + j] = L.Jp[3 * i + j] * sW[i]; }
+  }
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) V.dep[ch] = dep_raw[ch];
+  if (!c.optim_Z0 || (o == 0 && !c.optim_Z_1st_cam)) V.dep[0] = 0.f;
+}
+
+// Load + linearize local (track-sorted) observation k.
+template <int CT>
+__device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>& V, int& tl) {
+  const DevPlan& d = c.d;
+  const int img = d.img_t[k];
+  tl = d.trk_t[k];
+  const int gid = d.trk_gid[tl];
+  const Cam cam = load_cam(c.img_rec + (int64_t)img * kImgRec);
+  const float X[3] = {__ldg(c.pts3d + 3 * (int64_t)gid), __ldg(c.pts3d + 3 * (int64_t)gid + 1),
+                      __ldg(c.pts3d + 3 * (int64_t)gid + 2)};
+  const float2 s = d.t_std[k];
+  float dep[CT], zc[CT];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) {
+    dep[ch] = d.t_dep[(int64_t)ch * d.n_loc + k];
+    zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
+  }
+  ObsLin L;
+  float r0, r1, r2, w0, w1, w2;
+  if (c.pix2d) {
+    const float2 px = d.t_pix[k];
+    linearize_obs<float, true, true, CT>(cam, X, px.x, px.y, s.x, s.y, dep, zc, CT, c.o, L);
+    r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
+  } else {
+    linearize_obs<float, false, true, CT>(cam, X, 0.f, 0.f, s.x, s.y, dep, zc, CT, c.o, L);
+    const int64_t n = d.n_loc;
+    r0 = c.t_rw[k]; r1 = c.t_rw[n + k]; r2 = c.t_rw[2 * n + k];
+    w0 = c.t_rw[3 * n + k]; w1 = c.t_rw[4 * n + k]; w2 = c.t_rw[5 * n + k];
+  }
+  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, d.perm_t[k], image_mask(d, img), V);
+}
+
+// Load + linearize image-sorted observation o of image img.
+template <int CT>
+__device__ __forceinline__ void view_image(const Ctx& c, int64_t o, int img, const Cam& cam,
+                                           const float* zc, ObsView<CT>& V) {
+  const int pid = __ldg(c.pids + o);
+  const float X[3] = {__ldg(c.pts3d + 3 * (int64_t)pid), __ldg(c.pts3d + 3 * (int64_t)pid + 1),
+                      __ldg(c.pts3d + 3 * (int64_t)pid + 2)};
+  float dep[CT];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) dep[ch] = __ldg(c.pix2d_dep + o * CT + ch);
+  const float sx = __ldg(c.pix2d_std + 2 * o), sy = __ldg(c.pix2d_std + 2 * o + 1);
+  ObsLin L;
+  float r0, r1, r2, w0, w1, w2;
+  if (c.pix2d) {
+    linearize_obs<float, true, true, CT>(cam, X, __ldg(c.pix2d + 2 * o), __ldg(c.pix2d + 2 * o + 1), sx, sy,
+                                         dep, zc, CT, c.o, L);
+    r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
+  } else {
+    linearize_obs<float, false, true, CT>(cam, X, 0.f, 0.f, sx, sy, dep, zc, CT, c.o, L);
+    r0 = c.res[o * c.rs_n]; r1 = c.res[o * c.rs_n + c.rs_c]; r2 = c.res[o * c.rs_n + 2 * c.rs_c];
+    const int64_t wc = c.w_cols == 1 ? 0 : c.ws_c;
+    w0 = c.wpt[o * c.ws_n]; w1 = c.wpt[o * c.ws_n + wc]; w2 = c.wpt[o * c.ws_n + 2 * wc];
+  }
+  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, o, image_mask(c.d, img), V);
+}
+
+
+// Hpp (upper: 00 01 02 11 12 22) and g_p of one observation.
+template <int CT>
+__device__ __forceinline__ void point_terms(const ObsView<CT>& V, float v[9]) {
+  const int ia[6] = {0, 0, 0, 1, 1, 2}, ib[6] = {0, 1, 2, 1, 2, 2};
+#pragma unroll
+  for (int e = 0; e < 6; ++e) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) s += V.Jpw[3 * i + ia[e]] * V.Jpw[3 * i + ib[e]];
+    v[e] = s;
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) s += V.Jp[3 * i + j] * V.Wr[i];
+    v[6 + j] = s;
+  }
+}
+
+template <int CT>
+__host__ __device__ constexpr int rec_floats() { return (27 + CT + 3) & ~3; }
+
+// Elimination record of one observation: Y = L^-1 Hpc (column-major 3x9) + depth channels.
+template <int CT>
+__device__ __forceinline__ void write_record(const Ctx& c, int64_t k, const ObsView<CT>& V, const float l[6]) {
+  constexpr int R = rec_floats<CT>();
+  float rv[R];
+#pragma unroll
+  for (int a = 0; a < 9; ++a) {
+    float h[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) s += V.Jpw[3 * i + j] * V.Jcw[9 * i + a];
+      h[j] = s;
+    }
+    float y[3];
+    chol3_fwd<float>(l, h, y);
+    rv[3 * a] = y[0]; rv[3 * a + 1] = y[1]; rv[3 * a + 2] = y[2];
+  }
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) rv[27 + ch] = V.dep[ch];
+#pragma unroll
+  for (int e = 27 + CT; e < R; ++e) rv[e] = 0.f;
+  float4* dst = reinterpret_cast<float4*>(c.rec + k * R);
+#pragma unroll
+  for (int q = 0; q < R / 4; ++q) dst[q] = make_float4(rv[4 * q], rv[4 * q + 1], rv[4 * q + 2], rv[4 * q + 3]);
+}
+
+// Pass "points": per-track Hpp and g_p, and the max |diag(Hpp)|.
+template <int CT>
+__global__ void __launch_bounds__(128) k_points(Ctx c) {
+  const int task = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (task >= c.d.n_pt_tasks) return;                    // warp-uniform
+  const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
+  const int n = ke - kb;
+  float v[9];
+#pragma unroll
+  for (int j = 0; j < 9; ++j) v[j] = 0.f;
+  float wmax = 0.f;
+  if (n <= kWarp) {
+    const bool act = lane < n;
+    int tl = -1 - lane;
+    if (act) {
+      ObsView<CT> V;
+      view_local<CT>(c, kb + lane, V, tl);
+      point_terms<CT>(V, v);
+    }
+    const int tl_prev = __shfl_up_sync(0xffffffffu, tl, 1);
+    const int tl_next = __shfl_down_sync(0xffffffffu, tl, 1);
+    const bool head = act && (lane == 0 || tl_prev != tl);
+    const bool tail = act && (lane == n - 1 || tl_next != tl);
+    const unsigned heads = __ballot_sync(0xffffffffu, head);
+    const unsigned below = heads & ((2u << lane) - 1u);
+    const int seg_start = act ? 31 - __clz(below) : lane;
+#pragma unroll
+    for (int j = 0; j < 9; ++j) v[j] = seg_scan(v[j], lane, seg_start);
+    if (tail) {
+      float* t = c.trec + (int64_t)tl * 24;
+#pragma unroll
+      for (int j = 0; j < 9; ++j) t[j] = v[j];
+      wmax = fmaxf(v[0], fmaxf(v[3], v[5]));
+    }
+  } else {                                               // one long track, in rounds
+    const int tl = c.d.trk_t[kb];
+    for (int k = kb + lane; k < ke; k += kWarp) {
+      ObsView<CT> V;
+      int tl_k;
+      view_local<CT>(c, k, V, tl_k);
+      float u[9];
+      point_terms<CT>(V, u);
+#pragma unroll
+      for (int j = 0; j < 9; ++j) v[j] += u[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 9; ++j) v[j] = warp_sum(v[j]);
+    if (lane == 0) {
+      float* t = c.trec + (int64_t)tl * 24;
+#pragma unroll
+      for (int j = 0; j < 9; ++j) t[j] = v[j];
+      wmax = fmaxf(v[0], fmaxf(v[3], v[5]));
+    }
+  }
+  wmax = warp_max(wmax);
+  if (lane == 0) atomic_max_nonneg(c.hpp_max, wmax);
+}
+
+// Damped Cholesky factor of a track (BlockDiagMat.dampen_ then chol3x3_solve's guarded
+// factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599).
+__device__ __forceinline__ void track_factor(const Ctx& c, float lam, int tl, float l[6], float z[3]) {
+  const float* t = c.trec + (int64_t)tl * 24;
+  const float h00 = t[0] + lam, h01 = t[1], h02 = t[2], h11 = t[3] + lam, h12 = t[4], h22 = t[5] + lam;
+  chol3<float>(h00, h01, h02, h01, h11, h12, h02, h12, h22, 1e-12f, l);
+  const float g[3] = {t[6], t[7], t[8]};
+  chol3_fwd<float>(l, g, z);
+}
+
+// Pass "eliminate": Cholesky factor per track and the per-observation records.
+template <int CT>
+__global__ void __launch_bounds__(128) k_eliminate(Ctx c) {
+  const int task = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (task >= c.d.n_pt_tasks) return;
+  const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
+  const int n = ke - kb;
+  const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
+  if (n <= kWarp) {
+    if (lane >= n) return;
+    const int64_t k = kb + lane;
+    ObsView<CT> V;
+    int tl;
+    view_local<CT>(c, k, V, tl);
+    float l[6], z[3];
+    track_factor(c, lam, tl, l, z);
+    write_record<CT>(c, k, V, l);
+    const bool tail = (lane == n - 1) || (c.d.trk_t[k + 1] != tl);
+    if (tail) {
+      float* t = c.trec + (int64_t)tl * 24;
+#pragma unroll
+      for (int j = 0; j < 6; ++j) t[12 + j] = l[j];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) t[18 + j] = z[j];
+    }
+  } else {
+    const int tl = c.d.trk_t[kb];
+    float l[6], z[3];
+    track_factor(c, lam, tl, l, z);
+    for (int k = kb + lane; k < ke; k += kWarp) {
+      ObsView<CT> V;
+      int tl_k;
+      view_local<CT>(c, k, V, tl_k);
+      write_record<CT>(c, k, V, l);
+    }
+    if (lane == 0) {
+      float* t = c.trec + (int64_t)tl * 24;
+#pragma unroll
+      for (int j = 0; j < 6; ++j) t[12 + j] = l[j];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) t[18 + j] = z[j];
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// pass "diag": image-major per-observation terms
+// ------------------------------------------------------------------------------------
+// Unique values accumulated per image chunk (symmetric blocks keep their upper triangle).
+template <int CT>
+struct DiagLayout {
+  static constexpr int FF = 0;                      // (f,f)   3
+  static constexpr int FT = 3;                      // (f,t)  12
+  static constexpr int FZ = FT + 12;                // (f,z)  2C
+  static constexpr int TT = FZ + 2 * CT;            // (t,t)  21
+  static constexpr int TZ = TT + 21;                // (t,z)  6C
+  static constexpr int ZZ = TZ + 6 * CT;            // (z,z)  C(C+1)/2
+  static constexpr int B = ZZ + CT * (CT + 1) / 2;  // b      8+C
+  static constexpr int DA = B + 8 + CT;             // diag(Hcc) 8+C
+  static constexpr int N = DA + 8 + CT;
+  // destination entries written per chunk (full blocks)
+  static constexpr int E = 4 + 12 + 2 * CT + 36 + 6 * CT + CT * CT + 2 * (8 + CT);
+};
+
+__host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - a * (a - 1) / 2 + (b - a); }
+
+template <int CT>
+__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, int64_t k, float* acc) {
+  using Lay = DiagLayout<CT>;
+  float H[9][9];
+#pragma unroll
+  for (int a = 0; a < 9; ++a)
+#pragma unroll
+    for (int b = a; b < 9; ++b) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) s += V.Jcw[9 * i + a] * V.Jcw[9 * i + b];
+      H[a][b] = s;
+    }
+  float g[9];
+#pragma unroll
+  for (int a = 0; a < 9; ++a) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) s += V.Jc2[9 * i + a] * V.Wr[i];
+    g[a] = s;
+  }
+  // undamped diag(A) = diag(Hcc)
+  acc[Lay::DA + 0] += H[0][0];
+  acc[Lay::DA + 1] += H[1][1];
+#pragma unroll
+  for (int t = 0; t < 6; ++t) acc[Lay::DA + 2 + t] += H[2 + t][2 + t];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) acc[Lay::DA + 8 + ch] += H[8][8] * V.dep[ch] * V.dep[ch];
+  if (k >= 0) {                                   // eliminated track: subtract Y^T Y, Y^T z
+    constexpr int R = rec_floats<CT>();
+    const float4* r4 = reinterpret_cast<const float4*>(c.rec + k * R);
+    float Y[28];
+#pragma unroll
+    for (int q = 0; q < 7; ++q) {
+      const float4 v = __ldg(r4 + q);
+      Y[4 * q] = v.x; Y[4 * q + 1] = v.y; Y[4 * q + 2] = v.z; Y[4 * q + 3] = v.w;
+    }
+    const float* tz = c.trec + (int64_t)c.d.trk_t[k] * 24 + 18;
+    const float z0 = tz[0], z1 = tz[1], z2 = tz[2];
+#pragma unroll
+    for (int a = 0; a < 9; ++a) {
+#pragma unroll
+      for (int b = a; b < 9; ++b)
+        H[a][b] -= Y[3 * a] * Y[3 * b] + Y[3 * a + 1] * Y[3 * b + 1] + Y[3 * a + 2] * Y[3 * b + 2];
+      g[a] -= Y[3 * a] * z0 + Y[3 * a + 1] * z1 + Y[3 * a + 2] * z2;
+    }
+  }
+  acc[Lay::FF + 0] += H[0][0];
+  acc[Lay::FF + 1] += H[0][1];
+  acc[Lay::FF + 2] += H[1][1];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+#pragma unroll
+    for (int t = 0; t < 6; ++t) acc[Lay::FT + 6 * r + t] += H[r][2 + t];
+#pragma unroll
+    for (int ch = 0; ch < CT; ++ch) acc[Lay::FZ + CT * r + ch] += H[r][8] * V.dep[ch];
+  }
+#pragma unroll
+  for (int a = 0; a < 6; ++a) {
+#pragma unroll
+    for (int b = a; b < 6; ++b) acc[Lay::TT + sym_idx(a, b, 6)] += H[2 + a][2 + b];
+#pragma unroll
+    for (int ch = 0; ch < CT; ++ch) acc[Lay::TZ + CT * a + ch] += H[2 + a][8] * V.dep[ch];
+  }
+#pragma unroll
+  for (int a = 0; a < CT; ++a) {
+    const float ha = H[8][8] * V.dep[a];
+#pragma unroll
+    for (int b = a; b < CT; ++b) acc[Lay::ZZ + sym_idx(a, b, CT)] += ha * V.dep[b];
+  }
+#pragma unroll
+  for (int a = 0; a < 8; ++a) acc[Lay::B + a] += g[a];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) acc[Lay::B + 8 + ch] += g[8] * V.dep[ch];
+}
+
+constexpr int kDiagThreads = 128;
+
+template <int CT>
+__global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
+                                                       float* __restrict__ diagA) {
+  using Lay = DiagLayout<CT>;
+  __shared__ float red[kDiagThreads / kWarp][Lay::N];
+  const int chunk = blockIdx.x;
+  const int img = c.d.c1_img[chunk];
+  const int eb = c.d.c1_chunk[chunk], ee = c.d.c1_chunk[chunk + 1];
+  const Cam cam = load_cam(c.img_rec + (int64_t)img * kImgRec);
+  float zc[CT];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
+  float acc[Lay::N];
+#pragma unroll
+  for (int v = 0; v < Lay::N; ++v) acc[v] = 0.f;
+  for (int e = eb + threadIdx.x; e < ee; e += kDiagThreads) {
+    const int64_t o = c.d.c1_obs[e];
+    const int64_t k = c.d.c1_k[e];
+    ObsView<CT> V;
+    view_image<CT>(c, o, img, cam, zc, V);
+    diag_terms<CT>(c, V, k, acc);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int v = 0; v < Lay::N; ++v) {
+    const float s = warp_sum(acc[v]);
+    if (lane == 0) red[warp][v] = s;
+  }
+  __syncthreads();
+  const int* dst = c.d.img_dst + 6 * img;
+  const int* sc = c.d.img_sc + 3 * img;
+  for (int e = threadIdx.x; e < Lay::E; e += kDiagThreads) {
+    int v, g = e;
+    float* addr = nullptr;
+    if (g < 4) {                                           // (f,f)
+      const int r = g >> 1, q = g & 1;
+      v = Lay::FF + sym_idx(min(r, q), max(r, q), 2);
+      if (dst[0] >= 0) addr = S + dst[0] + g;
+    } else if ((g -= 4) < 12) {                            // (f,t)
+      v = Lay::FT + g;
+      if (dst[1] >= 0) addr = S + dst[1] + g;
+    } else if ((g -= 12) < 2 * CT) {                       // (f,z)
+      v = Lay::FZ + g;
+      if (dst[2] >= 0) addr = S + dst[2] + g;
+    } else if ((g -= 2 * CT) < 36) {                       // (t,t)
+      const int r = g / 6, q = g % 6;
+      v = Lay::TT + sym_idx(min(r, q), max(r, q), 6);
+      if (dst[3] >= 0) addr = S + dst[3] + g;
+    } else if ((g -= 36) < 6 * CT) {                       // (t,z)
+      v = Lay::TZ + g;
+      if (dst[4] >= 0) addr = S + dst[4] + g;
+    } else if ((g -= 6 * CT) < CT * CT) {                  // (z,z)
+      const int r = g / CT, q = g % CT;
+      v = Lay::ZZ + sym_idx(min(r, q), max(r, q), CT);
+      if (dst[5] >= 0) addr = S + dst[5] + g;
+    } else if ((g -= CT * CT) < 8 + CT) {                  // b
+      v = Lay::B + g;
+      const int blk = g < 2 ? 0 : (g < 8 ? 1 : 2), loc = g < 2 ? g : (g < 8 ? g - 2 : g - 8);
+      if (sc[blk] >= 0) addr = b + sc[blk] + loc;
+    } else {                                               // diag(A)
+      g -= 8 + CT;
+      v = Lay::DA + g;
+      const int blk = g < 2 ? 0 : (g < 8 ? 1 : 2), loc = g < 2 ? g : (g < 8 ? g - 2 : g - 8);
+      if (sc[blk] >= 0) addr = diagA + sc[blk] + loc;
+    }
+    if (addr) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDiagThreads / kWarp; ++w) s += red[w][v];
+      atomicAdd(addr, s);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// pass "pairs": segment-major observation-pair products
+// ------------------------------------------------------------------------------------
+// A segment (i, i') owns the S blocks between image i's typed blocks (rows) and image
+// i''s (columns).  For each of its observation pairs (o in i, o' in i', same track) the
+// product P = Y_o^T Y_o' (13x13 for C = 5 once the depth columns are expanded) is summed
+// in registers.  The 8+C output rows are split among NROLE warps (roles) so that no
+// thread holds more than 5 rows of accumulators; every role streams the same pairs.
+constexpr int kPairBatch = 32;
+
+template <int CT> __host__ __device__ constexpr int pair_roles() { return (8 + CT + 4) / 5; }
+template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() { return r * (8 + CT) / NR; }
+
+template <int CT>
+__device__ __forceinline__ void stage_batch(const Ctx& c, int64_t base, int64_t pe, float* sm_row, float* sm_col) {
+  constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
+  for (int q = threadIdx.x; q < 2 * kPairBatch * Q; q += blockDim.x) {
+    const int ri = q / Q, part = q - ri * Q;
+    const int pair = ri >> 1, side = ri & 1;
+    const int64_t p = base + pair;
+    if (p < pe) {
+      const int2 kk = c.d.pairs[p];
+      const int64_t k = side ? kk.y : kk.x;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(c.rec + k * R) + part);
+      float* dst = (side ? sm_col : sm_row) + pair * RS + 4 * part;
+      *reinterpret_cast<float4*>(dst) = v;
+    }
+  }
+}
+
+template <int CT>
+__device__ __forceinline__ void emit_pair_value(const Ctx& c, float* __restrict__ S, int s, int a, int bcol, float v) {
+  const int ta = a < 2 ? 0 : (a < 8 ? 1 : 2), ra = a < 2 ? a : (a < 8 ? a - 2 : a - 8);
+  const int tb = bcol < 2 ? 0 : (bcol < 8 ? 1 : 2), cb = bcol < 2 ? bcol : (bcol < 8 ? bcol - 2 : bcol - 8);
+  const int bsa = ta == 0 ? 2 : (ta == 1 ? 6 : CT), bsb = tb == 0 ? 2 : (tb == 1 ? 6 : CT);
+  const int sb = 3 * ta + tb;
+  const int mode = (c.d.seg_mode[s] >> (2 * sb)) & 3;
+  if (mode == kModeNone) return;
+  float* base = S + c.d.seg_dst[9 * (int64_t)s + sb];
+  if (mode == kModeDirect) {
+    atomicAdd(base + ra * bsb + cb, -v);
+  } else if (mode == kModeTrans) {
+    atomicAdd(base + cb * bsa + ra, -v);
+  } else {
+    atomicAdd(base + ra * bsb + cb, -v);
+    atomicAdd(base + cb * bsb + ra, -v);
+  }
+}
+
+template <int CT, int A0, int A1>
+__device__ __forceinline__ void pair_role(const Ctx& c, float* __restrict__ S, int s, int64_t pb, int64_t pe,
+                                          float* sm_row, float* sm_col) {
+  constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
+  constexpr int W = 8 + CT, NA = A1 - A0;
+  // row-record floats this role reads: Y columns of its focal/tau rows, Y column 8 and
+  // its depth channels for depth rows
+  constexpr int LO = A0 < 8 ? 3 * A0 : 24;
+  constexpr int HI = A1 > 8 ? 27 + (A1 - 8) : 3 * A1;
+  constexpr int QLO = LO / 4, QHI = (HI + 3) / 4;
+  constexpr bool HAS_Z = A1 > 8;
+  const int lane = threadIdx.x & 31;
+  float acc[NA * W];
+#pragma unroll
+  for (int v = 0; v < NA * W; ++v) acc[v] = 0.f;
+  for (int64_t base = pb; base < pe; base += kPairBatch) {
+    stage_batch<CT>(c, base, pe, sm_row, sm_col);
+    __syncthreads();
+    if (base + lane < pe) {
+      float yc[R], yr[R];
+      const float4* pc = reinterpret_cast<const float4*>(sm_col + lane * RS);
+      const float4* pr = reinterpret_cast<const float4*>(sm_row + lane * RS);
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const float4 v = pc[q];
+        yc[4 * q] = v.x; yc[4 * q + 1] = v.y; yc[4 * q + 2] = v.z; yc[4 * q + 3] = v.w;
+      }
+#pragma unroll
+      for (int q = QLO; q < QHI; ++q) {
+        const float4 v = pr[q];
+        yr[4 * q] = v.x; yr[4 * q + 1] = v.y; yr[4 * q + 2] = v.z; yr[4 * q + 3] = v.w;
+      }
+      float qz[8], sz = 0.f;
+      if (HAS_Z) {
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb) qz[bb] = yr[24] * yc[3 * bb] + yr[25] * yc[3 * bb + 1] + yr[26] * yc[3 * bb + 2];
+        sz = yr[24] * yc[24] + yr[25] * yc[25] + yr[26] * yc[26];
+      }
+#pragma unroll
+      for (int a = A0; a < A1; ++a) {
+        float* ac = acc + (a - A0) * W;
+        if (a < 8) {
+          const float t0 = yr[3 * a], t1 = yr[3 * a + 1], t2 = yr[3 * a + 2];
+#pragma unroll
+          for (int bb = 0; bb < 8; ++bb) ac[bb] += t0 * yc[3 * bb] + t1 * yc[3 * bb + 1] + t2 * yc[3 * bb + 2];
+          const float u = t0 * yc[24] + t1 * yc[25] + t2 * yc[26];
+#pragma unroll
+          for (int ch = 0; ch < CT; ++ch) ac[8 + ch] += u * yc[27 + ch];
+        } else {
+          const float dr = yr[27 + (a - 8)];
+#pragma unroll
+          for (int bb = 0; bb < 8; ++bb) ac[bb] += dr * qz[bb];
+          const float ds = dr * sz;
+#pragma unroll
+          for (int ch = 0; ch < CT; ++ch) ac[8 + ch] += ds * yc[27 + ch];
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int v = 0; v < NA * W; ++v) {
+    const float tot = warp_sum(acc[v]);
+    if (lane == (v & 31)) emit_pair_value<CT>(c, S, s, A0 + v / W, v % W, tot);
+  }
+}
+
+template <int CT>
+__global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* __restrict__ S) {
+  constexpr int R = rec_floats<CT>(), RS = R + 4, NR = pair_roles<CT>();
+  __shared__ __align__(16) float sm[2 * kPairBatch * RS];
+  const int64_t task = blockIdx.x;
+  const int s = c.d.task_seg[task];
+  const int64_t pb = c.d.task_pb[task], pe = c.d.task_pb[task + 1];
+  float* sm_row = sm;
+  float* sm_col = sm + kPairBatch * RS;
+  const int role = threadIdx.x >> 5;
+  if (role == 0) pair_role<CT, role_row<CT, NR, 0>(), role_row<CT, NR, 1>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 1) if (role == 1) pair_role<CT, role_row<CT, NR, 1>(), role_row<CT, NR, 2>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 2) if (role == 2) pair_role<CT, role_row<CT, NR, 2>(), role_row<CT, NR, 3>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 3) if (role == 3) pair_role<CT, role_row<CT, NR, 3>(), role_row<CT, NR, 4>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 4) if (role == 4) pair_role<CT, role_row<CT, NR, 4>(), role_row<CT, NR, 5>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 5) if (role == 5) pair_role<CT, role_row<CT, NR, 5>(), role_row<CT, NR, 6>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 6) if (role == 6) pair_role<CT, role_row<CT, NR, 6>(), role_row<CT, NR, 7>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if constexpr (NR > 7) if (role == 7) pair_role<CT, role_row<CT, NR, 7>(), role_row<CT, NR, 8>()>(c, S, s, pb, pe, sm_row, sm_col);
+}
+
+// ------------------------------------------------------------------------------------
+// finalize: per-type adaptive damping and the Jacobi preconditioner
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ int scalar_type(const DevPlan& d, int j) { return j < d.off_P ? 0 : (j < d.off_Z ? 1 : 2); }
+
+__global__ void k_fin_max(Ctx c, const float* __restrict__ diagA) {
+  float m[3] = {0.f, 0.f, 0.f};
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c.d.n_cam_params; j += gridDim.x * blockDim.x)
+    m[scalar_type(c.d, j)] = fmaxf(m[scalar_type(c.d, j)], fabsf(diagA[j]));
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const float w = warp_max(m[t]);
+    if ((threadIdx.x & 31) == 0) atomic_max_nonneg(c.misc + 4 + t, w);
+  }
+}
+
+__global__ void k_fin_apply(Ctx c, const float* __restrict__ diagA, float* __restrict__ S, float* __restrict__ precond) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= c.d.n_cam_params) return;
+  const int t = scalar_type(c.d, j);
+  const int zero = t == 0 ? c.d.zeroK : (t == 1 ? c.d.zeroP : c.d.zeroZ);
+  // BlockDiagMat.dampen_ scales by max |diag| of the type; ZerosMat.dampen_ uses 1e-12*I
+  const float lam = zero ? c.dampen : c.dampen * (c.adaptive ? c.misc[4 + t] : 1.f);
+  S[c.d.sdiag_pos[j]] += lam;
+  if (precond) precond[j] = fmaxf(diagA[j] + lam, 1e-12f);
+}
+
+// ------------------------------------------------------------------------------------
+// y = S x from the upper block triangle
+// ------------------------------------------------------------------------------------
+template <typename T>
+__global__ void k_spmv(DevPlan d, const float* __restrict__ S, const T* __restrict__ x, T* __restrict__ y) {
+  const int64_t blk = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (blk >= d.nnzb) return;
+  const int lane = threadIdx.x & 31;
+  const int p = d.blk_row[blk], q = d.col_idx[blk];
+  const int bp = d.bsize[p], bq = d.bsize[q], op = d.boff[p], oq = d.boff[q];
+  const float* A = S + d.val_off[blk];
+  // rows: y_p += A x_q
+  for (int r = lane; r < bp; r += 32) {
+    T s = 0;
+    for (int cc = 0; cc < bq; ++cc) s += (T)A[r * bq + cc] * x[oq + cc];
+    atomicAdd(y + op + r, s);
+  }
+  if (p == q) return;
+  // columns: y_q += A^T x_p
+  for (int cc = lane; cc < bq; cc += 32) {
+    T s = 0;
+    for (int r = 0; r < bp; ++r) s += (T)A[r * bq + cc] * x[op + r];
+    atomicAdd(y + oq + cc, s);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// point back-substitution: delta_p = L^-T (z - sum_o Y_o dc_o)
+// ------------------------------------------------------------------------------------
+template <int CT>
+__global__ void k_backsub(DevPlan d, const float* __restrict__ rec, const float* __restrict__ trec,
+                          const float* __restrict__ dc, float* __restrict__ dp) {
+  const int tl = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tl >= d.nT_loc) return;
+  constexpr int R = rec_floats<CT>();
+  const float* t = trec + (int64_t)tl * 24;
+  float l[6], acc[3] = {t[18], t[19], t[20]};
+#pragma unroll
+  for (int j = 0; j < 6; ++j) l[j] = t[12 + j];
+  for (int k = d.trk_ptr[tl]; k < d.trk_ptr[tl + 1]; ++k) {
+    const int img = d.img_t[k];
+    const int* sc = d.img_sc + 3 * img;
+    const float* Y = rec + (int64_t)k * R;
+    float v[9];
+#pragma unroll
+    for (int a = 0; a < 2; ++a) v[a] = sc[0] >= 0 ? dc[sc[0] + a] : 0.f;
+#pragma unroll
+    for (int a = 0; a < 6; ++a) v[2 + a] = sc[1] >= 0 ? dc[sc[1] + a] : 0.f;
+    float zz = 0.f;
+    if (sc[2] >= 0) {
+#pragma unroll
+      for (int ch = 0; ch < CT; ++ch) zz += Y[27 + ch] * dc[sc[2] + ch];
+    }
+    v[8] = zz;
+#pragma unroll
+    for (int a = 0; a < 9; ++a) {
+      acc[0] -= Y[3 * a] * v[a];
+      acc[1] -= Y[3 * a + 1] * v[a];
+      acc[2] -= Y[3 * a + 2] * v[a];
+    }
+  }
+  float x[3];
+  chol3_bwd<float>(l, acc, x);
+  const int64_t col = d.trk_col[tl];
+  dp[3 * col] = x[0]; dp[3 * col + 1] = x[1]; dp[3 * col + 2] = x[2];
+}
+
+// ------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------
+// Depth-channel counts with compiled kernels (the reference's multi-depth maps carry up
+// to 17 channels, scripts/xps/*.sh "-nz 1 17").
+#define B3R_FOR_EACH_C(X) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(17)
+
+int check_device(const b3r_plan* plan) {
+  int dev = -1;
+  B3R_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  B3R_REQUIRE(dev == plan->device, "current device %d differs from the plan's device %d", dev, plan->device);
+  return B3R_OK;
+}
+
+int make_ctx(b3r_plan* plan, const b3r_params* p, const b3r_lin_opts* o, void* ws, Ctx& c) {
+  B3R_REQUIRE(plan && o && ws, "NULL plan/options/workspace");
+  B3R_REQUIRE(((uintptr_t)ws & 255) == 0, "workspace must be 256-byte aligned");
+  std::memset(&c, 0, sizeof(c));
+  c.d = plan->d;
+  c.o.is_depth_log = o->is_depth_log;
+  c.o.weight_z = o->weight_z; c.o.pnorm = o->pnorm; c.o.max_pix_err = o->max_pix_err;
+  c.o.huber_delta = o->huber_delta; c.o.w_pts_nul = o->w_pts_nul;
+  c.o.clamp_lo = o->clamp_w_lo; c.o.clamp_hi = o->clamp_w_hi;
+  B3R_REQUIRE(o->pnorm > 0.f && o->pnorm <= 2.f, "pnorm must be in ]0, 2] for a linearization");
+  c.no_grad_f_from_rz = o->no_grad_f_from_rz;
+  c.optim_Z0 = o->optim_Z0;
+  c.optim_Z_1st_cam = o->optim_Z_1st_cam;
+  c.dampen = (float)o->dampen;
+  c.adaptive = o->adaptive_dampen;
+  char* w = (char*)ws;
+  c.img_rec = (float*)(w + plan->ws_img);
+  c.trec = (float*)(w + plan->ws_trec);
+  c.rec = (float*)(w + plan->ws_rec);
+  c.t_rw = (float*)(w + plan->ws_rw);
+  c.misc = (float*)(w + plan->ws_misc);
+  if (p) {
+    B3R_REQUIRE(p->K && p->P_rig2c && p->P_w2rig && p->z_coefs && p->pts3d && p->pix2d_std && p->pix2d_dep,
+                "NULL parameter pointer");
+    B3R_REQUIRE(p->P_rig2c_stride >= 16, "P_rig2c stride must be >= 16");
+    c.K = p->K; c.P_rig2c = p->P_rig2c; c.P_stride = p->P_rig2c_stride; c.P_w2rig = p->P_w2rig;
+    c.z_coefs = p->z_coefs; c.pts3d = p->pts3d;
+    c.pix2d = p->pix2d; c.pix2d_std = p->pix2d_std; c.pix2d_dep = p->pix2d_dep;
+    if (!p->pix2d) {
+      B3R_REQUIRE(p->residuals && p->w_pts, "residuals and w_pts are required when pix2d is NULL");
+      B3R_REQUIRE(p->w_cols == 1 || p->w_cols == 3, "w_cols must be 1 or 3");
+      c.res = p->residuals; c.rs_n = p->res_stride_n; c.rs_c = p->res_stride_c;
+      c.wpt = p->w_pts; c.ws_n = p->w_stride_n; c.ws_c = p->w_stride_c; c.w_cols = p->w_cols;
+    }
+  }
+  return B3R_OK;
+}
+
+template <int CT>
+int launch_points(const Ctx& c, cudaStream_t s) {
+  if (c.d.n_pt_tasks == 0) return B3R_OK;
+  k_points<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
+  return check_launch("points pass");
+}
+
+template <int CT>
+int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
+  if (c.d.n_pt_tasks > 0) {
+    k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
+    B3R_TRY(check_launch("eliminate pass"));
+  }
+  if (c.d.n_c1_chunks > 0) {
+    k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, 0, s>>>(c, S, b, diagA);
+    B3R_TRY(check_launch("diag pass"));
+  }
+  if (c.d.n_tasks > 0) {
+    k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, 0, s>>>(c, S);
+    B3R_TRY(check_launch("pairs pass"));
+  }
+  return B3R_OK;
+}
+
+template <int CT>
+int launch_backsub(const DevPlan& d, const float* rec, const float* trec, const float* dc, float* dp,
+                   cudaStream_t s) {
+  if (d.nT_loc == 0) return B3R_OK;
+  k_backsub<CT><<<grid_for(d.nT_loc, 128), 128, 0, s>>>(d, rec, trec, dc, dp);
+  return check_launch("backsub");
+}
+
+int stage_if_needed(b3r_plan* plan, const b3r_params* p, cudaStream_t s) {
+  if (plan->staged && plan->staged_src[0] == p->pix2d && plan->staged_src[1] == p->pix2d_std &&
+      plan->staged_src[2] == p->pix2d_dep)
+    return B3R_OK;
+  return b3r_plan_stage_obs(plan, p->pix2d, p->pix2d_std, p->pix2d_dep, s);
+}
+
+}  // namespace
+}  // namespace b3r
+
+using namespace b3r;
+
+extern "C" int b3r_plan_stage_obs(b3r_plan* plan, const float* pix2d, const float* pix2d_std,
+                                  const float* pix2d_dep, void* stream) {
+  B3R_REQUIRE(plan != nullptr, "NULL plan");
+  B3R_TRY(check_device(plan));
+  B3R_REQUIRE(plan->d.n_loc == 0 || (pix2d_std && pix2d_dep), "NULL pix2d_std/pix2d_dep");
+  if (plan->d.n_loc > 0) {
+    k_stage_obs<<<grid_for(plan->d.n_loc, 256), 256, 0, as_stream(stream)>>>(plan->d, pix2d, pix2d_std, pix2d_dep);
+    B3R_TRY(check_launch("b3r_plan_stage_obs"));
+  }
+  plan->staged = true;
+  plan->staged_src[0] = pix2d; plan->staged_src[1] = pix2d_std; plan->staged_src[2] = pix2d_dep;
+  return B3R_OK;
+}
+
+extern "C" int b3r_lin_points(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                              void* workspace, const b3r_outputs* out, void* stream) {
+  B3R_REQUIRE(params && out, "NULL params/outputs");
+  Ctx c;
+  B3R_TRY(make_ctx(plan, params, opts, workspace, c));
+  B3R_TRY(check_device(plan));
+  cudaStream_t s = as_stream(stream);
+  B3R_TRY(stage_if_needed(plan, params, s));
+  c.hpp_max = out->hpp_max ? out->hpp_max : c.misc;
+  k_prep_images<<<grid_for(c.d.n_imgs, 128), 128, 0, s>>>(c);
+  B3R_TRY(check_launch("prep images"));
+  if (!params->pix2d && c.d.n_loc > 0) {
+    k_stage_rw<<<grid_for(c.d.n_loc, 256), 256, 0, s>>>(c);
+    B3R_TRY(check_launch("stage residuals"));
+  }
+  B3R_TRY(check_cuda(cudaMemsetAsync(c.hpp_max, 0, sizeof(float), s), "memset hpp_max"));
+  switch (c.d.C) {
+#define X(CC) case CC: return launch_points<CC>(c, s);
+    B3R_FOR_EACH_C(X)
+#undef X
+    default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", c.d.C);
+  }
+}
+
+extern "C" int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                                void* workspace, const b3r_outputs* out, void* stream) {
+  B3R_REQUIRE(params && out && out->S_vals && out->b && out->diagA, "NULL params/outputs");
+  Ctx c;
+  B3R_TRY(make_ctx(plan, params, opts, workspace, c));
+  B3R_TRY(check_device(plan));
+  cudaStream_t s = as_stream(stream);
+  c.hpp_max = out->hpp_max ? out->hpp_max : c.misc;
+  B3R_TRY(check_cuda(cudaMemsetAsync(out->S_vals, 0, sizeof(float) * (size_t)c.d.nnz, s), "memset S"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(out->b, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset b"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(out->diagA, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset diagA"));
+  switch (c.d.C) {
+#define X(CC) case CC: return launch_assemble<CC>(c, out->S_vals, out->b, out->diagA, s);
+    B3R_FOR_EACH_C(X)
+#undef X
+    default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", c.d.C);
+  }
+}
+
+extern "C" int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
+                                const b3r_outputs* out, void* stream) {
+  B3R_REQUIRE(out && out->S_vals && out->diagA, "NULL outputs");
+  Ctx c;
+  B3R_TRY(make_ctx(plan, nullptr, opts, workspace, c));
+  B3R_TRY(check_device(plan));
+  cudaStream_t s = as_stream(stream);
+  if (c.d.n_cam_params == 0) return B3R_OK;
+  B3R_TRY(check_cuda(cudaMemsetAsync(c.misc + 4, 0, 4 * sizeof(float), s), "memset maxima"));
+  k_fin_max<<<std::min(grid_for(c.d.n_cam_params, 256), 148), 256, 0, s>>>(c, out->diagA);
+  B3R_TRY(check_launch("finalize max"));
+  k_fin_apply<<<grid_for(c.d.n_cam_params, 256), 256, 0, s>>>(c, out->diagA, out->S_vals, out->precond);
+  return check_launch("finalize apply");
+}
+
+extern "C" int b3r_linearize_schur(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                                   void* workspace, const b3r_outputs* out, void* stream) {
+  B3R_TRY(b3r_lin_points(plan, params, opts, workspace, out, stream));
+  B3R_TRY(b3r_lin_assemble(plan, params, opts, workspace, out, stream));
+  return b3r_lin_finalize(plan, opts, workspace, out, stream);
+}
+
+template <typename T>
+static int spmv_impl(const b3r_plan* plan, const float* S, const T* x, T* y, void* stream) {
+  B3R_REQUIRE(plan && S && x && y, "NULL argument");
+  B3R_TRY(check_device(plan));
+  cudaStream_t s = as_stream(stream);
+  B3R_TRY(check_cuda(cudaMemsetAsync(y, 0, sizeof(T) * (size_t)plan->d.n_cam_params, s), "memset y"));
+  if (plan->d.nnzb == 0) return B3R_OK;
+  k_spmv<T><<<grid_for(plan->d.nnzb, 4), 128, 0, s>>>(plan->d, S, x, y);
+  return check_launch("b3r_schur_spmv");
+}
+
+extern "C" int b3r_schur_spmv(const b3r_plan* plan, const float* S_vals, const float* x, float* y, void* stream) {
+  return spmv_impl<float>(plan, S_vals, x, y, stream);
+}
+
+extern "C" int b3r_schur_spmv_f64(const b3r_plan* plan, const float* S_vals, const double* x, double* y,
+                                  void* stream) {
+  return spmv_impl<double>(plan, S_vals, x, y, stream);
+}
+
+extern "C" int b3r_backsub(const b3r_plan* plan, const void* workspace, const float* delta_c, float* delta_p,
+                           void* stream) {
+  B3R_REQUIRE(plan && workspace && delta_c && delta_p, "NULL argument");
+  B3R_TRY(check_device(plan));
+  const char* w = (const char*)workspace;
+  const float* rec = (const float*)(w + plan->ws_rec);
+  const float* trec = (const float*)(w + plan->ws_trec);
+  cudaStream_t s = as_stream(stream);
+  switch (plan->d.C) {
+#define X(CC) case CC: return launch_backsub<CC>(plan->d, rec, trec, delta_c, delta_p, s);
+    B3R_FOR_EACH_C(X)
+#undef X
+    default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", plan->d.C);
+  }
+}

@@ -1,0 +1,251 @@
+/*
+ * b3r.h -- C ABI of the B200-native BLASt3R bundle-adjustment linearization library.
+ *
+ * Every entry point takes plain pointers and sizes (device pointers unless stated
+ * otherwise), an opaque CUDA stream handle (`void* stream`, a cudaStream_t; NULL = the
+ * legacy default stream) and returns an int status: B3R_OK (0) or a negative B3R_E_*
+ * code, with a message available from b3r_last_error().  No C++ exception crosses the
+ * ABI.  All work is enqueued asynchronously on `stream`; nothing synchronises the
+ * device.  The library never allocates output buffers: callers pass them in.
+ *
+ * Part 1 mirrors, one to one, the native ops the reference binds through pybind
+ * (naver/blast3r, src/blast3r/extensions/cujac/sfm_jacobian_rigs.cu:1254-1275, re-exported
+ * by extensions/cujac/__init__.py:18-22), with the same argument meaning and layouts.
+ *
+ * Part 2 is the fused hot path that replaces the reference's per-LM-iteration
+ * linearization (GaussNewtonSolver.compute_jacobians + solve_delta up to its PCG,
+ * inference/ba_solver.py:34-188): residual, Jacobians, Huber/IRLS weights, per-track
+ * 3x3 point-block inversion and the Schur-reduced camera/depth system
+ * S = Hcc - Hcp Hpp^-1 Hpc with its gradient b, written into a precomputed
+ * block-sparse pattern of S.
+ */
+#ifndef B3R_H
+#define B3R_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B3R_OK 0
+#define B3R_E_INVALID -1     /* bad argument (shape, size, flag, NULL pointer)        */
+#define B3R_E_CUDA -2        /* a CUDA runtime call failed                            */
+#define B3R_E_NOMEM -3       /* host or device allocation failed (plan creation only) */
+#define B3R_E_UNSUPPORTED -4 /* valid request this build does not implement           */
+
+#define B3R_F32 0
+#define B3R_F64 1
+
+/* Message of the last failed call on the calling thread ("" if none). */
+const char* b3r_last_error(void);
+/* Library version string. */
+const char* b3r_version(void);
+
+/* ===================================================================================
+ * Part 1 -- reference op mirrors
+ * =================================================================================== */
+
+/* Residuals, Huber error and IRLS weights per observation.
+ * Replaces residuals_with_rigs (sfm_jacobian_rigs.cu:1048-1101, kernel :129-259).
+ * infos: int32 [3, n_imgs] = (cumulative obs count per image, node id, cam id);
+ * K [n_cams,3,3]; P_rig2c [n_cams,4,4] with `P_rig2c_stride` floats between cameras;
+ * P_w2rig [n_nodes,4,4]; z_coefs [n_imgs,C]; pts3d [n_tracks,3]; pids int32 [n_obs];
+ * pix2d, pix2d_std [n_obs,2]; pix2d_dep [n_obs,C].
+ * out: float [n_out, n_obs] with n_out = 9 if pnorm > 0 else 3 (rows: residual x,y,z,
+ * err x,y,z, weight x,y,z); the reference returns it transposed as (n_obs, n_out).
+ * Rows of observations whose camera depth is <= 1e-3 are zero.  pnorm must be -1 or in
+ * (0, 2] (sfm_jacobian_rigs.cu:1067). */
+int b3r_residuals_with_rigs(const int32_t* infos, int n_imgs, const float* K, int n_cams,
+                            const float* P_rig2c, int64_t P_rig2c_stride, const float* P_w2rig,
+                            int n_nodes, const float* z_coefs, int C, const float* pts3d,
+                            int n_tracks, const int32_t* pids, int64_t n_obs, const float* pix2d,
+                            const float* pix2d_std, const float* pix2d_dep, int is_depth_log,
+                            float weight_z, float pnorm, float max_pix_err, float huber_delta,
+                            float w_pts_nul, float* out, void* stream);
+
+/* Explicit Jacobians per observation.
+ * Replaces jacobians_with_rigs (sfm_jacobian_rigs.cu:1105-1148, kernel :323-509).
+ * J_cam [n_obs,3,8] (d/dfx, d/dfy, d/dtau x6), J_zcf [n_obs,1,C] (depth row only),
+ * J_pts [n_obs,3,3]; element type float (output_float64 = 0) or double (= 1), computed
+ * in that precision from the float inputs as the reference does.  The three outputs are
+ * fully written (zero rows for invalid depth). */
+int b3r_jacobians_with_rigs(const int32_t* infos, int n_imgs, const float* K, int n_cams,
+                            const float* P_rig2c, int64_t P_rig2c_stride, const float* P_w2rig,
+                            int n_nodes, const float* z_coefs, int C, const float* pts3d,
+                            int n_tracks, const int32_t* pids, int64_t n_obs,
+                            const float* pix2d_std, const float* pix2d_dep, int is_depth_log,
+                            int output_float64, void* J_cam, void* J_zcf, void* J_pts,
+                            void* stream);
+
+/* Batched 3x3 SPD solve by guarded Cholesky with diagonal jitter.
+ * Replaces chol3x3_solve (sfm_jacobian_rigs.cu:1151-1169, kernel :560-634).
+ * blocks [N,3,3], rhs [N,3], out [N,3], dtype B3R_F32 or B3R_F64. */
+int b3r_chol3x3_solve(const void* blocks, const void* rhs, void* out, int64_t N, double jitter,
+                      int dtype, void* stream);
+
+/* Block-COO matrix-vector product y = A x (transpose = 0) or y = A^T x (transpose = 1).
+ * Replaces blockcoo_matvec (sfm_jacobian_rigs.cu:1171-1219, kernel :760-803).
+ * blocks [N,bh,bw]; row/col indices int32 (index_is_64 = 0) or int64 (= 1), in blocks;
+ * the matrix has HB1 x WB1 blocks; x has WB1*bw (HB1*bh if transposed) entries; y has
+ * HB1*bh (WB1*bw) entries and is overwritten.  Any bh, bw in 1..32 is accepted (the
+ * reference instantiates 31 fixed shapes). */
+int b3r_blockcoo_matvec(const void* blocks, int bh, int bw, const void* row_idx,
+                        const void* col_idx, int index_is_64, int64_t N, const void* x, void* y,
+                        int64_t HB1, int64_t WB1, int transpose, int dtype, void* stream);
+
+/* out[b] = left[b]^T right[b] for left [B,K,I] (strides l_bs, l_ks, unit inner stride) and
+ * right [B,K,J] (strides r_bs, r_ks); out [B,I,J] contiguous.
+ * Replaces fused_einsum_bki_bkj (sfm_jacobian_rigs.cu:1222-1250, kernel :880-941).
+ * Any K, I, J with I*J <= 1024 is accepted. */
+int b3r_fused_einsum_bki_bkj(const void* left, int64_t l_bs, int64_t l_ks, const void* right,
+                             int64_t r_bs, int64_t r_ks, void* out, int64_t B, int K, int I, int J,
+                             int dtype, void* stream);
+
+/* ===================================================================================
+ * Part 2 -- fused linearization + Schur assembly
+ * =================================================================================== */
+
+/* How one parameter type takes part, mirroring GaussNewtonSolver.enable
+ * (inference/ba_solver.py:72-108): */
+#define B3R_ENABLE_ALL 0   /* status True: every block is a variable                    */
+#define B3R_ENABLE_ZERO 1  /* status False: columns kept, J zero, damped to 1e-12 * I    */
+#define B3R_ENABLE_MASK 2  /* bool tensor: disabled blocks' columns are removed          */
+
+typedef struct b3r_plan b3r_plan;
+
+/* Problem structure, fixed for one BA phase.  `infos` and `pids` are HOST pointers
+ * (the image-sorted observation layout of ObservedTracks / RigsData.infos,
+ * inference/tracks.py:20-31, inference/rigs.py:50-51). */
+typedef struct {
+    int32_t n_imgs, n_cams, n_nodes, n_tracks;
+    int64_t n_obs;
+    int32_t C;                        /* number of depth coefficients per image            */
+    const int32_t* infos;             /* host, int32 [3, n_imgs]                           */
+    const int32_t* pids;              /* host, int32 [n_obs]                               */
+    int32_t mode_K, mode_P, mode_Z, mode_X;          /* B3R_ENABLE_*                       */
+    const uint8_t *mask_K, *mask_P, *mask_Z, *mask_X; /* host bool masks for MODE_MASK    */
+    int32_t track_begin, track_end;   /* tracks owned by this rank (all: 0, n_tracks)      */
+    int32_t device;                   /* CUDA device ordinal the plan lives on; < 0 builds
+                                         a host-only plan (info and pattern queries only) */
+} b3r_plan_desc;
+
+typedef struct {
+    int64_t n_obs, n_obs_local, n_tracks_local;   /* observations / eliminated tracks here */
+    int32_t n_blocks;                 /* typed parameter blocks (foc | tau | zcf)          */
+    int32_t n_cam_params;             /* size of the reduced camera/depth vector           */
+    int32_t n_points;                 /* point-block count of the full delta (3 each)      */
+    int64_t nnzb;                     /* stored blocks of S (upper block triangle)         */
+    int64_t nnz;                      /* floats in the S value array                       */
+    int64_t n_pairs, n_segments, n_pair_tasks, n_point_tasks, n_diag_chunks;
+    int64_t workspace_bytes;          /* scratch bytes b3r_linearize_* needs               */
+    int32_t nb_K, nb_P, nb_Z;         /* blocks per type                                   */
+    int32_t off_P, off_Z;             /* scalar offsets of the tau and zcf ranges          */
+    int32_t record_floats;            /* floats per per-observation elimination record     */
+} b3r_plan_info;
+
+/* Build the plan: image -> block maps, the track-sorted observation order, per-warp
+ * point tasks, the image-pair segments with their observation-pair lists, and the
+ * block-sparse pattern of S (upper block triangle, diagonal blocks stored in full).
+ * The pattern is the same on every rank of a sharded problem (it is built from all
+ * tracks); pair lists and tasks only cover tracks [track_begin, track_end).
+ * Replaces the structure discovery the reference redoes every iteration inside
+ * HStackMat.gram_matrix / OneBlockPerRow.__matmul__obpc_obpr (ba_solver.py:854-924). */
+int b3r_plan_create(b3r_plan** plan, const b3r_plan_desc* desc);
+int b3r_plan_destroy(b3r_plan* plan);
+int b3r_plan_get_info(const b3r_plan* plan, b3r_plan_info* info);
+
+/* Host copies of the S pattern: row_ptr [n_blocks+1], col_idx [nnzb] (block columns,
+ * ascending, >= row), val_off [nnzb] (offset of each dense row-major block in the value
+ * array), block_size [n_blocks], block_off [n_blocks] (scalar offset in the reduced
+ * camera/depth vector).  Any pointer may be NULL. */
+int b3r_plan_get_pattern(const b3r_plan* plan, int32_t* row_ptr, int32_t* col_idx,
+                         int64_t* val_off, int32_t* block_size, int32_t* block_off);
+
+/* Gather the static observation data (device pointers, image-sorted reference layout:
+ * pix2d [n_obs,2], pix2d_std [n_obs,2], pix2d_dep [n_obs,C]) into the plan's
+ * track-sorted structure-of-arrays copy.  Call once per phase, or whenever those arrays
+ * change; pix2d may be NULL when residuals and weights are passed to the linearization
+ * instead of being recomputed. */
+int b3r_plan_stage_obs(b3r_plan* plan, const float* pix2d, const float* pix2d_std,
+                       const float* pix2d_dep, void* stream);
+
+/* Per-iteration parameters (device pointers, reference layouts and dtypes). */
+typedef struct {
+    const float* K;            /* [n_cams,3,3]                                        */
+    const float* P_rig2c;      /* [n_cams,4,4], P_rig2c_stride floats apart            */
+    int64_t P_rig2c_stride;
+    const float* P_w2rig;      /* [n_nodes,4,4]                                       */
+    const float* z_coefs;      /* [n_imgs,C]                                          */
+    const float* pts3d;        /* [n_tracks,3]                                        */
+    const float* pix2d;        /* [n_obs,2] image-sorted; NULL: use residuals/w below */
+    const float* pix2d_std;    /* [n_obs,2] image-sorted                              */
+    const float* pix2d_dep;    /* [n_obs,C] image-sorted                              */
+    /* residuals (n_obs,3) and IRLS weights (n_obs, w_cols in {1,3}) as the solver receives
+     * them (ba_solver.py:110); strides in floats.  Used only when pix2d == NULL. */
+    const float* residuals;
+    int64_t res_stride_n, res_stride_c;
+    const float* w_pts;
+    int64_t w_stride_n, w_stride_c;
+    int32_t w_cols;
+} b3r_params;
+
+/* Solver options (lm_step / GaussNewtonSolver arguments, engine.py:206-219, ba_solver.py:22,
+ * residual op arguments sfm_jacobian_rigs.cu:1255-1258). */
+typedef struct {
+    int32_t is_depth_log;
+    float weight_z, pnorm, max_pix_err, huber_delta, w_pts_nul;
+    float clamp_w_lo, clamp_w_hi;     /* W clamp of solve_delta (1e-6, 1e6)              */
+    double dampen;                    /* 1e-12                                           */
+    int32_t adaptive_dampen;          /* damping x max |diag| per block type             */
+    int32_t no_grad_f_from_rz, optim_Z0, optim_Z_1st_cam;
+} b3r_lin_opts;
+
+/* Device outputs of one linearization (caller-owned, overwritten). */
+typedef struct {
+    float* S_vals;     /* [nnz]           block values of S (upper block triangle)          */
+    float* b;          /* [n_cam_params]  reduced gradient g_c - Hcp Hpp^-1 g_p            */
+    float* diagA;      /* [n_cam_params]  undamped diag(Hcc) (needed across ranks)         */
+    float* precond;    /* [n_cam_params]  max(diag(A) + damping, 1e-12), or NULL           */
+    float* hpp_max;    /* [1]             max |diag(Hpp)| over this rank's tracks (NULL:
+                          kept in the workspace; sharded callers pass it to all-reduce it) */
+} b3r_outputs;
+
+/* One full linearization on one GPU: b3r_lin_points, b3r_lin_assemble and
+ * b3r_lin_finalize in sequence.  `workspace`: b3r_plan_info.workspace_bytes of device
+ * memory, 256-byte aligned; it keeps the per-track Cholesky factors and per-observation
+ * elimination records needed by b3r_backsub. */
+int b3r_linearize_schur(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                        void* workspace, const b3r_outputs* out, void* stream);
+
+/* Stage 1: per-track Hpp and g_p, and out->hpp_max (the adaptive damping of the point
+ * blocks needs the max over ALL tracks: sharded callers all-reduce it before stage 2). */
+int b3r_lin_points(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                   void* workspace, const b3r_outputs* out, void* stream);
+/* Stage 2: point elimination, per-image diagonal blocks, pair products, b and diag(A).
+ * Zeroes and accumulates out->S_vals, out->b, out->diagA (partial sums on each rank). */
+int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                     void* workspace, const b3r_outputs* out, void* stream);
+/* Stage 3: per-type adaptive damping of S's diagonal from the (reduced) diag(A)
+ * (ba_solver.py:510-517, 572-582) and the Jacobi preconditioner. */
+int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
+                     const b3r_outputs* out, void* stream);
+
+/* y = S x with S given by its upper block triangle (symmetric). x, y: [n_cam_params]. */
+int b3r_schur_spmv(const b3r_plan* plan, const float* S_vals, const float* x, float* y,
+                   void* stream);
+/* Same in double precision (S values promoted on load). */
+int b3r_schur_spmv_f64(const b3r_plan* plan, const float* S_vals, const double* x, double* y,
+                       void* stream);
+
+/* Point back-substitution delta_p = Hpp^-1 (g_p - Hpc delta_c) for this rank's tracks
+ * (ba_solver.py:203), from the factors kept in `workspace` by the last linearization.
+ * delta_c: [n_cam_params]; delta_p: [n_points*3], only this rank's tracks written. */
+int b3r_backsub(const b3r_plan* plan, const void* workspace, const float* delta_c, float* delta_p,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B3R_H */
