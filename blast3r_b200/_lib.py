@@ -12,6 +12,7 @@ LIB_PATH = os.path.join(_HERE, 'libb3r.so')
 B3R_OK = 0
 B3R_F32, B3R_F64 = 0, 1
 ENABLE_ALL, ENABLE_ZERO, ENABLE_MASK = 0, 1, 2
+PASS_PREP, PASS_POINTS, PASS_ELIMINATE, PASS_DIAG, PASS_PAIRS = 0, 1, 2, 3, 4
 
 _i32, _i64, _f32, _f64, _vp = C.c_int32, C.c_int64, C.c_float, C.c_double, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)
@@ -78,10 +79,11 @@ _SIGS = {
                                       C.POINTER(Outputs), _vp]),
     'b3r_lin_points': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), _vp]),
     'b3r_lin_assemble': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), _vp]),
+    'b3r_lin_pass': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), C.c_int, _vp]),
     'b3r_lin_finalize': (C.c_int, [_vp, C.POINTER(LinOpts), _vp, C.POINTER(Outputs), _vp]),
     'b3r_schur_spmv': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     'b3r_schur_spmv_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
-    'b3r_backsub': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    'b3r_backsub': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, _vp, _vp, _vp]),
 }
 
 _lib = None

@@ -1,0 +1,157 @@
+"""Drop-in for the reference's ``GaussNewtonSolver`` (inference/ba_solver.py:20-248).
+
+Same constructor, ``compute_jacobians``, ``solve_delta`` and ``unpack_delta_inplace``
+signatures and results.  Instead of wrapping explicit Jacobians in block matrices and
+running a matrix-free PCG on the implicit Schur complement (ba_solver.py:184-206), it
+
+1. ``compute_jacobians`` returns a lazy ``Linearization`` handle (the structure is planned
+   once per phase and cached: ``BAPlan``);
+2. ``solve_delta`` runs the fused B200 linearization (residual, Jacobians, IRLS weights,
+   per-track Hpp inversion, Schur assembly into the block-sparse S and b, per-type
+   adaptive damping), then the reference's PCG on the explicit S, then the point
+   back-substitution delta_p = D^-1 (g_p - C delta_c).
+
+``compute_jacobians`` accepts one extra keyword, ``pix2d``: with it the kernels recompute
+residuals and weights in-kernel (identical values: one shared device function); without
+it they read the ``residuals`` / ``w_pts`` handed to ``solve_delta``, as the reference does.
+"""
+import torch
+
+from .pcg import pcg
+from .plan import BAPlan
+
+N_FOC = 2
+N_TAU = 6
+
+
+class Param:
+    def __init__(self, n):
+        self.n = self.true_n = n
+        self.true_idxs = None
+
+
+class Linearization:
+    """Everything solve_delta needs to linearize at the current parameters."""
+
+    def __init__(self, plan, tensors, flags):
+        self.plan, self.tensors, self.flags = plan, tensors, flags
+        self.system = None
+        n = plan.n_obs
+        self.shape = (3 * n, plan.n_cam_params + 3 * plan.info.n_points)
+
+
+_PLAN_CACHE = {}
+
+
+def _fingerprint(t):
+    """Shape + two weighted sums of an integer/bool tensor (one small reduction)."""
+    v = t.reshape(-1).long()
+    w = torch.arange(1, v.numel() + 1, device=v.device, dtype=torch.int64) % 1000003
+    return (tuple(t.shape),) + tuple(torch.stack([v.sum(), (v * w).sum()]).tolist())
+
+
+def _structure_key(rigs, pids, n_cams, n_nodes, n_tracks, C, modes):
+    return (_fingerprint(rigs), _fingerprint(pids), n_cams, n_nodes, n_tracks, C,
+            tuple(m if isinstance(m, bool) else ('mask',) + _fingerprint(m) for m in modes))
+
+
+def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=True, optim_Z=True,
+             optim_X=True, device=None):
+    """Plan for this structure, reused while the structure tensors are unchanged."""
+    key = _structure_key(rigs, pids, n_cams, n_nodes, n_tracks, C, (optim_K, optim_P, optim_Z, optim_X))
+    plan = _PLAN_CACHE.get(key)
+    if plan is None:
+        if len(_PLAN_CACHE) > 8:
+            _PLAN_CACHE.clear()
+        plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
+                      optim_Z=optim_Z, optim_X=optim_X, device=device)
+        _PLAN_CACHE[key] = plan
+    return plan
+
+
+class GaussNewtonSolver:
+    """Bundle-adjustment solver for a problem with existing depth estimates."""
+
+    def __init__(self, n_cams, n_nodes, n_imgs, n_tracks, device, no_grad_f_from_rz=False, dampen=1e-12,
+                 adaptive_dampen=True, dtype=torch.float32):
+        self.cams = Param(n_cams)
+        self.nodes = Param(n_nodes)
+        self.imgs = Param(n_imgs)
+        self.tracks = Param(n_tracks)
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.dampen = dampen
+        self.adaptive_dampen = adaptive_dampen
+        self.no_grad_f_from_rz = no_grad_f_from_rz
+        self.last_solve = {}
+
+    def compute_jacobians(self, rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d_std, pix2d_dep,
+                          is_depth_log, optim_Z_1st_cam=True, optim_Z0=True, optim_K=True, optim_Z=True,
+                          optim_P=True, optim_X=True, pix2d=None):
+        assert rigs.shape == (3, self.imgs.n)
+        C = pix2d_dep.shape[1]
+        self.n_kpts, self.n_zcf = len(pids), C
+        plan = get_plan(rigs, pids, self.cams.n, self.nodes.n, self.imgs.n, self.tracks.n, C, optim_K, optim_P,
+                        optim_Z, optim_X, device=self.device)
+        # column counts after enabling (ba_solver.py:72-108)
+        for prm, status in ((self.cams, optim_K), (self.nodes, optim_P), (self.imgs, optim_Z),
+                            (self.tracks, optim_X)):
+            if isinstance(status, torch.Tensor):
+                idxs = status.nonzero().squeeze(-1)
+                if len(idxs):
+                    prm.n = len(idxs)
+                    prm.true_idxs = idxs.to(self.device)
+        flags = dict(is_depth_log=bool(is_depth_log), optim_Z_1st_cam=bool(optim_Z_1st_cam),
+                     optim_Z0=bool(optim_Z0))
+        tensors = dict(K=K, P_rig2cam=P_rig2cam, P_w2rig=P_w2rig, z_coefs=z_coefs, pts3d=pts3d,
+                       pix2d_std=pix2d_std, pix2d_dep=pix2d_dep, pix2d=pix2d)
+        return Linearization(plan, tensors, flags)
+
+    def linearize(self, J, residuals=None, w_pts=None, clamp_w=(1e-6, 1e6), lin_kw=None):
+        """Run the fused linearization; returns the SchurSystem (S, b, diag A, preconditioner)."""
+        t, f = J.tensors, J.flags
+        kw = dict(lin_kw or {})
+        opts = BAPlan.lin_opts(is_depth_log=f['is_depth_log'], clamp_w=clamp_w, dampen=self.dampen,
+                               adaptive_dampen=self.adaptive_dampen, no_grad_f_from_rz=self.no_grad_f_from_rz,
+                               optim_Z0=f['optim_Z0'], optim_Z_1st_cam=f['optim_Z_1st_cam'], **kw)
+        if t['pix2d'] is not None:
+            p = J.plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                              t['pix2d_dep'], pix2d=t['pix2d'])
+        else:
+            p = J.plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                              t['pix2d_dep'], residuals=residuals, w_pts=w_pts)
+        J.system = J.plan.linearize(p, opts)
+        return J.system
+
+    def solve_delta(self, J, residuals, w_pts, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
+        """delta = [delta_c, delta_p] solving (J^T W J + damping) delta = J^T W r through the
+        Schur complement (ba_solver.py:110-182); float32 like the reference."""
+        assert residuals.shape == (self.n_kpts, 3)
+        assert w_pts.shape in ((self.n_kpts, 1), (self.n_kpts, 3))
+        if z_prior is not None and z_prior[0] is not None:
+            raise NotImplementedError('dense tangent prior (z_prior) is not supported by the fused path yet')
+        s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw)
+        dt = torch.float64 if self.dtype == torch.float64 else torch.float32
+        b = s.b.to(dt)
+        M = s.precond.to(dt)
+        delta_c, niter, conv = pcg(lambda v: s.matvec(v), b, M_mv=lambda v: v / M, tol=1e-6, maxiter=300)
+        delta_p = s.backsub(delta_c.to(torch.float32))
+        self.last_solve = dict(iters=niter, converged=conv)
+        return torch.cat([delta_c.to(torch.float32), delta_p])
+
+    def unpack_delta_inplace(self, delta):
+        """(dK, dP, dZ, dX), re-expanded over disabled columns (ba_solver.py:228-248)."""
+        sizes = [self.cams.n * N_FOC, self.nodes.n * N_TAU, self.imgs.n * self.n_zcf, self.tracks.n * 3]
+        cum = torch.tensor(sizes).cumsum(0)
+        assert delta.shape == (int(cum[-1]),)
+        dK, dP, dZ, dX = delta.tensor_split(cum[:-1].tolist())
+
+        def expand(d, prm, k):
+            d = d.view(prm.n, k)
+            if prm.true_idxs is not None:
+                d2 = d.new_zeros((prm.true_n, k))
+                d2[prm.true_idxs] = d
+                return d2
+            return d
+        return (expand(dK, self.cams, N_FOC), expand(dP, self.nodes, N_TAU), expand(dZ, self.imgs, self.n_zcf),
+                expand(dX, self.tracks, 3))

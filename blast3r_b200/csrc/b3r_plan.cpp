@@ -68,7 +68,7 @@ struct PlanBuild {
   std::vector<char> obs_live;              // [n_obs] observation touches an active block
   // local side
   std::vector<int> loc_tracks, trk_col, perm_t, trk_t, img_t, pt_task, kof;
-  std::vector<int> c1_obs, c1_k, c1_chunk, c1_img;
+  std::vector<int> c1_obs, c1_k, c1_pid, c1_chunk, c1_img;
   // segments (global)
   std::vector<int> seg_row_ptr, seg_col;   // CSR over row image
   std::vector<int64_t> seg_cnt;
@@ -223,6 +223,7 @@ static int build_tracks(PlanBuild& B) {
     }
     B.c1_obs.push_back((int)o);
     B.c1_k.push_back(B.kof[o]);
+    B.c1_pid.push_back(t);
     ++in_chunk;
   }
   B.c1_chunk.push_back((int)B.c1_obs.size());
@@ -496,7 +497,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.loc_tracks, &d.trk_gid); A.add(B.trk_col, &d.trk_col); A.add(B.pt_task, &d.pt_task);
   A.add_mut<float2>(d.n_loc, &d.t_pix); A.add_mut<float2>(d.n_loc, &d.t_std);
   A.add_mut<float>((size_t)d.n_loc * desc->C, &d.t_dep);
-  A.add(B.c1_obs, &d.c1_obs); A.add(B.c1_k, &d.c1_k); A.add(B.c1_chunk, &d.c1_chunk);
+  A.add(B.c1_obs, &d.c1_obs); A.add(B.c1_k, &d.c1_k); A.add(B.c1_pid, &d.c1_pid); A.add(B.c1_chunk, &d.c1_chunk);
   A.add(B.c1_img, &d.c1_img);
   A.add(B.seg_dst, &d.seg_dst); A.add(B.seg_mode, &d.seg_mode);
   A.add(B.pairs, &d.pairs); A.add(B.task_pb, &d.task_pb); A.add(B.task_seg, &d.task_seg);

@@ -56,6 +56,7 @@ struct DevPlan {
   int64_t n_c1;
   const int* c1_obs;      // [n_c1] o
   const int* c1_k;        // [n_c1] k, -1 if the track is not eliminated
+  const int* c1_pid;      // [n_c1] track id (point index) of the observation
   int n_c1_chunks;
   const int* c1_chunk;    // [n_c1_chunks+1]
   const int* c1_img;      // [n_c1_chunks]

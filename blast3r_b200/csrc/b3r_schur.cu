@@ -32,7 +32,7 @@ struct Ctx {
   LinOpts o;
   const float* K; const float* P_rig2c; int64_t P_stride; const float* P_w2rig;
   const float* z_coefs; const float* pts3d;
-  const float* pix2d; const float* pix2d_std; const float* pix2d_dep; const int* pids;
+  const float* pix2d; const float* pix2d_std; const float* pix2d_dep;
   const float* res; int64_t rs_n, rs_c;
   const float* wpt; int64_t ws_n, ws_c; int w_cols;
   float* img_rec;     // [n_imgs*32]
@@ -185,9 +185,8 @@ __device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>&
 
 // Load + linearize image-sorted observation o of image img.
 template <int CT>
-__device__ __forceinline__ void view_image(const Ctx& c, int64_t o, int img, const Cam& cam,
+__device__ __forceinline__ void view_image(const Ctx& c, int64_t o, int pid, int img, const Cam& cam,
                                            const float* zc, ObsView<CT>& V) {
-  const int pid = __ldg(c.pids + o);
   const float X[3] = {__ldg(c.pts3d + 3 * (int64_t)pid), __ldg(c.pts3d + 3 * (int64_t)pid + 1),
                       __ldg(c.pts3d + 3 * (int64_t)pid + 2)};
   float dep[CT];
@@ -339,6 +338,7 @@ __global__ void __launch_bounds__(128) k_eliminate(Ctx c) {
   const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
   const int n = ke - kb;
   const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
+  if (task == 0 && lane == 0) c.misc[1] = lam;   // point damping, reused by the back-substitution
   if (n <= kWarp) {
     if (lane >= n) return;
     const int64_t k = kb + lane;
@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
     const int64_t o = c.d.c1_obs[e];
     const int64_t k = c.d.c1_k[e];
     ObsView<CT> V;
-    view_image<CT>(c, o, img, cam, zc, V);
+    view_image<CT>(c, o, c.d.c1_pid[e], img, cam, zc, V);
     diag_terms<CT>(c, V, k, acc);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -739,44 +739,119 @@ __global__ void k_spmv(DevPlan d, const float* __restrict__ S, const T* __restri
 }
 
 // ------------------------------------------------------------------------------------
-// point back-substitution: delta_p = L^-T (z - sum_o Y_o dc_o)
+// point back-substitution: delta_p = D^-1 (g_p - C delta_c) (ba_solver.py:203)
 // ------------------------------------------------------------------------------------
-template <int CT>
-__global__ void k_backsub(DevPlan d, const float* __restrict__ rec, const float* __restrict__ trec,
-                          const float* __restrict__ dc, float* __restrict__ dp) {
-  const int tl = blockIdx.x * blockDim.x + threadIdx.x;
-  if (tl >= d.nT_loc) return;
-  constexpr int R = rec_floats<CT>();
-  const float* t = trec + (int64_t)tl * 24;
-  float l[6], acc[3] = {t[18], t[19], t[20]};
+// Each track's Hpp, g_p and C delta_c are re-accumulated in double from the observations
+// (the same float32 per-observation Jacobians as the linearization), then solved with the
+// damped guarded Cholesky.  Weakly triangulated points (short baselines) make Hpp badly
+// conditioned, so the solve is done in double rather than from the float32 factors.
+__device__ __forceinline__ double seg_scan_d(double v, int lane, int seg_start) {
 #pragma unroll
-  for (int j = 0; j < 6; ++j) l[j] = t[12 + j];
-  for (int k = d.trk_ptr[tl]; k < d.trk_ptr[tl + 1]; ++k) {
-    const int img = d.img_t[k];
-    const int* sc = d.img_sc + 3 * img;
-    const float* Y = rec + (int64_t)k * R;
-    float v[9];
-#pragma unroll
-    for (int a = 0; a < 2; ++a) v[a] = sc[0] >= 0 ? dc[sc[0] + a] : 0.f;
-#pragma unroll
-    for (int a = 0; a < 6; ++a) v[2 + a] = sc[1] >= 0 ? dc[sc[1] + a] : 0.f;
-    float zz = 0.f;
-    if (sc[2] >= 0) {
-#pragma unroll
-      for (int ch = 0; ch < CT; ++ch) zz += Y[27 + ch] * dc[sc[2] + ch];
-    }
-    v[8] = zz;
-#pragma unroll
-    for (int a = 0; a < 9; ++a) {
-      acc[0] -= Y[3 * a] * v[a];
-      acc[1] -= Y[3 * a + 1] * v[a];
-      acc[2] -= Y[3 * a + 2] * v[a];
-    }
+  for (int d = 1; d < 32; d <<= 1) {
+    double u = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane - d >= seg_start) v += u;
   }
-  float x[3];
-  chol3_bwd<float>(l, acc, x);
-  const int64_t col = d.trk_col[tl];
-  dp[3 * col] = x[0]; dp[3 * col + 1] = x[1]; dp[3 * col + 2] = x[2];
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+
+template <int CT>
+__device__ __forceinline__ void backsub_terms(const Ctx& c, int64_t k, const float* __restrict__ dc, double u[12],
+                                              int& tl) {
+  ObsView<CT> V;
+  view_local<CT>(c, k, V, tl);
+  const int* sc = c.d.img_sc + 3 * c.d.img_t[k];
+  double v[9];
+#pragma unroll
+  for (int a = 0; a < 2; ++a) v[a] = sc[0] >= 0 ? (double)dc[sc[0] + a] : 0.0;
+#pragma unroll
+  for (int a = 0; a < 6; ++a) v[2 + a] = sc[1] >= 0 ? (double)dc[sc[1] + a] : 0.0;
+  double zz = 0.0;
+  if (sc[2] >= 0) {
+#pragma unroll
+    for (int ch = 0; ch < CT; ++ch) zz += (double)V.dep[ch] * (double)dc[sc[2] + ch];
+  }
+  v[8] = zz;
+  double Jv[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    double s = 0.0;
+#pragma unroll
+    for (int a = 0; a < 9; ++a) s += (double)V.Jcw[9 * i + a] * v[a];
+    Jv[i] = s;
+  }
+  const int ia[6] = {0, 0, 0, 1, 1, 2}, ib[6] = {0, 1, 2, 1, 2, 2};
+#pragma unroll
+  for (int e = 0; e < 6; ++e) {
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) s += (double)V.Jpw[3 * i + ia[e]] * (double)V.Jpw[3 * i + ib[e]];
+    u[e] = s;
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    double g = 0.0, cdv = 0.0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      g += (double)V.Jp[3 * i + j] * (double)V.Wr[i];
+      cdv += (double)V.Jpw[3 * i + j] * Jv[i];
+    }
+    u[6 + j] = g - cdv;
+  }
+  u[9] = u[10] = u[11] = 0.0;
+}
+
+__device__ __forceinline__ void backsub_solve(const Ctx& c, double lam, int tl, const double u[12], float* dp) {
+  double l[6], z[3], x[3];
+  chol3<double>(u[0] + lam, u[1], u[2], u[1], u[3] + lam, u[4], u[2], u[4], u[5] + lam, 1e-12, l);
+  const double rhs[3] = {u[6], u[7], u[8]};
+  chol3_fwd<double>(l, rhs, z);
+  chol3_bwd<double>(l, z, x);
+  const int64_t col = c.d.trk_col[tl];
+  dp[3 * col] = (float)x[0]; dp[3 * col + 1] = (float)x[1]; dp[3 * col + 2] = (float)x[2];
+}
+
+template <int CT>
+__global__ void __launch_bounds__(128) k_backsub(Ctx c, const float* __restrict__ dc, float* __restrict__ dp) {
+  const int task = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (task >= c.d.n_pt_tasks) return;
+  const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
+  const int n = ke - kb;
+  const double lam = (double)c.misc[1];
+  double u[12];
+#pragma unroll
+  for (int j = 0; j < 12; ++j) u[j] = 0.0;
+  if (n <= kWarp) {
+    const bool act = lane < n;
+    int tl = -1 - lane;
+    if (act) backsub_terms<CT>(c, kb + lane, dc, u, tl);
+    const int tl_prev = __shfl_up_sync(0xffffffffu, tl, 1);
+    const int tl_next = __shfl_down_sync(0xffffffffu, tl, 1);
+    const bool head = act && (lane == 0 || tl_prev != tl);
+    const bool tail = act && (lane == n - 1 || tl_next != tl);
+    const unsigned heads = __ballot_sync(0xffffffffu, head);
+    const int seg_start = act ? 31 - __clz(heads & ((2u << lane) - 1u)) : lane;
+#pragma unroll
+    for (int j = 0; j < 9; ++j) u[j] = seg_scan_d(u[j], lane, seg_start);
+    if (tail) backsub_solve(c, lam, tl, u, dp);
+  } else {
+    const int tl = c.d.trk_t[kb];
+    for (int k = kb + lane; k < ke; k += kWarp) {
+      double w[12];
+      int tl_k;
+      backsub_terms<CT>(c, k, dc, w, tl_k);
+#pragma unroll
+      for (int j = 0; j < 9; ++j) u[j] += w[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 9; ++j) u[j] = warp_sum_d(u[j]);
+    if (lane == 0) backsub_solve(c, lam, tl, u, dp);
+  }
 }
 
 // ------------------------------------------------------------------------------------
@@ -839,6 +914,27 @@ int launch_points(const Ctx& c, cudaStream_t s) {
 }
 
 template <int CT>
+int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaStream_t s) {
+  switch (pass) {
+    case B3R_PASS_POINTS:
+      return launch_points<CT>(c, s);
+    case B3R_PASS_ELIMINATE:
+      if (c.d.n_pt_tasks == 0) return B3R_OK;
+      k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
+      return check_launch("eliminate pass");
+    case B3R_PASS_DIAG:
+      if (c.d.n_c1_chunks == 0) return B3R_OK;
+      k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, 0, s>>>(c, S, b, diagA);
+      return check_launch("diag pass");
+    case B3R_PASS_PAIRS:
+      if (c.d.n_tasks == 0) return B3R_OK;
+      k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, 0, s>>>(c, S);
+      return check_launch("pairs pass");
+  }
+  return fail(B3R_E_INVALID, "bad pass %d", pass);
+}
+
+template <int CT>
 int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
   if (c.d.n_pt_tasks > 0) {
     k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
@@ -856,10 +952,9 @@ int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t
 }
 
 template <int CT>
-int launch_backsub(const DevPlan& d, const float* rec, const float* trec, const float* dc, float* dp,
-                   cudaStream_t s) {
-  if (d.nT_loc == 0) return B3R_OK;
-  k_backsub<CT><<<grid_for(d.nT_loc, 128), 128, 0, s>>>(d, rec, trec, dc, dp);
+int launch_backsub(const Ctx& c, const float* dc, float* dp, cudaStream_t s) {
+  if (c.d.n_pt_tasks == 0) return B3R_OK;
+  k_backsub<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c, dc, dp);
   return check_launch("backsub");
 }
 
@@ -932,6 +1027,26 @@ extern "C" int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const 
   }
 }
 
+extern "C" int b3r_lin_pass(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                            void* workspace, const b3r_outputs* out, int pass, void* stream) {
+  B3R_REQUIRE(params && out, "NULL params/outputs");
+  Ctx c;
+  B3R_TRY(make_ctx(plan, params, opts, workspace, c));
+  B3R_TRY(check_device(plan));
+  cudaStream_t s = as_stream(stream);
+  c.hpp_max = out->hpp_max ? out->hpp_max : c.misc;
+  if (pass == B3R_PASS_PREP) {
+    k_prep_images<<<grid_for(c.d.n_imgs, 128), 128, 0, s>>>(c);
+    return check_launch("prep images");
+  }
+  switch (c.d.C) {
+#define X(CC) case CC: return launch_pass<CC>(c, pass, out->S_vals, out->b, out->diagA, s);
+    B3R_FOR_EACH_C(X)
+#undef X
+    default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", c.d.C);
+  }
+}
+
 extern "C" int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
                                 const b3r_outputs* out, void* stream) {
   B3R_REQUIRE(out && out->S_vals && out->diagA, "NULL outputs");
@@ -974,16 +1089,15 @@ extern "C" int b3r_schur_spmv_f64(const b3r_plan* plan, const float* S_vals, con
   return spmv_impl<double>(plan, S_vals, x, y, stream);
 }
 
-extern "C" int b3r_backsub(const b3r_plan* plan, const void* workspace, const float* delta_c, float* delta_p,
-                           void* stream) {
-  B3R_REQUIRE(plan && workspace && delta_c && delta_p, "NULL argument");
+extern "C" int b3r_backsub(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                           void* workspace, const float* delta_c, float* delta_p, void* stream) {
+  B3R_REQUIRE(params && delta_c && delta_p, "NULL argument");
+  Ctx c;
+  B3R_TRY(make_ctx(plan, params, opts, workspace, c));
   B3R_TRY(check_device(plan));
-  const char* w = (const char*)workspace;
-  const float* rec = (const float*)(w + plan->ws_rec);
-  const float* trec = (const float*)(w + plan->ws_trec);
   cudaStream_t s = as_stream(stream);
   switch (plan->d.C) {
-#define X(CC) case CC: return launch_backsub<CC>(plan->d, rec, trec, delta_c, delta_p, s);
+#define X(CC) case CC: return launch_backsub<CC>(c, delta_c, delta_p, s);
     B3R_FOR_EACH_C(X)
 #undef X
     default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", plan->d.C);

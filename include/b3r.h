@@ -232,6 +232,18 @@ int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const b3r_lin_opt
 int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
                      const b3r_outputs* out, void* stream);
 
+/* One pass of b3r_lin_points/b3r_lin_assemble on its own (profiling and custom
+ * pipelines): B3R_PASS_PREP (per-image records), _POINTS, _ELIMINATE, _DIAG, _PAIRS.
+ * Outputs are NOT zeroed here; the caller keeps the order prep, points, eliminate, then
+ * diag and pairs on zeroed S_vals / b / diagA. */
+#define B3R_PASS_PREP 0
+#define B3R_PASS_POINTS 1
+#define B3R_PASS_ELIMINATE 2
+#define B3R_PASS_DIAG 3
+#define B3R_PASS_PAIRS 4
+int b3r_lin_pass(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts, void* workspace,
+                 const b3r_outputs* out, int pass, void* stream);
+
 /* y = S x with S given by its upper block triangle (symmetric). x, y: [n_cam_params]. */
 int b3r_schur_spmv(const b3r_plan* plan, const float* S_vals, const float* x, float* y,
                    void* stream);
@@ -240,10 +252,12 @@ int b3r_schur_spmv_f64(const b3r_plan* plan, const float* S_vals, const double* 
                        void* stream);
 
 /* Point back-substitution delta_p = Hpp^-1 (g_p - Hpc delta_c) for this rank's tracks
- * (ba_solver.py:203), from the factors kept in `workspace` by the last linearization.
+ * (ba_solver.py:203).  Must follow a linearization of the same plan with the same
+ * params/opts/workspace (it reuses the per-image records and the point damping kept in
+ * the workspace); each track's point block is re-accumulated and solved in double.
  * delta_c: [n_cam_params]; delta_p: [n_points*3], only this rank's tracks written. */
-int b3r_backsub(const b3r_plan* plan, const void* workspace, const float* delta_c, float* delta_p,
-                void* stream);
+int b3r_backsub(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts, void* workspace,
+                const float* delta_c, float* delta_p, void* stream);
 
 #ifdef __cplusplus
 }

@@ -266,10 +266,10 @@ class Layout:
         self.block_type = np.concatenate([np.zeros(self.nK, int), np.ones(self.nP, int),
                                           np.full(self.nZ, 2)])
         # per-observation typed block ids (-1: inactive / zero)
-        self.bK = np.where(self.actK & ~self.zeroK, self.colK[self.cam], -1)
-        self.bP = np.where(self.actP & ~self.zeroP, self.nK + self.colP[self.node], -1)
-        self.bZ = np.where(self.actZ & ~self.zeroZ, self.nK + self.nP + self.colZ[self.img], -1)
-        self.tX = np.where(self.actX & ~self.zeroX, self.colX[self.trk], -1)
+        self.bK = np.where(self.actK & (not self.zeroK), self.colK[self.cam], -1)
+        self.bP = np.where(self.actP & (not self.zeroP), self.nK + self.colP[self.node], -1)
+        self.bZ = np.where(self.actZ & (not self.zeroZ), self.nK + self.nP + self.colZ[self.img], -1)
+        self.tX = np.where(self.actX & (not self.zeroX), self.colX[self.trk], -1)
 
     def obs_blocks(self):
         return np.stack([self.bK, self.bP, self.bZ], axis=1)

@@ -1,0 +1,163 @@
+"""GPU parity of the fused linearization + Schur assembly (C ABI part 2).
+
+* against the golden fixtures made by the reference's own solver (S, b, damped diag A);
+* against the CPU oracle on seeded scenes of every configuration generator;
+* the general path (residuals and weights passed in) against the recomputing path;
+* point back-substitution against the oracle;
+* at larger sizes, size-independent properties: S v against the implicit Schur operator
+  A v - B D^-1 C v built from the explicit Jacobian op, and b against J^T W r.
+"""
+import numpy as np
+import pytest
+import torch
+
+from blast3r_b200 import cujac
+from blast3r_b200.plan import BAPlan
+from blast3r_b200.synthetic import make_scene
+from oracle import ba_oracle as O
+from tests.helpers import TOL_ACC, golden_files, load_golden, rel_err, scene_inputs, to_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+def run_plan(inp, opts, recompute=True):
+    t = to_cuda(inp)
+    plan = BAPlan(t['infos'], t['pids'], len(inp['K']), len(inp['P_w2rig']), len(inp['pts3d']),
+                  inp['pix2d_dep'].shape[1], optim_K=opts.get('optim_K', True), optim_P=opts.get('optim_P', True),
+                  optim_Z=opts.get('optim_Z', True), optim_X=opts.get('optim_X', True))
+    is_log = opts.get('depth_mode', 'log') == 'log'
+    lo = BAPlan.lin_opts(is_depth_log=is_log, weight_z=opts['weight_z'], pnorm=opts['pnorm'],
+                         max_pix_err=opts['clip_pix_err'], huber_delta=opts['huber_delta'],
+                         no_grad_f_from_rz=opts.get('no_grad_f_from_rz', False), optim_Z0=opts.get('optim_Z0', True),
+                         optim_Z_1st_cam=opts.get('optim_Z_1st_cam', True))
+    if recompute:
+        p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                        t['pix2d_dep'], pix2d=t['pix2d'])
+    else:
+        res = cujac.residuals_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'],
+                                        t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], is_log,
+                                        opts['weight_z'], opts['pnorm'], opts['clip_pix_err'], opts['huber_delta'])
+        r, _, w = res.view(-1, 3, 3).unbind(dim=1)
+        p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                        t['pix2d_dep'], residuals=r, w_pts=w)
+    sys_ = plan.linearize(p, lo)
+    torch.cuda.synchronize()
+    return plan, sys_
+
+
+@pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
+def test_schur_matches_reference_solver(path):
+    inp, opts, ref = load_golden(path)
+    plan, s = run_plan(inp, opts)
+    S = s.to_dense().cpu().numpy()
+    assert S.shape == ref['f64_S'].shape
+    assert rel_err(S, ref['f64_S']) < TOL_ACC
+    assert rel_err(s.b.cpu().numpy(), ref['f64_b']) < TOL_ACC
+    # reference preconditioner: damped diag(A) clamped at 1e-12 (ba_solver.py:191-192)
+    assert rel_err(s.precond.cpu().numpy(), np.maximum(ref['f64_diagA'], 1e-12)) < TOL_ACC
+    # the S pattern holds exactly the reference's non-zero blocks (the oracle test pins the
+    # oracle pattern to them)
+    lay = O.Layout(inp['infos'], inp['pids'], len(inp['K']), len(inp['P_w2rig']), len(inp['pts3d']),
+                   inp['pix2d_dep'].shape[1], opts['optim_K'], opts['optim_P'], opts['optim_Z'], opts['optim_X'])
+    rows, cols = plan.pattern()
+    assert np.array_equal(np.stack([rows, cols], 1), O.s_pattern(lay))
+
+
+@pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
+def test_general_path_equals_recompute(path):
+    inp, opts, _ = load_golden(path)
+    _, a = run_plan(inp, opts, recompute=True)
+    _, b = run_plan(inp, opts, recompute=False)
+    assert rel_err(b.S_vals.cpu().numpy(), a.S_vals.cpu().numpy()) < 1e-6
+    assert rel_err(b.b.cpu().numpy(), a.b.cpu().numpy()) < 1e-6
+
+
+SCENES = [(0, None, None), (3, None, None), (1, 60, 6000), (2, 80, 8000), (4, 60, 6000)]
+
+
+@pytest.mark.parametrize('cfg,ni,nt', SCENES, ids=lambda v: str(v))
+def test_schur_matches_oracle(cfg, ni, nt):
+    sc = make_scene(cfg, n_imgs=ni, n_tracks=nt)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    want = O.linearize(inp, opts, dtype=np.float64, residual_dtype=np.float32)
+    _, s = run_plan(inp, opts)
+    assert rel_err(s.to_dense().cpu().numpy(), want['S']) < TOL_ACC
+    assert rel_err(s.b.cpu().numpy(), want['b']) < TOL_ACC
+    assert rel_err(s.diagA.cpu().numpy() + want['lam'], want['diagA']) < TOL_ACC
+
+
+@pytest.mark.parametrize('cfg', [0, 3])
+def test_backsub_matches_oracle(cfg):
+    sc = make_scene(cfg)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    want = O.linearize(inp, opts, dtype=np.float64, residual_dtype=np.float32)
+    plan, s = run_plan(inp, opts)
+    rng = np.random.default_rng(cfg)
+    dc = rng.normal(size=plan.n_cam_params) * 1e-3
+    dp = s.backsub(torch.from_numpy(dc).float().cuda()).cpu().numpy().reshape(-1, 3)
+    # oracle: delta_p = D^-1 (g_p - C dc), C = Hpc per observation summed per track
+    lay = want['layout']
+    Jc = O.camera_jacobian(want['J_cam'], want['J_zcf'], lay)
+    W = np.clip(want['residuals'][:, 6:9].astype(np.float32), np.float32(1e-6), np.float32(1e6)).astype(np.float64)
+    Hpc = np.einsum('nki,nk,nkj->nij', want['J_pts'], W, Jc)
+    idx = want['idx']
+    dco = np.where(idx >= 0, dc[np.maximum(idx, 0)], 0.0)
+    Cdc = np.zeros((lay.nX, 3))
+    np.add.at(Cdc, lay.tX, np.einsum('nij,nj->ni', Hpc, dco))
+    ref = O.chol3x3_solve(want['Hpp'], want['g_p'] - Cdc)
+    assert rel_err(dp, ref) < 1e-4
+
+
+@pytest.mark.parametrize('cfg', [1, 2])
+def test_schur_operator_property_full_size(cfg):
+    """S v == A v - B D^-1 C v with A, B, C, D built from the explicit Jacobian op (fp64),
+    and b == g_c - B D^-1 g_p, on the full configuration (size-independent check)."""
+    sc = make_scene(cfg)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    plan, s = run_plan(inp, opts)
+    t = to_cuda(inp)
+    res = cujac.residuals_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'],
+                                    t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], True, opts['weight_z'],
+                                    opts['pnorm'], opts['clip_pix_err'], opts['huber_delta'])
+    r, _, w = [x.contiguous() for x in res.view(-1, 3, 3).unbind(dim=1)]
+    Jc8, Jz, Jp = cujac.jacobians_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'],
+                                            t['pts3d'], t['pids'], t['pix2d_std'], t['pix2d_dep'], True, float64=True)
+    n, C = Jz.shape[0], Jz.shape[2]
+    W = w.clamp(1e-6, 1e6).double()
+    Jc = torch.zeros(n, 3, 8 + C, dtype=torch.float64, device='cuda')
+    Jc[:, :, :8] = Jc8
+    Jc[:, 2, 8:] = Jz[:, 0]
+    img = torch.searchsorted(t['infos'][0].long(), torch.arange(n, device='cuda'), right=True)
+    cam, node = t['infos'][2].long()[img], t['infos'][1].long()[img]
+    nbK, nbP = plan.info.nb_K, plan.info.nb_P
+    cols = torch.cat([2 * cam[:, None] + torch.arange(2, device='cuda'),
+                      plan.info.off_P + 6 * node[:, None] + torch.arange(6, device='cuda'),
+                      plan.info.off_Z + C * img[:, None] + torch.arange(C, device='cuda')], 1)
+    pid = t['pids'].long()
+    T = len(inp['pts3d'])
+    Hpp = torch.zeros(T, 3, 3, dtype=torch.float64, device='cuda').index_add_(0, pid, torch.einsum('nki,nk,nkj->nij', Jp, W, Jp))
+    lam_p = 1e-12 * torch.diagonal(Hpp, dim1=1, dim2=2).max()
+    Hpp = Hpp + lam_p * torch.eye(3, dtype=torch.float64, device='cuda')
+    Hpc = torch.einsum('nki,nk,nkj->nij', Jp, W, Jc)
+    g = (W * r.double())
+    g_c = torch.zeros(plan.n_cam_params, dtype=torch.float64, device='cuda').index_add_(0, cols.reshape(-1), torch.einsum('nkj,nk->nj', Jc, g).reshape(-1))
+    g_p = torch.zeros(T, 3, dtype=torch.float64, device='cuda').index_add_(0, pid, torch.einsum('nkj,nk->nj', Jp, g))
+    Dinv = torch.linalg.inv(Hpp)
+    gen = torch.Generator(device='cuda').manual_seed(0)
+    v = torch.randn(plan.n_cam_params, dtype=torch.float64, device='cuda', generator=gen)
+
+    def schur_mv(v):
+        Jv = torch.einsum('nkj,nj->nk', Jc, v[cols])
+        Av = torch.zeros_like(v).index_add_(0, cols.reshape(-1), torch.einsum('nkj,nk->nj', Jc, W * Jv).reshape(-1))
+        Cv = torch.zeros(T, 3, dtype=torch.float64, device='cuda').index_add_(0, pid, torch.einsum('nij,nj->ni', Hpc, v[cols]))
+        DCv = torch.einsum('tij,tj->ti', Dinv, Cv)
+        BDCv = torch.zeros_like(v).index_add_(0, cols.reshape(-1), torch.einsum('nij,ni->nj', Hpc, DCv[pid]).reshape(-1))
+        return Av - BDCv
+
+    lam = s.precond.double() - s.diagA.double()          # damping added to diag(S)
+    want = schur_mv(v) + lam * v
+    got = s.matvec(v)
+    assert rel_err(got.cpu().numpy(), want.cpu().numpy()) < TOL_ACC
+    Dg = torch.einsum('tij,tj->ti', Dinv, g_p)
+    b_want = g_c - torch.zeros_like(g_c).index_add_(0, cols.reshape(-1), torch.einsum('nij,ni->nj', Hpc, Dg[pid]).reshape(-1))
+    assert rel_err(s.b.cpu().numpy(), b_want.cpu().numpy()) < TOL_ACC
