@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""Benchmark of the BA linearization + Schur assembly hot path (one JSON line on rank 0).
+
+A step is one linearization of the whole problem: residual, Jacobians, IRLS weights,
+per-track 3x3 point elimination and assembly of the Schur-reduced camera/depth system S
+and its gradient b (plus, on several GPUs, the all-reduce of the point-damping maximum and
+the NCCL reduce of the partial S, b and diag(A) to rank 0, which then damps S).
+
+Workload: configs[2] of the benchmark (1,000 cameras, 1M tracks, ~5.8M observations,
+mono focal, K=4 depth channels), seeded synthetic data; tracks are sharded by id across
+ranks (strong scaling: the total problem is fixed).  The observation arrays (~260 MB) are
+larger than the 126 MB L2, so no explicit flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 2]
+"""
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'observations linearized+Schur-assembled/sec'
+UNIT = 'observations/s'
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--config', type=int, default=2)
+    ap.add_argument('--cpu-sample-tracks', type=int, default=20000,
+                    help='tracks in the bounded CPU-baseline sample (same generator)')
+    ap.add_argument('--ref-step-tracks', type=int, default=4000,
+                    help='tracks per step of the reference (CPU) arm')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--e2e-steps', type=int, default=5)
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    return world, rank, local
+
+
+def shard_tracks(pids, n_tracks, world, rank):
+    """Contiguous track-id range of this rank, balanced by observation count."""
+    cnt = np.bincount(pids, minlength=n_tracks)
+    cum = np.concatenate([[0], np.cumsum(cnt)])
+    total = cum[-1]
+    bounds = [int(np.searchsorted(cum, total * r / world, side='left')) for r in range(world + 1)]
+    bounds[0], bounds[-1] = 0, n_tracks
+    return bounds[rank], bounds[rank + 1], int(cum[bounds[rank + 1]] - cum[bounds[rank]])
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.gpu}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.f.read().strip().splitlines():
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == 'active':
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unavailable'], 'samples': 0}
+        return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': float(max(mx)), 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.isfile(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+def algorithmic_bytes(n_obs, n_tracks, plan_info, block_size):
+    """Compulsory bytes of one linearization (fp32): per observation pix2d 8 + std 8 +
+    depth channels 4C + image id 4 + residual write 12 = 52 B (C = 5); per track point 12
+    + track offset 4 = 16 B; S (upper-triangle scalars) and b written once."""
+    bs = np.asarray(block_size, np.int64)
+    nnz_upper = int(plan_info.nnz) - int((bs * (bs - 1) // 2).sum())
+    return 52 * n_obs + 16 * n_tracks + 4 * (nnz_upper + int(plan_info.n_cam_params)), nnz_upper
+
+
+def fp32_flops(L):
+    """Useful fp32 FLOPs of one linearization with w = 13 camera-side columns:
+    per observation ~300 + 3w(w+1) + 36w + 36, per observation pair 6 w^2."""
+    w = 13
+    L = np.asarray(L, np.int64)
+    return float((L * (300 + 3 * w * (w + 1) + 36 * w + 36) + L * (L - 1) // 2 * 6 * w * w).sum())
+
+
+def cpu_baseline(cfg, n_tracks, scene_kw=None):
+    """Oracle port on a bounded sample of the same generator (single process)."""
+    from blast3r_b200.synthetic import make_scene
+    from oracle import ba_oracle as O
+    sc = make_scene(cfg, n_tracks=n_tracks)
+    d = dict(sc.lm_inputs())
+    d['infos'] = d.pop('rigs')
+    t = time.perf_counter()
+    O.linearize(d, sc.options, dtype=np.float64, dense=False, residual_dtype=np.float32)
+    dt = time.perf_counter() - t
+    return {'value': sc.n_obs / dt, 'unit': UNIT, 'cores': 1, 'kind': 'port',
+            'sample': f'configs[{cfg}] generator with {n_tracks} tracks ({sc.n_obs} observations), '
+                      f'oracle/ba_oracle.linearize (numpy float64, sparse S), {dt:.1f} s'}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from blast3r_b200.synthetic import make_scene
+    from oracle import ba_oracle as O
+    times, nobs = [], []
+    for step in range(args.warmup + args.steps):
+        sc = make_scene(args.config, n_tracks=args.ref_step_tracks, seed=1000 + step)
+        d = dict(sc.lm_inputs())
+        d['infos'] = d.pop('rigs')
+        t = time.perf_counter()
+        O.linearize(d, sc.options, dtype=np.float64, dense=False, residual_dtype=np.float32)
+        if step >= args.warmup:
+            times.append(time.perf_counter() - t)
+            nobs.append(sc.n_obs)
+    value = float(np.sum(nobs) / np.sum(times))
+    sample = (f'configs[{args.config}] generator, {args.ref_step_tracks} tracks (~{int(np.mean(nobs))} observations) '
+              f'per step, oracle port (numpy float64, sparse S), single process')
+    print(json.dumps({'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus,
+                      'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1e3 * float(np.mean(times)),
+                      'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f64',
+                      'data': 'synthetic', 'config': {'workload': f'configs[{args.config}] (bounded CPU sample)'},
+                      'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': 1, 'kind': 'port', 'sample': sample},
+                      'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    from blast3r_b200 import _lib as L
+    from blast3r_b200.plan import BAPlan
+    from blast3r_b200.synthetic import make_scene
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+    sc = make_scene(args.config)
+    t0, t1, n_local = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+    o = sc.options
+    plan = BAPlan(sc.infos, sc.pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
+                  optim_P=o['optim_P'], optim_Z=o['optim_Z'], optim_X=o['optim_X'], track_range=(t0, t1), device=dev)
+    host = {k: np.ascontiguousarray(v) for k, v in sc.lm_inputs().items()}
+    t = {k: torch.from_numpy(v).to(dev) for k, v in host.items()}
+    p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'], t['pix2d_dep'],
+                    pix2d=t['pix2d'])
+    lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
+                         huber_delta=o['huber_delta'])
+    ncp, nnz = plan.n_cam_params, int(plan.info.nnz)
+    red = torch.empty(nnz + 2 * ncp, dtype=torch.float32, device=dev)     # S | b | diag(A), one reduce
+    S, b, dA = red[:nnz], red[nnz:nnz + ncp], red[nnz + ncp:]
+    pc = torch.empty(ncp, dtype=torch.float32, device=dev)
+    hm = torch.empty(1, dtype=torch.float32, device=dev)
+    outs = (S, b, dA, pc, hm)
+
+    def step():
+        if world == 1:
+            plan.linearize(p, lo, outs)
+            return
+        plan.lin_stage('points', p, lo, outs)
+        dist.all_reduce(hm, op=dist.ReduceOp.MAX)
+        plan.lin_stage('assemble', p, lo, outs)
+        dist.reduce(red, dst=0)
+        if rank == 0:
+            plan.lin_stage('finalize', p, lo, outs)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_total = float(ms.item())
+    ms_step = ms_total / args.steps
+    value = sc.n_obs * args.steps / (ms_total * 1e-3)
+    clocks = clk.summary()
+
+    # per-pass device time on this rank (same workload, events between the launches)
+    names = ['prep', 'points', 'eliminate', 'diag', 'pairs', 'finalize']
+    acc = {k: 0.0 for k in names}
+    R = 5
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(R):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        S.zero_(); b.zero_(); dA.zero_(); hm.zero_()
+        ev[0].record()
+        for j, nm in enumerate(names):
+            if nm == 'finalize':
+                plan.lin_stage('finalize', p, lo, outs)
+            else:
+                pas = dict(prep=L.PASS_PREP, points=L.PASS_POINTS, eliminate=L.PASS_ELIMINATE, diag=L.PASS_DIAG,
+                           pairs=L.PASS_PAIRS)[nm]
+                plan.lin_pass(pas, p, lo, outs)
+            ev[j + 1].record()
+        torch.cuda.synchronize()
+        for j, nm in enumerate(names):
+            acc[nm] += ev[j].elapsed_time(ev[j + 1]) / R
+    tot = sum(acc.values())
+    passes = {k: {'ms': round(v, 4), 'share': round(v / tot, 4)} for k, v in acc.items()}
+
+    # end to end through the public API with host buffers
+    pin = {k: torch.from_numpy(v).pin_memory() for k, v in host.items()}
+    S_h = torch.empty(nnz, dtype=torch.float32).pin_memory()
+    b_h = torch.empty(ncp, dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    d2h = (S_h.numel() + b_h.numel()) * 4
+
+    def e2e_step():
+        for k in pin:
+            t[k].copy_(pin[k], non_blocking=True)
+        plan.stage_obs(t['pix2d'], t['pix2d_std'], t['pix2d_dep'])
+        step()
+        if rank == 0:
+            S_h.copy_(S, non_blocking=True)
+            b_h.copy_(b, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_e, op=dist.ReduceOp.MAX)
+    e2e_value = sc.n_obs * args.e2e_steps / (float(ms_e.item()) * 1e-3)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        L_t = np.bincount(sc.pids, minlength=sc.n_tracks)[t0:t1]
+        B, nnz_upper = algorithmic_bytes(n_local, t1 - t0, plan.info, plan.block_size)
+        achieved = B / (ms_step * 1e-3) / 1e9
+        flops = fp32_flops(L_t)
+        sm_mhz = clocks['sm_mhz'] or 1965.0
+        fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+        roof = {'bound': 'hbm', 'achieved': round(achieved, 2), 'peak': peak, 'unit': 'GB/s',
+                'frac': round(achieved / peak, 4), 'traffic': read_traffic(args.config, world),
+                'kernel': 'fused linearization step (prep, points, eliminate, diag, pairs, finalize)',
+                'algorithmic_bytes_per_step': int(B), 'peak_kind': f'of {peak_kind}',
+                'fp32': {'flops_per_step': flops, 'achieved_tflops': round(flops / (ms_step * 1e-3) / 1e12, 2),
+                         'peak_tflops_at_median_clock': round(fp32_peak, 1),
+                         'frac': round(flops / (ms_step * 1e-3) / 1e12 / fp32_peak, 4)},
+                'passes': passes}
+        line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+                'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'strong',
+                'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded generator of the configuration)',
+                'config': {'workload': f'configs[{args.config}]', 'n_obs': sc.n_obs, 'n_tracks': sc.n_tracks,
+                           'n_imgs': sc.n_imgs, 'mean_track_length': sc.meta['mean_track_length'],
+                           'n_obs_pairs': int(plan.info.n_pairs), 'nnz_S': nnz,
+                           'parallelism': f'track-sharded x{world}' + (' + NCCL reduce of S, b' if world > 1 else ''),
+                           'l2': 'inputs larger than L2 (observation arrays ~260 MB), no flush'},
+                'roofline': roof, 'clocks': clocks,
+                'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
+                'gpu_launches': (6 + (1 if world == 1 else 0)) * args.steps}
+        if world == 1 and not args.no_cpu_baseline:
+            line['cpu_baseline'] = cpu_baseline(args.config, args.cpu_sample_tracks)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(cfg, world):
+    """DRAM bytes per step from the committed ncu summary (profiles/), or None."""
+    path = os.path.join(ROOT, 'profiles', f'traffic_cfg{cfg}.txt')
+    if world != 1 or not os.path.isfile(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.startswith('dram_bytes_per_step:'):
+                return float(line.split(':', 1)[1])
+    return None
+
+
+def main():
+    args = parse_args()
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -559,11 +559,18 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
 // thread holds more than 5 rows of accumulators; every role streams the same pairs.
 constexpr int kPairBatch = 32;
 
-template <int CT> __host__ __device__ constexpr int pair_roles() { return (8 + CT + 4) / 5; }
-template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() { return r * (8 + CT) / NR; }
+// 16-byte asynchronous global -> shared copies (cp.async, completion by commit groups)
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+// Stage the two records of up to 32 pairs into `buf` ([2 sides][32 pairs][RS floats]).
 template <int CT>
-__device__ __forceinline__ void stage_batch(const Ctx& c, int64_t base, int64_t pe, float* sm_row, float* sm_col) {
+__device__ __forceinline__ void stage_batch(const Ctx& c, int64_t base, int64_t pe, float* buf) {
   constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
   for (int q = threadIdx.x; q < 2 * kPairBatch * Q; q += blockDim.x) {
     const int ri = q / Q, part = q - ri * Q;
@@ -572,13 +579,12 @@ __device__ __forceinline__ void stage_batch(const Ctx& c, int64_t base, int64_t 
     if (p < pe) {
       const int2 kk = c.d.pairs[p];
       const int64_t k = side ? kk.y : kk.x;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(c.rec + k * R) + part);
-      float* dst = (side ? sm_col : sm_row) + pair * RS + 4 * part;
-      *reinterpret_cast<float4*>(dst) = v;
+      cp_async16(buf + (side * kPairBatch + pair) * RS + 4 * part, c.rec + k * R + 4 * part);
     }
   }
 }
 
+// Add -v to S at output (row a, column bcol) of segment s's pair product.
 template <int CT>
 __device__ __forceinline__ void emit_pair_value(const Ctx& c, float* __restrict__ S, int s, int a, int bcol, float v) {
   const int ta = a < 2 ? 0 : (a < 8 ? 1 : 2), ra = a < 2 ? a : (a < 8 ? a - 2 : a - 8);
@@ -598,28 +604,51 @@ __device__ __forceinline__ void emit_pair_value(const Ctx& c, float* __restrict_
   }
 }
 
+template <int CT> __host__ __device__ constexpr int pair_roles() { return (8 + CT + 4) / 5; }
+template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() { return r * (8 + CT) / NR; }
+template <int CT> __host__ __device__ constexpr int pair_max_acc() {
+  return (role_row<CT, pair_roles<CT>(), 1>() - role_row<CT, pair_roles<CT>(), 0>() + 1) * (8 + CT);
+}
+template <int CT> __host__ __device__ constexpr int pair_stage_floats() {
+  return 2 * 2 * kPairBatch * (rec_floats<CT>() + 4);
+}
+template <int CT> __host__ __device__ constexpr int pair_red_floats() {
+  return pair_roles<CT>() * pair_max_acc<CT>() * 33;
+}
+template <int CT> __host__ __device__ constexpr int pair_smem_floats() {
+  return pair_stage_floats<CT>() > pair_red_floats<CT>() ? pair_stage_floats<CT>() : pair_red_floats<CT>();
+}
+
+// One role (output rows [A0, A1)) of a pair task.  Every warp of the CTA takes part in
+// the staging; each lane accumulates the products of pair `lane` of every batch.
 template <int CT, int A0, int A1>
 __device__ __forceinline__ void pair_role(const Ctx& c, float* __restrict__ S, int s, int64_t pb, int64_t pe,
-                                          float* sm_row, float* sm_col) {
+                                          float* sm) {
   constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
   constexpr int W = 8 + CT, NA = A1 - A0;
-  // row-record floats this role reads: Y columns of its focal/tau rows, Y column 8 and
-  // its depth channels for depth rows
   constexpr int LO = A0 < 8 ? 3 * A0 : 24;
   constexpr int HI = A1 > 8 ? 27 + (A1 - 8) : 3 * A1;
   constexpr int QLO = LO / 4, QHI = (HI + 3) / 4;
   constexpr bool HAS_Z = A1 > 8;
+  constexpr int BUF = 2 * kPairBatch * RS;
   const int lane = threadIdx.x & 31;
   float acc[NA * W];
 #pragma unroll
   for (int v = 0; v < NA * W; ++v) acc[v] = 0.f;
-  for (int64_t base = pb; base < pe; base += kPairBatch) {
-    stage_batch<CT>(c, base, pe, sm_row, sm_col);
+  const int nb = (int)((pe - pb + kPairBatch - 1) / kPairBatch);
+  stage_batch<CT>(c, pb, pe, sm);
+  cp_async_commit();
+  for (int it = 0; it < nb; ++it) {
+    const int64_t base = pb + (int64_t)it * kPairBatch;
+    if (it + 1 < nb) stage_batch<CT>(c, base + kPairBatch, pe, sm + ((it + 1) & 1) * BUF);
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
+    const float* buf = sm + (it & 1) * BUF;
     if (base + lane < pe) {
       float yc[R], yr[R];
-      const float4* pc = reinterpret_cast<const float4*>(sm_col + lane * RS);
-      const float4* pr = reinterpret_cast<const float4*>(sm_row + lane * RS);
+      const float4* pr = reinterpret_cast<const float4*>(buf + lane * RS);
+      const float4* pc = reinterpret_cast<const float4*>(buf + (kPairBatch + lane) * RS);
 #pragma unroll
       for (int q = 0; q < Q; ++q) {
         const float4 v = pc[q];
@@ -658,31 +687,35 @@ __device__ __forceinline__ void pair_role(const Ctx& c, float* __restrict__ S, i
     }
     __syncthreads();
   }
+  // epilogue: transpose the lane partials through shared memory (stride 33: conflict-free),
+  // then each lane sums and emits values lane, lane+32, ... with a compact runtime loop
+  float* red = sm + (threadIdx.x >> 5) * pair_max_acc<CT>() * 33;
 #pragma unroll
-  for (int v = 0; v < NA * W; ++v) {
-    const float tot = warp_sum(acc[v]);
-    if (lane == (v & 31)) emit_pair_value<CT>(c, S, s, A0 + v / W, v % W, tot);
+  for (int v = 0; v < NA * W; ++v) red[v * 33 + lane] = acc[v];
+  __syncwarp();
+  for (int v = lane; v < NA * W; v += 32) {
+    float t = 0.f;
+    for (int j = 0; j < 32; ++j) t += red[v * 33 + j];
+    emit_pair_value<CT>(c, S, s, A0 + v / W, v % W, t);
   }
 }
 
 template <int CT>
 __global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* __restrict__ S) {
-  constexpr int R = rec_floats<CT>(), RS = R + 4, NR = pair_roles<CT>();
-  __shared__ __align__(16) float sm[2 * kPairBatch * RS];
+  constexpr int NR = pair_roles<CT>();
+  extern __shared__ __align__(16) float sm_dyn[];
   const int64_t task = blockIdx.x;
   const int s = c.d.task_seg[task];
   const int64_t pb = c.d.task_pb[task], pe = c.d.task_pb[task + 1];
-  float* sm_row = sm;
-  float* sm_col = sm + kPairBatch * RS;
   const int role = threadIdx.x >> 5;
-  if (role == 0) pair_role<CT, role_row<CT, NR, 0>(), role_row<CT, NR, 1>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 1) if (role == 1) pair_role<CT, role_row<CT, NR, 1>(), role_row<CT, NR, 2>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 2) if (role == 2) pair_role<CT, role_row<CT, NR, 2>(), role_row<CT, NR, 3>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 3) if (role == 3) pair_role<CT, role_row<CT, NR, 3>(), role_row<CT, NR, 4>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 4) if (role == 4) pair_role<CT, role_row<CT, NR, 4>(), role_row<CT, NR, 5>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 5) if (role == 5) pair_role<CT, role_row<CT, NR, 5>(), role_row<CT, NR, 6>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 6) if (role == 6) pair_role<CT, role_row<CT, NR, 6>(), role_row<CT, NR, 7>()>(c, S, s, pb, pe, sm_row, sm_col);
-  if constexpr (NR > 7) if (role == 7) pair_role<CT, role_row<CT, NR, 7>(), role_row<CT, NR, 8>()>(c, S, s, pb, pe, sm_row, sm_col);
+  if (role == 0) pair_role<CT, role_row<CT, NR, 0>(), role_row<CT, NR, 1>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 1) if (role == 1) pair_role<CT, role_row<CT, NR, 1>(), role_row<CT, NR, 2>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 2) if (role == 2) pair_role<CT, role_row<CT, NR, 2>(), role_row<CT, NR, 3>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 3) if (role == 3) pair_role<CT, role_row<CT, NR, 3>(), role_row<CT, NR, 4>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 4) if (role == 4) pair_role<CT, role_row<CT, NR, 4>(), role_row<CT, NR, 5>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 5) if (role == 5) pair_role<CT, role_row<CT, NR, 5>(), role_row<CT, NR, 6>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 6) if (role == 6) pair_role<CT, role_row<CT, NR, 6>(), role_row<CT, NR, 7>()>(c, S, s, pb, pe, sm_dyn);
+  if constexpr (NR > 7) if (role == 7) pair_role<CT, role_row<CT, NR, 7>(), role_row<CT, NR, 8>()>(c, S, s, pb, pe, sm_dyn);
 }
 
 // ------------------------------------------------------------------------------------
@@ -914,6 +947,19 @@ int launch_points(const Ctx& c, cudaStream_t s) {
 }
 
 template <int CT>
+int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
+  const size_t smem = pair_smem_floats<CT>() * sizeof(float);
+  static bool configured = false;          // one attribute call per instantiation
+  if (!configured) {
+    B3R_TRY(check_cuda(cudaFuncSetAttribute(k_pairs<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "pairs smem attribute"));
+    configured = true;
+  }
+  k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, smem, s>>>(c, S);
+  return check_launch("pairs pass");
+}
+
+template <int CT>
 int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaStream_t s) {
   switch (pass) {
     case B3R_PASS_POINTS:
@@ -928,8 +974,7 @@ int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaSt
       return check_launch("diag pass");
     case B3R_PASS_PAIRS:
       if (c.d.n_tasks == 0) return B3R_OK;
-      k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, 0, s>>>(c, S);
-      return check_launch("pairs pass");
+      return pairs_launch<CT>(c, S, s);
   }
   return fail(B3R_E_INVALID, "bad pass %d", pass);
 }
@@ -944,10 +989,7 @@ int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t
     k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, 0, s>>>(c, S, b, diagA);
     B3R_TRY(check_launch("diag pass"));
   }
-  if (c.d.n_tasks > 0) {
-    k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, 0, s>>>(c, S);
-    B3R_TRY(check_launch("pairs pass"));
-  }
+  if (c.d.n_tasks > 0) B3R_TRY(pairs_launch<CT>(c, S, s));
   return B3R_OK;
 }
 

@@ -207,3 +207,18 @@ class BAPlan:
             if p != q:
                 D[c0:c0 + bq, r0:r0 + bp] = blk.T
         return torch.from_numpy(D).to(S_vals.device)
+
+    def lin_pass(self, pass_id, params, opts, outputs, stream=None):
+        """One pass (b3r_lin_pass): PASS_PREP/POINTS/ELIMINATE/DIAG/PAIRS of _lib."""
+        S, b, dA, pc, hm = outputs
+        out = L.Outputs(S_vals=S.data_ptr(), b=b.data_ptr(), diagA=dA.data_ptr(),
+                        precond=pc.data_ptr() if pc is not None else None, hpp_max=hm.data_ptr())
+        s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        L.call('b3r_lin_pass', self._h, C.byref(params), C.byref(opts), self.workspace(), C.byref(out),
+               int(pass_id), s)
+
+    def stage_obs(self, pix2d, pix2d_std, pix2d_dep, stream=None):
+        """Re-gather the static observation arrays into the plan's track-sorted copy."""
+        s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        L.call('b3r_plan_stage_obs', self._h, pix2d.data_ptr() if pix2d is not None else None,
+               pix2d_std.data_ptr(), pix2d_dep.data_ptr(), s)

@@ -446,7 +446,24 @@ def schur_system(J_cam, J_zcf, J_pts, residuals, w_pts, layout, clamp_w=(1e-6, 1
                 _scatter_sym(S, idx, P, pi, pj, sign=-1.0)
         S[np.arange(nc), np.arange(nc)] += lam
         out['S'] = S
+    else:
+        # same sums, accumulated as a sparse matrix in chunks (large problems)
+        import scipy.sparse as sp
+        S = _sparse_sum(idx, Hcc, np.arange(n), np.arange(n), nc, 1.0)
+        for s in range(0, len(pairs_i), 1 << 17):
+            pi, pj = pairs_i[s:s + (1 << 17)], pairs_j[s:s + (1 << 17)]
+            P = np.einsum('nki,nkj->nij', Hpc[pi], DinvHpc[pj])
+            S = S + _sparse_sum(idx, P, pi, pj, nc, -1.0)
+        out['S'] = (S + sp.diags(lam)).tocsr()
     return out
+
+
+def _sparse_sum(idx, P, pi, pj, nc, sign):
+    import scipy.sparse as sp
+    ri = np.broadcast_to(idx[pi][:, :, None], P.shape)
+    cj = np.broadcast_to(idx[pj][:, None, :], P.shape)
+    m = (ri >= 0) & (cj >= 0)
+    return sp.coo_matrix((sign * P[m], (ri[m], cj[m])), shape=(nc, nc)).tocsr()
 
 
 def _track_pairs(trk):
