@@ -568,19 +568,25 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+// Pair indices of the batch starting at `base`: lane l holds pair base + l (or (-1,-1)).
+__device__ __forceinline__ int2 load_batch_pairs(const Ctx& c, int64_t base, int64_t pe) {
+  const int64_t p = base + (threadIdx.x & 31);
+  return p < pe ? __ldg(reinterpret_cast<const int2*>(c.d.pairs) + p) : make_int2(-1, -1);
+}
+
 // Stage the two records of up to 32 pairs into `buf` ([2 sides][32 pairs][RS floats]).
+// `kk` is this warp's copy of the batch's pair indices (load_batch_pairs); every warp of
+// the CTA holds the same 32 indices, so the item loop needs no dependent global load.
 template <int CT>
-__device__ __forceinline__ void stage_batch(const Ctx& c, int64_t base, int64_t pe, float* buf) {
+__device__ __forceinline__ void stage_batch(const Ctx& c, int2 kk, float* buf) {
   constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
   for (int q = threadIdx.x; q < 2 * kPairBatch * Q; q += blockDim.x) {
     const int ri = q / Q, part = q - ri * Q;
     const int pair = ri >> 1, side = ri & 1;
-    const int64_t p = base + pair;
-    if (p < pe) {
-      const int2 kk = c.d.pairs[p];
-      const int64_t k = side ? kk.y : kk.x;
-      cp_async16(buf + (side * kPairBatch + pair) * RS + 4 * part, c.rec + k * R + 4 * part);
-    }
+    const int kx = __shfl_sync(0xffffffffu, kk.x, pair);
+    const int ky = __shfl_sync(0xffffffffu, kk.y, pair);
+    const int k = side ? ky : kx;
+    if (k >= 0) cp_async16(buf + (side * kPairBatch + pair) * RS + 4 * part, c.rec + (int64_t)k * R + 4 * part);
   }
 }
 
@@ -636,12 +642,14 @@ __device__ __forceinline__ void pair_role(const Ctx& c, float* __restrict__ S, i
 #pragma unroll
   for (int v = 0; v < NA * W; ++v) acc[v] = 0.f;
   const int nb = (int)((pe - pb + kPairBatch - 1) / kPairBatch);
-  stage_batch<CT>(c, pb, pe, sm);
+  stage_batch<CT>(c, load_batch_pairs(c, pb, pe), sm);
   cp_async_commit();
+  int2 kk_next = load_batch_pairs(c, pb + kPairBatch, pe);      // one batch ahead
   for (int it = 0; it < nb; ++it) {
     const int64_t base = pb + (int64_t)it * kPairBatch;
-    if (it + 1 < nb) stage_batch<CT>(c, base + kPairBatch, pe, sm + ((it + 1) & 1) * BUF);
+    if (it + 1 < nb) stage_batch<CT>(c, kk_next, sm + ((it + 1) & 1) * BUF);
     cp_async_commit();
+    kk_next = load_batch_pairs(c, base + 2 * kPairBatch, pe);
     cp_async_wait<1>();
     __syncthreads();
     const float* buf = sm + (it & 1) * BUF;
