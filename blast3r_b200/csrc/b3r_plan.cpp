@@ -78,6 +78,7 @@ struct PlanBuild {
   // pattern
   std::vector<int> row_ptr, col_idx, val_off;
   std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
+  std::vector<int4> t_idx, c1_idx;
   int64_t nnz = 0;
 };
 
@@ -227,6 +228,15 @@ static int build_tracks(PlanBuild& B) {
     ++in_chunk;
   }
   B.c1_chunk.push_back((int)B.c1_obs.size());
+  // packed per-observation indices (one 16-byte load per observation in the kernels)
+  B.t_idx.resize(B.perm_t.size());
+  for (size_t kk = 0; kk < B.perm_t.size(); ++kk)
+    B.t_idx[kk] = make_int4(B.img_t[kk], B.loc_tracks[B.trk_t[kk]], B.trk_t[kk], B.perm_t[kk]);
+  B.c1_idx.resize(B.c1_obs.size());
+  for (size_t e = 0; e < B.c1_obs.size(); ++e) {
+    const int kk = B.c1_k[e];
+    B.c1_idx[e] = make_int4(B.c1_obs[e], kk, B.c1_pid[e], kk >= 0 ? B.trk_t[kk] : -1);
+  }
   return B3R_OK;
 }
 
@@ -504,6 +514,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.row_ptr, &d.row_ptr); A.add(B.col_idx, &d.col_idx); A.add(B.val_off, &d.val_off);
   A.add(B.bsize, &d.bsize); A.add(B.boff, &d.boff); A.add(B.sdiag_pos, &d.sdiag_pos);
   A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);
+  A.add(B.t_idx, &d.t_idx); A.add(B.c1_idx, &d.c1_idx);
   if (!host_only) {
     int rc = A.upload(&P->dev_mem);
     cudaSetDevice(prev_dev);

@@ -79,6 +79,8 @@ struct DevPlan {
   const int* sdiag_pos;   // [n_cam_params] position of each diagonal scalar in S_vals
   const int* blk_row;     // [nnzb] block row of each stored block
   const int* trk_ptr;     // [nT_loc+1] first k of each local track
+  const int4* t_idx;      // [n_loc] (image, global track id, tl, o) of local observation k
+  const int4* c1_idx;     // [n_c1] (o, k or -1, track id, tl or -1) of image-major entry e
 };
 
 struct HostPattern {

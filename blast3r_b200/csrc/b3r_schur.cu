@@ -155,9 +155,9 @@ __device__ __forceinline__ void make_view(const Ctx& c, const ObsLin& L, float r
 template <int CT>
 __device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>& V, int& tl) {
   const DevPlan& d = c.d;
-  const int img = d.img_t[k];
-  tl = d.trk_t[k];
-  const int gid = d.trk_gid[tl];
+  const int4 ix = __ldg(d.t_idx + k);          // image, global track id, local track, o
+  const int img = ix.x, gid = ix.y;
+  tl = ix.z;
   const Cam cam = load_cam(c.img_rec + (int64_t)img * kImgRec);
   const float X[3] = {__ldg(c.pts3d + 3 * (int64_t)gid), __ldg(c.pts3d + 3 * (int64_t)gid + 1),
                       __ldg(c.pts3d + 3 * (int64_t)gid + 2)};
@@ -180,7 +180,7 @@ __device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>&
     r0 = c.t_rw[k]; r1 = c.t_rw[n + k]; r2 = c.t_rw[2 * n + k];
     w0 = c.t_rw[3 * n + k]; w1 = c.t_rw[4 * n + k]; w2 = c.t_rw[5 * n + k];
   }
-  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, d.perm_t[k], image_mask(d, img), V);
+  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, ix.w, image_mask(d, img), V);
 }
 
 // Load + linearize image-sorted observation o of image img.
@@ -398,7 +398,7 @@ struct DiagLayout {
 __host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - a * (a - 1) / 2 + (b - a); }
 
 template <int CT>
-__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, int64_t k, float* acc) {
+__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, int64_t k, int tl, float* acc) {
   using Lay = DiagLayout<CT>;
   float H[9][9];
 #pragma unroll
@@ -434,7 +434,7 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, i
       const float4 v = __ldg(r4 + q);
       Y[4 * q] = v.x; Y[4 * q + 1] = v.y; Y[4 * q + 2] = v.z; Y[4 * q + 3] = v.w;
     }
-    const float* tz = c.trec + (int64_t)c.d.trk_t[k] * 24 + 18;
+    const float* tz = c.trec + (int64_t)tl * 24 + 18;
     const float z0 = tz[0], z1 = tz[1], z2 = tz[2];
 #pragma unroll
     for (int a = 0; a < 9; ++a) {
@@ -473,13 +473,19 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, i
   for (int ch = 0; ch < CT; ++ch) acc[Lay::B + 8 + ch] += g[8] * V.dep[ch];
 }
 
-constexpr int kDiagThreads = 128;
+constexpr int kDiagThreads = 64;   // two warps per image chunk
 
+// Per-image reduction of the per-observation values: each warp takes 32 observations at a
+// time (lane = observation), writes their values to shared memory (stride 33: conflict-
+// free), and each lane keeps running sums of values lane, lane+32, lane+64, ... only, so
+// the 8+C..117 values never sit in every thread's registers across observations.
 template <int CT>
 __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
                                                        float* __restrict__ diagA) {
   using Lay = DiagLayout<CT>;
-  __shared__ float red[kDiagThreads / kWarp][Lay::N];
+  constexpr int NW = kDiagThreads / kWarp;
+  constexpr int NV = (Lay::N + 31) / 32;           // values per lane
+  extern __shared__ __align__(16) float red_dyn[];   // [NW][N * 33]
   const int chunk = blockIdx.x;
   const int img = c.d.c1_img[chunk];
   const int eb = c.d.c1_chunk[chunk], ee = c.d.c1_chunk[chunk + 1];
@@ -487,21 +493,42 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
   float zc[CT];
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
-  float acc[Lay::N];
-#pragma unroll
-  for (int v = 0; v < Lay::N; ++v) acc[v] = 0.f;
-  for (int e = eb + threadIdx.x; e < ee; e += kDiagThreads) {
-    const int64_t o = c.d.c1_obs[e];
-    const int64_t k = c.d.c1_k[e];
-    ObsView<CT> V;
-    view_image<CT>(c, o, c.d.c1_pid[e], img, cam, zc, V);
-    diag_terms<CT>(c, V, k, acc);
-  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* rw = red_dyn + warp * (Lay::N * 33);
+  float run[NV];
 #pragma unroll
-  for (int v = 0; v < Lay::N; ++v) {
-    const float s = warp_sum(acc[v]);
-    if (lane == 0) red[warp][v] = s;
+  for (int j = 0; j < NV; ++j) run[j] = 0.f;
+  for (int base = eb + warp * kWarp; base < ee; base += NW * kWarp) {
+    const int e = base + lane;
+    float val[Lay::N];
+#pragma unroll
+    for (int v = 0; v < Lay::N; ++v) val[v] = 0.f;
+    if (e < ee) {
+      const int4 ix = __ldg(c.d.c1_idx + e);     // o, k, track id, local track
+      ObsView<CT> V;
+      view_image<CT>(c, ix.x, ix.z, img, cam, zc, V);
+      diag_terms<CT>(c, V, ix.y, ix.w, val);
+    }
+#pragma unroll
+    for (int v = 0; v < Lay::N; ++v) rw[v * 33 + lane] = val[v];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = lane + 32 * j;
+      if (v < Lay::N) {
+        float t = 0.f;
+#pragma unroll 8
+        for (int l = 0; l < 32; ++l) t += rw[v * 33 + l];
+        run[j] += t;
+      }
+    }
+    __syncwarp();
+  }
+  // cross-warp sum, then one atomic per destination entry
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = lane + 32 * j;
+    if (v < Lay::N) rw[v] = run[j];
   }
   __syncthreads();
   const int* dst = c.d.img_dst + 6 * img;
@@ -541,10 +568,10 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
       if (sc[blk] >= 0) addr = diagA + sc[blk] + loc;
     }
     if (addr) {
-      float s = 0.f;
+      float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < kDiagThreads / kWarp; ++w) s += red[w][v];
-      atomicAdd(addr, s);
+      for (int w = 0; w < NW; ++w) t += red_dyn[w * (Lay::N * 33) + v];
+      atomicAdd(addr, t);
     }
   }
 }
@@ -805,7 +832,7 @@ __device__ __forceinline__ void backsub_terms(const Ctx& c, int64_t k, const flo
                                               int& tl) {
   ObsView<CT> V;
   view_local<CT>(c, k, V, tl);
-  const int* sc = c.d.img_sc + 3 * c.d.img_t[k];
+  const int* sc = c.d.img_sc + 3 * __ldg(c.d.t_idx + k).x;
   double v[9];
 #pragma unroll
   for (int a = 0; a < 2; ++a) v[a] = sc[0] >= 0 ? (double)dc[sc[0] + a] : 0.0;
@@ -955,6 +982,19 @@ int launch_points(const Ctx& c, cudaStream_t s) {
 }
 
 template <int CT>
+int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
+  const size_t smem = (size_t)(kDiagThreads / kWarp) * DiagLayout<CT>::N * 33 * sizeof(float);
+  static bool configured = false;          // one attribute call per instantiation
+  if (!configured) {
+    B3R_TRY(check_cuda(cudaFuncSetAttribute(k_diag<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "diag smem attribute"));
+    configured = true;
+  }
+  k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, smem, s>>>(c, S, b, diagA);
+  return check_launch("diag pass");
+}
+
+template <int CT>
 int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
   const size_t smem = pair_smem_floats<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
@@ -978,8 +1018,7 @@ int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaSt
       return check_launch("eliminate pass");
     case B3R_PASS_DIAG:
       if (c.d.n_c1_chunks == 0) return B3R_OK;
-      k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, 0, s>>>(c, S, b, diagA);
-      return check_launch("diag pass");
+      return diag_launch<CT>(c, S, b, diagA, s);
     case B3R_PASS_PAIRS:
       if (c.d.n_tasks == 0) return B3R_OK;
       return pairs_launch<CT>(c, S, s);
@@ -993,10 +1032,7 @@ int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t
     k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
     B3R_TRY(check_launch("eliminate pass"));
   }
-  if (c.d.n_c1_chunks > 0) {
-    k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, 0, s>>>(c, S, b, diagA);
-    B3R_TRY(check_launch("diag pass"));
-  }
+  if (c.d.n_c1_chunks > 0) B3R_TRY(diag_launch<CT>(c, S, b, diagA, s));
   if (c.d.n_tasks > 0) B3R_TRY(pairs_launch<CT>(c, S, s));
   return B3R_OK;
 }

@@ -161,3 +161,24 @@ def test_schur_operator_property_full_size(cfg):
     Dg = torch.einsum('tij,tj->ti', Dinv, g_p)
     b_want = g_c - torch.zeros_like(g_c).index_add_(0, cols.reshape(-1), torch.einsum('nij,ni->nj', Hpc, Dg[pid]).reshape(-1))
     assert rel_err(s.b.cpu().numpy(), b_want.cpu().numpy()) < TOL_ACC
+
+
+@pytest.mark.parametrize('C,z0', [(1, True), (2, False), (17, True)])
+def test_schur_other_channel_counts(C, z0):
+    """Depth-channel counts of the reference's phase schedules (n_zcfs 1 -> 2 channels with
+    channel 0 frozen; 17 channels), each a separate kernel instantiation."""
+    sc = make_scene(0, n_imgs=12, n_tracks=600, seed=21 + C)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    rng = np.random.default_rng(C)
+    dep = inp['pix2d_dep']
+    if C <= dep.shape[1]:
+        dep = dep[:, :C]
+    else:
+        dep = np.concatenate([dep, rng.normal(0, 0.1, size=(len(dep), C - dep.shape[1])).astype(np.float32)], 1)
+    inp['pix2d_dep'] = np.ascontiguousarray(dep)
+    inp['z_coefs'] = np.ascontiguousarray(inp['z_coefs'][:, :1].repeat(C, 1) * (np.arange(C) == 0))
+    opts['optim_Z0'] = z0
+    want = O.linearize(inp, opts, dtype=np.float64, residual_dtype=np.float32)
+    plan, s = run_plan(inp, opts)
+    assert rel_err(s.to_dense().cpu().numpy(), want['S']) < TOL_ACC
+    assert rel_err(s.b.cpu().numpy(), want['b']) < TOL_ACC
