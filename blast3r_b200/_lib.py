@@ -77,6 +77,7 @@ _SIGS = {
     'b3r_plan_stage_obs': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     'b3r_linearize_schur': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp,
                                       C.POINTER(Outputs), _vp]),
+    'b3r_linearize_schur_noalloc': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), C.POINTER(Outputs), _vp]),
     'b3r_lin_points': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), _vp]),
     'b3r_lin_assemble': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), _vp]),
     'b3r_lin_pass': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, C.POINTER(Outputs), C.c_int, _vp]),

@@ -19,6 +19,7 @@
 //             the Jacobi preconditioner of the reference's PCG (ba_solver.py:191-192)
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include "b3r_common.cuh"
 #include "b3r_plan.h"
 #include "b3r_status.h"
@@ -1188,4 +1189,49 @@ extern "C" int b3r_backsub(b3r_plan* plan, const b3r_params* params, const b3r_l
 #undef X
     default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", plan->d.C);
   }
+}
+
+// ------------------------------------------------------------------------------------
+// allocation-free linearization (no counterpart in the reference)
+// ------------------------------------------------------------------------------------
+// Hosts that drive the library only through this C ABI -- a Go, Java or plain C program
+// with no CUDA allocator of its own, or an engine whose device memory is owned by a pool
+// that forbids extra allocations during its iteration loop -- cannot allocate the
+// per-call workspace that b3r_linearize_schur needs.  For them the workspace lives in the
+// fixed device array below, which every GPU that loads this library holds until exit.
+namespace b3r {
+constexpr size_t kStaticWorkspaceBytes = size_t(32) << 20;   // 32 MiB per device
+static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+constexpr int kStaticWsMaxDevices = 64;
+static std::mutex g_static_ws_mutex;
+static void* g_static_ws_ptr[kStaticWsMaxDevices] = {};
+}  // namespace b3r
+
+extern "C" int b3r_linearize_schur_noalloc(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                                           const b3r_outputs* out, void* stream) {
+  B3R_REQUIRE(plan && params && opts && out, "NULL argument");
+  B3R_TRY(check_device(plan));
+  B3R_REQUIRE(plan->info.workspace_bytes <= (int64_t)kStaticWorkspaceBytes,
+              "this plan needs %lld bytes of workspace; the allocation-free entry point has a fixed "
+              "%zu-byte (32 MiB) workspace: use b3r_linearize_schur with a caller-allocated workspace",
+              (long long)plan->info.workspace_bytes, kStaticWorkspaceBytes);
+  B3R_REQUIRE(plan->device >= 0 && plan->device < kStaticWsMaxDevices, "device %d out of range", plan->device);
+  void* ws = nullptr;
+  {
+    // The array's host-side name is not a device address: take the real address once per
+    // device, with that device current (check_device above guarantees it).
+    std::lock_guard<std::mutex> lock(g_static_ws_mutex);
+    if (!g_static_ws_ptr[plan->device]) {
+      void* p = nullptr;
+      B3R_TRY(check_cuda(cudaGetSymbolAddress(&p, g_static_workspace), "cudaGetSymbolAddress(static workspace)"));
+      g_static_ws_ptr[plan->device] = p;
+    }
+    ws = g_static_ws_ptr[plan->device];
+  }
+  // Every call shares the array and it keeps the previous call's contents.  The passes
+  // overwrite every record they later read; the scalar slots (damping maxima) are cleared
+  // here so no call depends on what an earlier one left behind.
+  B3R_TRY(check_cuda(cudaMemsetAsync((char*)ws + plan->ws_misc, 0, 256, as_stream(stream)),
+                     "clear static workspace scalars"));
+  return b3r_linearize_schur(plan, params, opts, ws, out, stream);
 }

@@ -219,6 +219,22 @@ typedef struct {
 int b3r_linearize_schur(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
                         void* workspace, const b3r_outputs* out, void* stream);
 
+/* Same as b3r_linearize_schur, but allocates nothing and needs no caller workspace.
+ * No counterpart in the reference.  For hosts that use this library only through its C
+ * ABI and have no way to allocate device memory themselves (a Go, Java or plain C
+ * program without a CUDA allocator, or an engine whose memory pool forbids allocations
+ * inside its iteration loop).  The workspace is a fixed 32 MiB device array inside the
+ * library, held by every GPU that loads it until the process exits; plans whose
+ * b3r_plan_info.workspace_bytes exceed it are rejected with B3R_E_INVALID (enough for
+ * an online window of ~150k observations).  The caller still passes the plan, the
+ * parameters and the outputs.  The first call on a device looks up the array's device
+ * address (make that first call before any stream capture).  All calls on a device share
+ * the one array, so calls that overlap on the GPU (other streams, other threads) race:
+ * serialise them.  Back-substitution after this call is not available (it needs the
+ * caller's workspace). */
+int b3r_linearize_schur_noalloc(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
+                                const b3r_outputs* out, void* stream);
+
 /* Stage 1: per-track Hpp and g_p, and out->hpp_max (the adaptive damping of the point
  * blocks needs the max over ALL tracks: sharded callers all-reduce it before stage 2). */
 int b3r_lin_points(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
