@@ -341,7 +341,7 @@ def run_b200(args):
 
 def read_traffic(cfg, world):
     """DRAM bytes per step from the committed ncu summary (profiles/), or None."""
-    path = os.path.join(ROOT, 'profiles', f'traffic_cfg{cfg}.txt')
+    path = os.path.join(ROOT, 'profiles', f'traffic_cfg{cfg}.txt')   # measured DRAM bytes of one step
     if world != 1 or not os.path.isfile(path):
         return None
     with open(path) as f:

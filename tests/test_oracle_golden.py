@@ -69,3 +69,32 @@ def test_jacobian_restatement_finite_differences():
         r0 = O.residuals_with_rigs(*args(P0), d['pix2d'], d['pix2d_std'], d['pix2d_dep'], True)
         fd = (r1 - r0) / (2 * eps)
         assert rel_err(Jp[:, :, j], fd) < 1e-6
+
+
+REFKERN = {p.split('golden_')[-1][:-4]: p.replace('golden_', 'refkern_') for p in CASES}
+
+
+@pytest.mark.parametrize('name', sorted(REFKERN))
+def test_oracle_matches_reference_kernels(name):
+    """The oracle's residual and Jacobian restatements against outputs of the reference's
+    own CUDA kernels captured on a B200 (tests/golden/make_golden_ref_kernels.py)."""
+    import os
+    path = REFKERN[name]
+    if not os.path.isfile(path):
+        pytest.skip('reference-kernel fixtures not captured yet')
+    inp, opts, _ = load_golden(path.replace('refkern_', 'golden_'))
+    rk = np.load(path)
+    is_log = opts['depth_mode'] == 'log'
+    a = [inp[k] for k in ('infos', 'K', 'P_rig2cam', 'P_w2rig', 'z_coefs', 'pts3d', 'pids')]
+    r = O.residuals_with_rigs(*a, inp['pix2d'], inp['pix2d_std'], inp['pix2d_dep'], is_log, opts['weight_z'],
+                              opts['pnorm'], opts['clip_pix_err'], opts['huber_delta'])
+    for j in range(3):
+        assert rel_err(r[:, j], rk['residuals9'][:, j]) < 1e-5, j
+    J = O.jacobians_with_rigs(*a, inp['pix2d_std'], inp['pix2d_dep'], is_log)
+    for tag, tol in (('f64', 1e-9), ('f32', 1e-5)):
+        for want, key in zip(J, ('J_cam', 'J_zcf', 'J_pts')):
+            got = rk[f'{key}_{tag}']
+            for rr in range(want.shape[1]):
+                for cc in range(want.shape[2]):
+                    if np.abs(want[:, rr, cc]).max() > 0:
+                        assert rel_err(got[:, rr, cc], want[:, rr, cc]) < max(tol, 2e-7 if (rr == 2 and cc < 2) else tol)
