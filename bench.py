@@ -54,16 +54,6 @@ def dist_env():
     return world, rank, local
 
 
-def shard_tracks(pids, n_tracks, world, rank):
-    """Contiguous track-id range of this rank, balanced by observation count."""
-    cnt = np.bincount(pids, minlength=n_tracks)
-    cum = np.concatenate([[0], np.cumsum(cnt)])
-    total = cum[-1]
-    bounds = [int(np.searchsorted(cum, total * r / world, side='left')) for r in range(world + 1)]
-    bounds[0], bounds[-1] = 0, n_tracks
-    return bounds[rank], bounds[rank + 1], int(cum[bounds[rank + 1]] - cum[bounds[rank]])
-
-
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
@@ -189,6 +179,7 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
     from blast3r_b200 import _lib as L
+    from blast3r_b200.distributed import ShardedSchur, shard_tracks
     from blast3r_b200.plan import BAPlan
     from blast3r_b200.synthetic import make_scene
 
@@ -209,22 +200,11 @@ def run_b200(args):
     lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
                          huber_delta=o['huber_delta'])
     ncp, nnz = plan.n_cam_params, int(plan.info.nnz)
-    red = torch.empty(nnz + 2 * ncp, dtype=torch.float32, device=dev)     # S | b | diag(A), one reduce
-    S, b, dA = red[:nnz], red[nnz:nnz + ncp], red[nnz + ncp:]
-    pc = torch.empty(ncp, dtype=torch.float32, device=dev)
-    hm = torch.empty(1, dtype=torch.float32, device=dev)
-    outs = (S, b, dA, pc, hm)
+    sharded = ShardedSchur(plan)
+    S, b, dA, pc, hm = outs = sharded.outputs
 
     def step():
-        if world == 1:
-            plan.linearize(p, lo, outs)
-            return
-        plan.lin_stage('points', p, lo, outs)
-        dist.all_reduce(hm, op=dist.ReduceOp.MAX)
-        plan.lin_stage('assemble', p, lo, outs)
-        dist.reduce(red, dst=0)
-        if rank == 0:
-            plan.lin_stage('finalize', p, lo, outs)
+        sharded.linearize(p, lo)
 
     for _ in range(args.warmup):
         step()

@@ -344,7 +344,7 @@ def s_pattern(layout):
 
 def schur_system(J_cam, J_zcf, J_pts, residuals, w_pts, layout, clamp_w=(1e-6, 1e6),
                  dampen=1e-12, adaptive_dampen=True, no_grad_f_from_rz=False,
-                 optim_Z_1st_cam=True, optim_Z0=True, dense=True, dtype=np.float64):
+                 optim_Z_1st_cam=True, optim_Z0=True, dense=True, dtype=np.float64, obs_mask=None):
     """The reduced system of ``GaussNewtonSolver.solve_delta`` before its PCG.
 
     Follows ``ba_solver.py:123-188``: W = clamp(w), g = J^T (W r), J *= sqrt(W), the Gram
@@ -355,7 +355,8 @@ def schur_system(J_cam, J_zcf, J_pts, residuals, w_pts, layout, clamp_w=(1e-6, 1
 
     Returns a dict with S (dense, reduced camera-side size) or S blocks, b, g, diagA (the
     damped diagonal of A, i.e. the reference's PCG preconditioner before its clamp),
-    and per-track quantities for back-substitution.
+    and per-track quantities for back-substitution.  ``obs_mask`` (bool per observation)
+    keeps only those observations' contributions: the partial system of one shard.
     """
     dt = dtype
     n = J_cam.shape[0]
@@ -368,6 +369,8 @@ def schur_system(J_cam, J_zcf, J_pts, residuals, w_pts, layout, clamp_w=(1e-6, 1
     W32 = np.clip(np.asarray(w_pts, np.float32), np.float32(clamp_w[0]), np.float32(clamp_w[1]))
     if W32.shape[1] == 1:
         W32 = np.repeat(W32, 3, axis=1)
+    if obs_mask is not None:
+        W32 = np.where(np.asarray(obs_mask, bool)[:, None], W32, np.float32(0))
     Wr = (W32 * np.asarray(residuals, np.float32)).astype(dt)        # ba_solver.py:128
     sW = np.sqrt(W32).astype(dt)                                      # ba_solver.py:132
     Jcw = Jc * sW[:, :, None]
@@ -509,7 +512,7 @@ def dense_to_blocks(S, layout, pattern):
 # one full linearization from raw inputs
 # --------------------------------------------------------------------------------------
 
-def linearize(scene_inputs, options, dtype=np.float64, dense=True, residual_dtype=None):
+def linearize(scene_inputs, options, dtype=np.float64, dense=True, residual_dtype=None, obs_mask=None):
     """Residual -> Jacobians -> Schur system for one LM iteration, from raw inputs.
 
     ``scene_inputs``: dict with infos, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam,
@@ -535,7 +538,7 @@ def linearize(scene_inputs, options, dtype=np.float64, dense=True, residual_dtyp
     sys_ = schur_system(J_cam, J_zcf, J_pts, res[:, :3].astype(np.float32), res[:, 6:9].astype(np.float32),
                         lay, no_grad_f_from_rz=o['no_grad_f_from_rz'],
                         optim_Z_1st_cam=o['optim_Z_1st_cam'], optim_Z0=o['optim_Z0'],
-                        dense=dense, dtype=dtype)
+                        dense=dense, dtype=dtype, obs_mask=obs_mask)
     sys_.update(residuals=res, J_cam=J_cam, J_zcf=J_zcf, J_pts=J_pts, layout=lay)
     return sys_
 

@@ -1,0 +1,73 @@
+"""Track-sharded linearization on 2 GPUs (NCCL) against the single-GPU result.
+
+Skipped when fewer than two GPUs are visible.  Two spawned ranks build their plans on their
+own track ranges, run ``ShardedSchur.linearize`` (all-reduce MAX of the point damping, NCCL
+reduce of S | b | diag(A), finalize on rank 0); rank 0 compares with the one-GPU plan.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, cfg, result_path):
+    from blast3r_b200.distributed import ShardedSchur, shard_tracks
+    from blast3r_b200.plan import BAPlan
+    from blast3r_b200.synthetic import make_scene
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
+    torch.cuda.set_device(rank)
+    dev = torch.device('cuda', rank)
+    dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        sc = make_scene(cfg, n_imgs=60 if cfg == 1 else None, n_tracks=6000 if cfg == 1 else None)
+        o = sc.options
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
+        lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
+                             huber_delta=o['huber_delta'])
+
+        def run(track_range):
+            plan = BAPlan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
+                          optim_P=o['optim_P'], track_range=track_range, device=dev)
+            p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                            t['pix2d_dep'], pix2d=t['pix2d'])
+            return plan, p
+
+        t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+        plan, p = run((t0, t1))
+        sh = ShardedSchur(plan).linearize(p, lo)
+        torch.cuda.synchronize()
+        if rank == 0:
+            full_plan, fp = run(None)
+            ref = full_plan.linearize(fp, lo)
+            torch.cuda.synchronize()
+
+            def rel(a, b):
+                a, b = a.double().cpu().numpy(), b.double().cpu().numpy()
+                return float(np.abs(a - b).max() / np.abs(b).max())
+            np.save(result_path, np.array([rel(sh.S, ref.S_vals), rel(sh.b, ref.b), rel(sh.precond, ref.precond)]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('cfg', [0, 1])
+def test_two_gpu_sharded_schur_equals_single_gpu(cfg, tmp_path):
+    out = str(tmp_path / 'errs.npy')
+    mp.spawn(_rank_main, args=(2, _free_port(), cfg, out), nprocs=2, join=True)
+    errs = np.load(out)
+    assert (errs < 1e-4).all(), errs
