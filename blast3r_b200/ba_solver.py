@@ -91,7 +91,7 @@ class GaussNewtonSolver:
         assert rigs.shape == (3, self.imgs.n)
         C = pix2d_dep.shape[1]
         self.n_kpts, self.n_zcf = len(pids), C
-        plan = get_plan(rigs, pids, self.cams.n, self.nodes.n, self.imgs.n, self.tracks.n, C, optim_K, optim_P,
+        plan = get_plan(rigs, pids, self.cams.n, self.nodes.n, self.tracks.n, C, optim_K, optim_P,
                         optim_Z, optim_X, device=self.device)
         # column counts after enabling (ba_solver.py:72-108)
         for prm, status in ((self.cams, optim_K), (self.nodes, optim_P), (self.imgs, optim_Z),

@@ -1,0 +1,122 @@
+"""Levenberg-Marquardt driver on the B200 solver: the reference's ``lm_step`` and
+``bundle_adjustment`` (inference/engine.py:206-334, 405-503) with the same arguments,
+update rules, line search and return values, running ``blast3r_b200.ba_solver`` and the
+library's residual op.
+
+Differences: the dense tangent prior (``weight_tan > 0``, ``tangent_reg > 0``) is not
+supported (it is off by default in the reference); with ``recompute_residuals`` (default)
+the linearization recomputes residuals and weights in-kernel instead of reading the
+objective's tensors (same device function, same values).
+"""
+from collections import namedtuple
+
+import torch
+
+from .ba_solver import GaussNewtonSolver
+from .cujac import exp_se3, residuals_with_rigs as residual_func
+
+BA_Status = namedtuple('BA_Status', 'init_loss, init_residuals, new_loss, new_residuals')
+
+
+def shape_of(tensor, is_contiguous=True):
+    """Input checks of the reference (engine.py:340-344)."""
+    assert tensor.dtype in (torch.float32, torch.int32)
+    if is_contiguous:
+        assert tensor.is_contiguous()
+    assert tensor.isfinite().all()
+    return tensor.shape
+
+
+def update_K(K0, delta_focal, min_f=100):
+    """Focal update with the reference's clipping (engine.py:347-354)."""
+    dfx, dfy = delta_focal.T
+    K = K0.clone()
+    K[:, 0, 0] -= dfx
+    K[:, 1, 1] -= dfy
+    K[:, 0, 0].clip_(min=min_f)
+    K[:, 1, 1].clip_(min=min_f)
+    return K
+
+
+def reproj_score(res):
+    """Mean of the best 80% reprojection errors (engine.py:357-361)."""
+    reproj_err = res[:, :2].norm(dim=-1)
+    reproj_err = reproj_err.sort().values
+    n80 = len(reproj_err) * 80 // 100
+    return reproj_err[:n80].mean()
+
+
+def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_coefs, pts3d, depth_mode='log',
+            pnorm=1, clip_pix_err=100, huber_delta=0.5, min_reproj=0.01, dampen=1e-12, min_loss_delta=1e-4,
+            weight_z=1, log_depth_maps=None, conf=None, pts3d_ref=None, weight_tan=0.0, tan_stride=4,
+            normalize_tangents=True, optim_K=True, optim_Z=True, optim_P=True, optim_X=True, optim_Z0=True,
+            recompute_residuals=True, verbose=False, **ba_options):
+    """One Levenberg-Marquardt step (engine.py:206-334): residuals, linearization + Schur
+    solve, back-substitution, then the line search over step scales 1, 1/2, 1/4, 1/8,
+    1/64, 1/512, 1/4096, 0 with the degenerate-geometry reject."""
+    assert depth_mode in ('lin', 'log')
+    if weight_tan > 0:
+        raise NotImplementedError('the dense tangent prior is not supported by the B200 solver')
+    is_depth_log = depth_mode == 'log'
+    n_imgs = rigs.shape[1]
+    assert shape_of(rigs) == (3, n_imgs)
+    n_cams = len(K)
+    assert shape_of(K) == (n_cams, 3, 3)
+    assert shape_of(P_rig2cam, is_contiguous=False) == (n_cams, 4, 4)
+    n_nodes = len(P_w2rig)
+    assert shape_of(P_w2rig) == (n_nodes, 4, 4)
+    n_zcf = z_coefs.shape[1]
+    assert shape_of(z_coefs) == (n_imgs, n_zcf)
+    n_tracks = len(pts3d)
+    assert shape_of(pts3d) == (n_tracks, 3)
+    n_obs = len(pids)
+    assert shape_of(pids) == (n_obs,)
+    assert shape_of(pix2d) == (n_obs, 2)
+    assert shape_of(pix2d_std) == (n_obs, 2)
+    assert shape_of(pix2d_dep) == (n_obs, n_zcf)
+    assert 0 <= weight_z <= 10
+    assert n_obs >= n_tracks, 'there must be more 2d kpts than tracks'
+    assert huber_delta >= 0.1
+
+    def objective(K, P_w2rig, pts3d, z_coefs):
+        residuals_, err_pts_, w_pts_ = residual_func(
+            rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep, is_depth_log,
+            weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
+        return err_pts_.mean(), residuals_, w_pts_
+
+    init_loss, init_residuals, w_pts = objective(K, P_w2rig, pts3d, z_coefs)
+    jac = GaussNewtonSolver(n_cams, n_nodes, n_imgs, n_tracks, pts3d.device, dampen=dampen, **ba_options)
+    J = jac.compute_jacobians(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d_std, pix2d_dep,
+                              optim_K=optim_K, optim_Z=optim_Z, optim_Z0=optim_Z0, optim_P=optim_P,
+                              optim_X=optim_X, is_depth_log=is_depth_log,
+                              pix2d=pix2d if recompute_residuals else None)
+    lin_kw = dict(weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err, huber_delta=huber_delta)
+    delta = jac.solve_delta(J, init_residuals, w_pts, lin_kw=lin_kw)
+    delta_K, delta_P, delta_zcf, delta_pts = jac.unpack_delta_inplace(delta)
+
+    update = dict()
+    last_a = 1
+    new_loss, new_residuals = init_loss, init_residuals
+    for a in [0.5, 0.25, 0.125, 1 / 64, 1 / 512, 1 / 4096, 0]:
+        update['K'] = update_K(K, delta_K)
+        update['P_w2rig'] = (exp_se3(-delta_P) @ P_w2rig).contiguous()
+        update['z_coefs'] = (z_coefs - delta_zcf).contiguous()
+        update['pts3d'] = (pts3d - delta_pts).contiguous()
+        new_loss, new_residuals, _ = objective(**update)
+        if new_loss.isnan():
+            if verbose:
+                print('Warning: loss is NaN')
+            new_loss = init_loss
+        new_loss = new_loss + min_loss_delta
+        new_reproj = float(reproj_score(new_residuals))
+        degenerate = new_reproj < min_reproj
+        if degenerate and verbose:
+            print(f'Rejecting step: reprojection residual collapsed to {new_reproj:.2e}')
+        if new_loss < init_loss and not degenerate:
+            break
+        delta *= a / last_a          # scales (delta_K, ..., delta_pts): they are views of delta
+        last_a = a
+    else:
+        if verbose:
+            print('Warning: loss is not decreasing')
+    return update, BA_Status(init_loss, init_residuals, new_loss, new_residuals)

@@ -120,6 +120,25 @@ def run_reference(ba_solver, engine, d, opts, dtype):
                 n_cam_params=np.int64(cap['S'].shape[0]))
 
 
+def run_reference_lm_step(engine, d, opts, dtype=torch.float64, prefix='lm'):
+    """One reference lm_step (engine.py:206-334), production float64 solver by default."""
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in d.items()}
+
+    def as_opt(v):
+        return torch.from_numpy(v) if isinstance(v, np.ndarray) else v
+    update, st = engine.lm_step(t['rigs'], t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], t['K'],
+                                t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], depth_mode=opts['depth_mode'],
+                                pnorm=opts['pnorm'], clip_pix_err=opts['clip_pix_err'],
+                                huber_delta=opts['huber_delta'], weight_z=opts['weight_z'],
+                                optim_K=as_opt(opts['optim_K']), optim_Z=as_opt(opts['optim_Z']),
+                                optim_P=as_opt(opts['optim_P']), optim_X=as_opt(opts['optim_X']),
+                                optim_Z0=opts['optim_Z0'], no_grad_f_from_rz=opts['no_grad_f_from_rz'],
+                                dampen=1e-12, adaptive_dampen=True, dtype=dtype)
+    return {f'{prefix}_K': update['K'].numpy(), f'{prefix}_P_w2rig': update['P_w2rig'].numpy(),
+            f'{prefix}_z_coefs': update['z_coefs'].numpy(), f'{prefix}_pts3d': update['pts3d'].numpy(),
+            f'{prefix}_init_loss': np.float64(st.init_loss), f'{prefix}_new_loss': np.float64(st.new_loss)}
+
+
 def main():
     ref = os.environ.get('B3R_REFERENCE')
     if not ref:
@@ -133,6 +152,9 @@ def main():
             r = run_reference(ba_solver, engine, d, opts, dt)
             for k, v in r.items():
                 out[f'{tag}_{k}'] = v
+        if opts['optim_Z_1st_cam']:          # lm_step has no optim_Z_1st_cam argument
+            out.update(run_reference_lm_step(engine, d, opts))
+            out.update(run_reference_lm_step(engine, d, opts, torch.float32, 'lm32'))
         meta = {k: (np.asarray(v) if not isinstance(v, str) else np.array(v)) for k, v in opts.items()}
         np.savez_compressed(os.path.join(HERE, f'golden_{name}.npz'),
                             **{f'in_{k}': v for k, v in d.items()},

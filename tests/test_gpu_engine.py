@@ -1,0 +1,49 @@
+"""One full Levenberg-Marquardt iteration (``blast3r_b200.engine.lm_step``: residuals,
+fused linearization, PCG on S, back-substitution, line search) against the reference's
+own ``lm_step`` recorded in the golden fixtures (production float64 solver).
+
+The fp32 linearization cannot be closer to the fp64 reference than conditioning allows:
+the bound for each quantity is 2e-3, or 1.5x the distance between the reference's own
+float32 and float64 solvers on the same case when that is larger (weakly constrained
+depth coefficients at omega = 1e-4; focal/depth coupling with per-frame focals)."""
+import numpy as np
+import pytest
+import torch
+
+from blast3r_b200.engine import lm_step
+from tests.helpers import golden_files, load_golden, rel_err, to_cuda
+
+pytestmark = pytest.mark.gpu
+
+CASES = [p for p in golden_files() if 'lm_K' in np.load(p).files]
+
+
+@pytest.mark.parametrize('recompute', [True, False])
+@pytest.mark.parametrize('path', CASES, ids=lambda p: p.split('golden_')[-1][:-4])
+def test_lm_step_matches_reference(path, recompute):
+    inp, opts, _ = load_golden(path)
+    z = np.load(path)
+    t = to_cuda(inp)
+
+    def as_opt(v):
+        return torch.from_numpy(v).cuda() if isinstance(v, np.ndarray) else v
+    update, st = lm_step(t['infos'], t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], t['K'], t['P_rig2cam'],
+                         t['P_w2rig'], t['z_coefs'], t['pts3d'], depth_mode=opts['depth_mode'], pnorm=opts['pnorm'],
+                         clip_pix_err=opts['clip_pix_err'], huber_delta=opts['huber_delta'],
+                         weight_z=opts['weight_z'], optim_K=as_opt(opts['optim_K']), optim_Z=as_opt(opts['optim_Z']),
+                         optim_P=as_opt(opts['optim_P']), optim_X=as_opt(opts['optim_X']), optim_Z0=opts['optim_Z0'],
+                         no_grad_f_from_rz=opts['no_grad_f_from_rz'], dtype=torch.float64,
+                         recompute_residuals=recompute)
+    assert abs(float(st.init_loss) - float(z['lm_init_loss'])) <= 1e-5 * abs(float(z['lm_init_loss']))
+    loss_gap32 = abs(float(z['lm32_new_loss']) - float(z['lm_new_loss']))
+    assert abs(float(st.new_loss) - float(z['lm_new_loss'])) <= max(1e-3 * abs(float(z['lm_init_loss'])),
+                                                                    1.5 * loss_gap32)
+    for key in ('pts3d', 'z_coefs', 'K', 'P_w2rig'):
+        x0 = inp[key].astype(np.float64)
+        step_ref = z['lm_' + key].astype(np.float64) - x0
+        step = update[key].double().cpu().numpy() - x0
+        if np.abs(step_ref).max() == 0:
+            assert np.abs(step).max() == 0, key
+            continue
+        bound = max(2e-3, 1.5 * rel_err(z['lm32_' + key].astype(np.float64) - x0, step_ref))
+        assert rel_err(step, step_ref) < bound, (key, rel_err(step, step_ref), bound)

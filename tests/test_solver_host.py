@@ -1,0 +1,49 @@
+"""Host-side logic of the GaussNewtonSolver mirror, without a GPU: planning through
+compute_jacobians (host-only plan on CPU tensors), plan caching, column counts after
+enabling, and unpack_delta_inplace (ba_solver.py:72-108, 228-248)."""
+import numpy as np
+import torch
+
+from blast3r_b200 import ba_solver as BS
+from blast3r_b200.synthetic import make_scene
+
+
+def _t(sc):
+    return {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in sc.lm_inputs().items()}
+
+
+def test_compute_jacobians_plans_and_caches():
+    sc = make_scene(0, n_imgs=8, n_tracks=100)
+    t = _t(sc)
+    BS._PLAN_CACHE.clear()
+    s = BS.GaussNewtonSolver(sc.n_cams, sc.n_nodes, sc.n_imgs, sc.n_tracks, 'cpu')
+    J = s.compute_jacobians(t['rigs'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pids'],
+                            t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    assert J.plan.n_cam_params == 2 + 6 * 8 + 5 * 8
+    assert J.shape == (3 * sc.n_obs, J.plan.n_cam_params + 3 * sc.n_tracks)
+    s2 = BS.GaussNewtonSolver(sc.n_cams, sc.n_nodes, sc.n_imgs, sc.n_tracks, 'cpu')
+    J2 = s2.compute_jacobians(t['rigs'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'],
+                              t['pids'].clone(), t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    assert J2.plan is J.plan                 # same structure (contents, not address) -> same plan
+    sc3 = make_scene(0, n_imgs=8, n_tracks=100, seed=5)
+    t3 = _t(sc3)
+    J3 = s2.compute_jacobians(t3['rigs'], t3['K'], t3['P_rig2cam'], t3['P_w2rig'], t3['z_coefs'], t3['pts3d'],
+                              t3['pids'], t3['pix2d_std'], t3['pix2d_dep'], is_depth_log=True)
+    assert J3.plan is not J.plan
+
+
+def test_masks_and_unpack_delta():
+    sc = make_scene(3, n_imgs=8, n_tracks=150)
+    t = _t(sc)
+    mP = torch.ones(sc.n_nodes, dtype=torch.bool)
+    mP[[0, 3]] = False
+    s = BS.GaussNewtonSolver(sc.n_cams, sc.n_nodes, sc.n_imgs, sc.n_tracks, 'cpu')
+    J = s.compute_jacobians(t['rigs'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pids'],
+                            t['pix2d_std'], t['pix2d_dep'], is_depth_log=True, optim_P=mP, optim_X=False)
+    assert s.nodes.n == 6 and list(s.nodes.true_idxs) == [1, 2, 4, 5, 6, 7]
+    n = 2 * 8 + 6 * 6 + 5 * 8 + 3 * sc.n_tracks
+    assert J.plan.n_cam_params + 3 * J.plan.info.n_points == n
+    delta = torch.arange(n, dtype=torch.float32)
+    dK, dP, dZ, dX = s.unpack_delta_inplace(delta)
+    assert dK.shape == (8, 2) and dP.shape == (8, 6) and dZ.shape == (8, 5) and dX.shape == (sc.n_tracks, 3)
+    assert (dP[0] == 0).all() and (dP[3] == 0).all() and dP[1, 0] == 16
