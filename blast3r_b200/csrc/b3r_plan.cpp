@@ -73,7 +73,7 @@ struct PlanBuild {
   std::vector<int> seg_row_ptr, seg_col;   // CSR over row image
   std::vector<int64_t> seg_cnt;
   std::vector<int2> pairs;
-  std::vector<int64_t> task_pb;
+  std::vector<int64_t> task_pb, task_pe;
   std::vector<int> task_seg;
   // pattern
   std::vector<int> row_ptr, col_idx, val_off;
@@ -318,12 +318,24 @@ static int build_pairs(PlanBuild& B) {
     std::vector<int64_t> fill(B.seg_cnt.begin(), B.seg_cnt.end() - 1);
     for_pairs([&](int64_t s, int ka, int kb) { B.pairs[fill[s]++] = make_int2(ka, kb); });
   }
+  // Tasks: segments cut into <= kPairTask pairs, issued longest first so the short ones
+  // fill in behind them (the pair lists stay in segment order; a task is a (segment, range)).
+  std::vector<std::pair<int64_t, int64_t>> cuts;   // (first pair, segment)
   for (int64_t s = 0; s < S; ++s)
-    for (int64_t p = B.seg_cnt[s]; p < B.seg_cnt[s + 1]; p += kPairTask) {
-      B.task_pb.push_back(p);
-      B.task_seg.push_back((int)s);
-    }
-  B.task_pb.push_back(P);
+    for (int64_t p = B.seg_cnt[s]; p < B.seg_cnt[s + 1]; p += kPairTask) cuts.emplace_back(p, s);
+  std::vector<int64_t> ord(cuts.size());
+  std::iota(ord.begin(), ord.end(), 0);
+  auto len = [&](int64_t t) { return std::min<int64_t>(B.seg_cnt[cuts[t].second + 1] - cuts[t].first, kPairTask); };
+  std::stable_sort(ord.begin(), ord.end(), [&](int64_t a, int64_t b) { return len(a) > len(b); });
+  B.task_pb.resize(cuts.size() + 1);
+  B.task_pe.resize(cuts.size());
+  B.task_seg.resize(cuts.size());
+  for (size_t t = 0; t < ord.size(); ++t) {
+    B.task_pb[t] = cuts[ord[t]].first;
+    B.task_pe[t] = cuts[ord[t]].first + len(ord[t]);
+    B.task_seg[t] = (int)cuts[ord[t]].second;
+  }
+  B.task_pb[cuts.size()] = P;
   return B3R_OK;
 }
 
@@ -510,7 +522,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.c1_obs, &d.c1_obs); A.add(B.c1_k, &d.c1_k); A.add(B.c1_pid, &d.c1_pid); A.add(B.c1_chunk, &d.c1_chunk);
   A.add(B.c1_img, &d.c1_img);
   A.add(B.seg_dst, &d.seg_dst); A.add(B.seg_mode, &d.seg_mode);
-  A.add(B.pairs, &d.pairs); A.add(B.task_pb, &d.task_pb); A.add(B.task_seg, &d.task_seg);
+  A.add(B.pairs, &d.pairs); A.add(B.task_pb, &d.task_pb); A.add(B.task_pe, &d.task_pe);
+  A.add(B.task_seg, &d.task_seg);
   A.add(B.row_ptr, &d.row_ptr); A.add(B.col_idx, &d.col_idx); A.add(B.val_off, &d.val_off);
   A.add(B.bsize, &d.bsize); A.add(B.boff, &d.boff); A.add(B.sdiag_pos, &d.sdiag_pos);
   A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);

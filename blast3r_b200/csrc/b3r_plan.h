@@ -66,7 +66,8 @@ struct DevPlan {
   const int* seg_dst;     // [n_seg*9] value offset of each (a,b) sub-block, -1 none
   const int* seg_mode;    // [n_seg] 2 bits per sub-block (a*3+b)
   const int2* pairs;      // [n_pairs] (k_row, k_col)
-  const int64_t* task_pb; // [n_tasks+1]
+  const int64_t* task_pb; // [n_tasks] first pair of each task (tasks longest first)
+  const int64_t* task_pe; // [n_tasks] end of each task
   const int* task_seg;    // [n_tasks]
 
   // S pattern

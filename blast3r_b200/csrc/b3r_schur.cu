@@ -230,10 +230,15 @@ __device__ __forceinline__ void point_terms(const ObsView<CT>& V, float v[9]) {
   }
 }
 
+// Elimination record of one observation, Y = L^-1 Hpc (3 x 9 reduced camera columns)
+// and its depth channels: [0, 24) Y[r][a] at 8 r + a for the columns a < 8 (row-major, so
+// that neighbouring columns pair up for packed float2 arithmetic), [24, 24+C) the depth
+// channels, [24+C, 27+C) the z-scale column Y[r][8], padded to a multiple of 4 floats.
 template <int CT>
 __host__ __device__ constexpr int rec_floats() { return (27 + CT + 3) & ~3; }
+template <int CT>
+__host__ __device__ constexpr int rec_zs() { return 24 + CT; }
 
-// Elimination record of one observation: Y = L^-1 Hpc (column-major 3x9) + depth channels.
 template <int CT>
 __device__ __forceinline__ void write_record(const Ctx& c, int64_t k, const ObsView<CT>& V, const float l[6]) {
   constexpr int R = rec_floats<CT>();
@@ -250,10 +255,11 @@ __device__ __forceinline__ void write_record(const Ctx& c, int64_t k, const ObsV
     }
     float y[3];
     chol3_fwd<float>(l, h, y);
-    rv[3 * a] = y[0]; rv[3 * a + 1] = y[1]; rv[3 * a + 2] = y[2];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) rv[a < 8 ? 8 * r + a : rec_zs<CT>() + r] = y[r];
   }
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) rv[27 + ch] = V.dep[ch];
+  for (int ch = 0; ch < CT; ++ch) rv[24 + ch] = V.dep[ch];
 #pragma unroll
   for (int e = 27 + CT; e < R; ++e) rv[e] = 0.f;
   float4* dst = reinterpret_cast<float4*>(c.rec + k * R);
@@ -429,20 +435,25 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, i
   if (k >= 0) {                                   // eliminated track: subtract Y^T Y, Y^T z
     constexpr int R = rec_floats<CT>();
     const float4* r4 = reinterpret_cast<const float4*>(c.rec + k * R);
-    float Y[28];
+    float Yf[R];
 #pragma unroll
-    for (int q = 0; q < 7; ++q) {
+    for (int q = 0; q < R / 4; ++q) {
       const float4 v = __ldg(r4 + q);
-      Y[4 * q] = v.x; Y[4 * q + 1] = v.y; Y[4 * q + 2] = v.z; Y[4 * q + 3] = v.w;
+      Yf[4 * q] = v.x; Yf[4 * q + 1] = v.y; Yf[4 * q + 2] = v.z; Yf[4 * q + 3] = v.w;
     }
+    float Y[9][3];   // Y[a][r] = Y[r][a] of the record
+#pragma unroll
+    for (int a = 0; a < 9; ++a)
+#pragma unroll
+      for (int r = 0; r < 3; ++r) Y[a][r] = Yf[a < 8 ? 8 * r + a : rec_zs<CT>() + r];
     const float* tz = c.trec + (int64_t)tl * 24 + 18;
     const float z0 = tz[0], z1 = tz[1], z2 = tz[2];
 #pragma unroll
     for (int a = 0; a < 9; ++a) {
 #pragma unroll
       for (int b = a; b < 9; ++b)
-        H[a][b] -= Y[3 * a] * Y[3 * b] + Y[3 * a + 1] * Y[3 * b + 1] + Y[3 * a + 2] * Y[3 * b + 2];
-      g[a] -= Y[3 * a] * z0 + Y[3 * a + 1] * z1 + Y[3 * a + 2] * z2;
+        H[a][b] -= Y[a][0] * Y[b][0] + Y[a][1] * Y[b][1] + Y[a][2] * Y[b][2];
+      g[a] -= Y[a][0] * z0 + Y[a][1] * z1 + Y[a][2] * z2;
     }
   }
   acc[Lay::FF + 0] += H[0][0];
@@ -582,10 +593,17 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
 // ------------------------------------------------------------------------------------
 // A segment (i, i') owns the S blocks between image i's typed blocks (rows) and image
 // i''s (columns).  For each of its observation pairs (o in i, o' in i', same track) the
-// product P = Y_o^T Y_o' (13x13 for C = 5 once the depth columns are expanded) is summed
-// in registers.  The 8+C output rows are split among NROLE warps (roles) so that no
-// thread holds more than 5 rows of accumulators; every role streams the same pairs.
-constexpr int kPairBatch = 32;
+// product P = Y_o^T Y_o' ((8+C) x (8+C) once the depth columns are expanded) is summed.
+// One warp per pair task, one observation pair per lane per step.  The warp copies the
+// 64 records of a step (32 pairs x 2 sides) into shared memory with coalesced 16-byte
+// cp.async (eight lanes per 128-byte record), kPairStages - 1 steps ahead of the step it
+// computes; each lane then reads its own pair's records from a padded slot (conflict-free
+// 16-byte reads).  Each lane keeps the rows [A0, A1) of the product in registers (all 8+C
+// rows for C <= 5; larger C splits the rows over `pair_roles` warps that each stream the
+// task); the lane partials are summed through shared memory at the end of the task, one
+// atomic per value.
+constexpr int kPairWarps = 1;    // independent warps (tasks) per CTA: one, so a finished task frees its slot
+constexpr int kPairStages = 3;   // cp.async ring depth per lane
 
 // 16-byte asynchronous global -> shared copies (cp.async, completion by commit groups)
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -595,28 +613,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
-// Pair indices of the batch starting at `base`: lane l holds pair base + l (or (-1,-1)).
-__device__ __forceinline__ int2 load_batch_pairs(const Ctx& c, int64_t base, int64_t pe) {
-  const int64_t p = base + (threadIdx.x & 31);
-  return p < pe ? __ldg(reinterpret_cast<const int2*>(c.d.pairs) + p) : make_int2(-1, -1);
-}
-
-// Stage the two records of up to 32 pairs into `buf` ([2 sides][32 pairs][RS floats]).
-// `kk` is this warp's copy of the batch's pair indices (load_batch_pairs); every warp of
-// the CTA holds the same 32 indices, so the item loop needs no dependent global load.
-template <int CT>
-__device__ __forceinline__ void stage_batch(const Ctx& c, int2 kk, float* buf) {
-  constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
-  for (int q = threadIdx.x; q < 2 * kPairBatch * Q; q += blockDim.x) {
-    const int ri = q / Q, part = q - ri * Q;
-    const int pair = ri >> 1, side = ri & 1;
-    const int kx = __shfl_sync(0xffffffffu, kk.x, pair);
-    const int ky = __shfl_sync(0xffffffffu, kk.y, pair);
-    const int k = side ? ky : kx;
-    if (k >= 0) cp_async16(buf + (side * kPairBatch + pair) * RS + 4 * part, c.rec + (int64_t)k * R + 4 * part);
-  }
-}
 
 // Add -v to S at output (row a, column bcol) of segment s's pair product.
 template <int CT>
@@ -638,120 +634,187 @@ __device__ __forceinline__ void emit_pair_value(const Ctx& c, float* __restrict_
   }
 }
 
-template <int CT> __host__ __device__ constexpr int pair_roles() { return (8 + CT + 4) / 5; }
+// Warps that split the 8+C product rows: a lane holds at most ~170 accumulators.
+template <int CT> __host__ __device__ constexpr int pair_roles() {
+  return CT <= 5 ? 1 : (CT <= 8 ? 2 : ((8 + CT) * (8 + CT) + 119) / 120);
+}
 template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() { return r * (8 + CT) / NR; }
-template <int CT> __host__ __device__ constexpr int pair_max_acc() {
-  return (role_row<CT, pair_roles<CT>(), 1>() - role_row<CT, pair_roles<CT>(), 0>() + 1) * (8 + CT);
+template <int CT> __host__ __device__ constexpr int pair_slot_floats() { return 2 * rec_floats<CT>() + 4; }
+template <int CT> __host__ __device__ constexpr int pair_max_rows() {
+  return (8 + CT + pair_roles<CT>() - 1) / pair_roles<CT>();
 }
-template <int CT> __host__ __device__ constexpr int pair_stage_floats() {
-  return 2 * 2 * kPairBatch * (rec_floats<CT>() + 4);
-}
-template <int CT> __host__ __device__ constexpr int pair_red_floats() {
-  return pair_roles<CT>() * pair_max_acc<CT>() * 33;
-}
-template <int CT> __host__ __device__ constexpr int pair_smem_floats() {
-  return pair_stage_floats<CT>() > pair_red_floats<CT>() ? pair_stage_floats<CT>() : pair_red_floats<CT>();
+// per warp: kPairStages step buffers (reused by the epilogue), then 64 staged record
+// indices; a multiple of 4 floats so every warp's region starts 16-byte aligned
+template <int CT> __host__ __device__ constexpr int pair_warp_floats() {
+  return (((kPairStages * 32 * pair_slot_floats<CT>() > pair_max_rows<CT>() * (8 + CT) * 33
+                ? kPairStages * 32 * pair_slot_floats<CT>()
+                : pair_max_rows<CT>() * (8 + CT) * 33) + 3) & ~3) + 64;
 }
 
-// One role (output rows [A0, A1)) of a pair task.  Every warp of the CTA takes part in
-// the staging; each lane accumulates the products of pair `lane` of every batch.
+// Rows [A0, A1) of one pair task, run by one warp over its private shared region `sm`.
+// The products are accumulated with packed float2 FMAs (two neighbouring columns per
+// instruction): row a < 8 of Y_o^T Y_o' is sum_r Y_o[r][a] * Y_o'[r][0..7] plus the depth
+// columns u_a * dep', u_a = sum_r Y_o[r][a] zs'[r]; a depth row is dep[ch] * (zs^T Y_o')
+// plus dep[ch] * (zs^T zs') * dep'.
 template <int CT, int A0, int A1>
-__device__ __forceinline__ void pair_role(const Ctx& c, float* __restrict__ S, int s, int64_t pb, int64_t pe,
-                                          float* sm) {
-  constexpr int R = rec_floats<CT>(), RS = R + 4, Q = R / 4;
+__device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, int64_t task, float* sm) {
+  constexpr int R = rec_floats<CT>(), SLOT = pair_slot_floats<CT>(), Q = R / 4, ZS = rec_zs<CT>();
   constexpr int W = 8 + CT, NA = A1 - A0;
-  constexpr int LO = A0 < 8 ? 3 * A0 : 24;
-  constexpr int HI = A1 > 8 ? 27 + (A1 - 8) : 3 * A1;
-  constexpr int QLO = LO / 4, QHI = (HI + 3) / 4;
-  constexpr bool HAS_Z = A1 > 8;
-  constexpr int BUF = 2 * kPairBatch * RS;
+  constexpr int NZ2 = CT / 2, ODD = CT & 1, NC2 = 4 + NZ2;   // float2 columns per row
+  constexpr int B0 = A0 < 8 ? A0 : 8, B1 = A1 < 8 ? A1 : 8;  // base rows of this role
+  constexpr int Z0 = A0 > 8 ? A0 - 8 : 0, Z1 = A1 > 8 ? A1 - 8 : 0;   // depth rows
+  constexpr int STAGE = 32 * SLOT;
   const int lane = threadIdx.x & 31;
-  float acc[NA * W];
+  const int s = c.d.task_seg[task];
+  const int64_t pb = c.d.task_pb[task], pe = c.d.task_pe[task];
+  const int nit = (int)((pe - pb + 31) >> 5);
+  const int2* __restrict__ pairs = reinterpret_cast<const int2*>(c.d.pairs);
+  int* sidx = reinterpret_cast<int*>(sm + pair_warp_floats<CT>() - 64);
+  auto load_kk = [&](int j) -> int2 {
+    const int64_t p = pb + lane + 32 * (int64_t)j;
+    return (j < nit && p < pe) ? __ldg(pairs + p) : make_int2(-1, -1);
+  };
+  // Copy the records of step j (pair indices kk, one pair per lane) into its buffer:
+  // piece g = lane + 32 m of the step is part g % Q of record g / Q (record 2 q + side is
+  // side `side` of pair q), so consecutive lanes read consecutive 16 bytes of a record.
+  auto stage = [&](int j, int2 kk) {
+    __syncwarp();                        // every lane is done with the buffer and the indices
+    reinterpret_cast<int2*>(sidx)[lane] = kk;
+    __syncwarp();
+    float* dst = sm + (j % kPairStages) * STAGE;
+    if constexpr (32 % Q == 0 && Q <= 16) {
+      // lane-constant part and record parity; the record advances by 32/Q per piece round
+      constexpr int RPM = 32 / Q;
+      const int r0 = lane / Q, part = lane % Q;
+      float* d0 = dst + (r0 >> 1) * SLOT + (r0 & 1) * R + 4 * part;
+      const float* s0 = c.rec + 4 * part;
 #pragma unroll
-  for (int v = 0; v < NA * W; ++v) acc[v] = 0.f;
-  const int nb = (int)((pe - pb + kPairBatch - 1) / kPairBatch);
-  stage_batch<CT>(c, load_batch_pairs(c, pb, pe), sm);
-  cp_async_commit();
-  int2 kk_next = load_batch_pairs(c, pb + kPairBatch, pe);      // one batch ahead
-  for (int it = 0; it < nb; ++it) {
-    const int64_t base = pb + (int64_t)it * kPairBatch;
-    if (it + 1 < nb) stage_batch<CT>(c, kk_next, sm + ((it + 1) & 1) * BUF);
-    cp_async_commit();
-    kk_next = load_batch_pairs(c, base + 2 * kPairBatch, pe);
-    cp_async_wait<1>();
-    __syncthreads();
-    const float* buf = sm + (it & 1) * BUF;
-    if (base + lane < pe) {
-      float yc[R], yr[R];
-      const float4* pr = reinterpret_cast<const float4*>(buf + lane * RS);
-      const float4* pc = reinterpret_cast<const float4*>(buf + (kPairBatch + lane) * RS);
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        const float4 v = pc[q];
-        yc[4 * q] = v.x; yc[4 * q + 1] = v.y; yc[4 * q + 2] = v.z; yc[4 * q + 3] = v.w;
+      for (int m = 0; m < 2 * Q; ++m) {
+        const int k = sidx[r0 + RPM * m];
+        if (k >= 0) cp_async16(d0 + (RPM / 2) * m * SLOT, s0 + (int64_t)k * R);
       }
-#pragma unroll
-      for (int q = QLO; q < QHI; ++q) {
-        const float4 v = pr[q];
-        yr[4 * q] = v.x; yr[4 * q + 1] = v.y; yr[4 * q + 2] = v.z; yr[4 * q + 3] = v.w;
-      }
-      float qz[8], sz = 0.f;
-      if (HAS_Z) {
-#pragma unroll
-        for (int bb = 0; bb < 8; ++bb) qz[bb] = yr[24] * yc[3 * bb] + yr[25] * yc[3 * bb + 1] + yr[26] * yc[3 * bb + 2];
-        sz = yr[24] * yc[24] + yr[25] * yc[25] + yr[26] * yc[26];
-      }
-#pragma unroll
-      for (int a = A0; a < A1; ++a) {
-        float* ac = acc + (a - A0) * W;
-        if (a < 8) {
-          const float t0 = yr[3 * a], t1 = yr[3 * a + 1], t2 = yr[3 * a + 2];
-#pragma unroll
-          for (int bb = 0; bb < 8; ++bb) ac[bb] += t0 * yc[3 * bb] + t1 * yc[3 * bb + 1] + t2 * yc[3 * bb + 2];
-          const float u = t0 * yc[24] + t1 * yc[25] + t2 * yc[26];
-#pragma unroll
-          for (int ch = 0; ch < CT; ++ch) ac[8 + ch] += u * yc[27 + ch];
-        } else {
-          const float dr = yr[27 + (a - 8)];
-#pragma unroll
-          for (int bb = 0; bb < 8; ++bb) ac[bb] += dr * qz[bb];
-          const float ds = dr * sz;
-#pragma unroll
-          for (int ch = 0; ch < CT; ++ch) ac[8 + ch] += ds * yc[27 + ch];
-        }
+    } else {
+#pragma unroll 4
+      for (int m = 0; m < 2 * Q; ++m) {
+        const int g = lane + 32 * m;
+        const int r = g / Q, part = g - r * Q;
+        const int k = sidx[r];
+        if (k >= 0) cp_async16(dst + (r >> 1) * SLOT + (r & 1) * R + 4 * part, c.rec + (int64_t)k * R + 4 * part);
       }
     }
-    __syncthreads();
-  }
-  // epilogue: transpose the lane partials through shared memory (stride 33: conflict-free),
-  // then each lane sums and emits values lane, lane+32, ... with a compact runtime loop
-  float* red = sm + (threadIdx.x >> 5) * pair_max_acc<CT>() * 33;
+    cp_async_commit();   // one group per step, empty past the end: uniform group counting
+  };
+  float2 acc[NA][NC2];
+  float acco[NA];
 #pragma unroll
-  for (int v = 0; v < NA * W; ++v) red[v * 33 + lane] = acc[v];
+  for (int a = 0; a < NA; ++a) {
+#pragma unroll
+    for (int q = 0; q < NC2; ++q) acc[a][q] = make_float2(0.f, 0.f);
+    acco[a] = 0.f;
+  }
+  stage(0, load_kk(0));
+  stage(1, load_kk(1));
+  int2 kk_next = load_kk(2);
+  for (int j = 0; j < nit; ++j) {
+    stage(j + 2, kk_next);
+    kk_next = load_kk(j + 3);
+    cp_async_wait<kPairStages - 1>();     // this lane's copies of step j have landed
+    __syncwarp();                         // ... and every other lane's
+    if (pb + lane + 32 * (int64_t)j < pe) {
+      const float* buf = sm + (j % kPairStages) * STAGE + lane * SLOT;
+      const float2* pc2 = reinterpret_cast<const float2*>(buf + R);
+      float2 yc[3][4];                    // column record, Y'[r][2q .. 2q+1]
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) yc[r][q] = pc2[4 * r + q];
+      float2 dc[NZ2 > 0 ? NZ2 : 1];       // column depth channels, paired
+#pragma unroll
+      for (int q = 0; q < NZ2; ++q) dc[q] = pc2[12 + q];
+      const float dco = ODD ? buf[R + 24 + CT - 1] : 0.f;
+      const float zc0 = buf[R + ZS], zc1 = buf[R + ZS + 1], zc2 = buf[R + ZS + 2];
+      if constexpr (Z1 > 0) {             // depth rows: dep[ch] * (zs^T Y'), dep[ch] * sz * dep'
+        const float zr0 = buf[ZS], zr1 = buf[ZS + 1], zr2 = buf[ZS + 2];
+        float2 qz[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          qz[q] = __fmul2_rn(make_float2(zr0, zr0), yc[0][q]);
+          qz[q] = __ffma2_rn(make_float2(zr1, zr1), yc[1][q], qz[q]);
+          qz[q] = __ffma2_rn(make_float2(zr2, zr2), yc[2][q], qz[q]);
+        }
+        const float sz = fmaf(zr2, zc2, fmaf(zr1, zc1, zr0 * zc0));
+#pragma unroll
+        for (int z = Z0; z < Z1; ++z) {
+          const int a = 8 + z - A0;
+          const float dr = buf[24 + z];
+          const float2 d2 = make_float2(dr, dr);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[a][q] = __ffma2_rn(d2, qz[q], acc[a][q]);
+          const float ds = dr * sz;
+          const float2 s2 = make_float2(ds, ds);
+#pragma unroll
+          for (int q = 0; q < NZ2; ++q) acc[a][4 + q] = __ffma2_rn(s2, dc[q], acc[a][4 + q]);
+          if (ODD) acco[a] = fmaf(ds, dco, acco[a]);
+        }
+      }
+#pragma unroll
+      for (int b = B0; b < B1; ++b) {      // base rows
+        const int a = b - A0;
+        const float t0 = buf[b], t1 = buf[8 + b], t2 = buf[16 + b];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[a][q] = __ffma2_rn(make_float2(t0, t0), yc[0][q], acc[a][q]);
+          acc[a][q] = __ffma2_rn(make_float2(t1, t1), yc[1][q], acc[a][q]);
+          acc[a][q] = __ffma2_rn(make_float2(t2, t2), yc[2][q], acc[a][q]);
+        }
+        const float u = fmaf(t2, zc2, fmaf(t1, zc1, t0 * zc0));
+        const float2 u2 = make_float2(u, u);
+#pragma unroll
+        for (int q = 0; q < NZ2; ++q) acc[a][4 + q] = __ffma2_rn(u2, dc[q], acc[a][4 + q]);
+        if (ODD) acco[a] = fmaf(u, dco, acco[a]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+  // epilogue: transpose the lane partials through shared memory (stride 33: conflict-free),
+  // then each lane sums values lane, lane+32, ... over the 32 lanes and emits them
+#pragma unroll
+  for (int a = 0; a < NA; ++a) {
+#pragma unroll
+    for (int q = 0; q < NC2; ++q) {
+      sm[(a * W + 2 * q) * 33 + lane] = acc[a][q].x;
+      if (2 * q + 1 < W) sm[(a * W + 2 * q + 1) * 33 + lane] = acc[a][q].y;
+    }
+    if (ODD) sm[(a * W + W - 1) * 33 + lane] = acco[a];
+  }
   __syncwarp();
   for (int v = lane; v < NA * W; v += 32) {
     float t = 0.f;
-    for (int j = 0; j < 32; ++j) t += red[v * 33 + j];
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) t += sm[v * 33 + j];
     emit_pair_value<CT>(c, S, s, A0 + v / W, v % W, t);
   }
 }
 
+template <int CT, int NR, int r>
+__device__ __forceinline__ void pair_role_dispatch(const Ctx& c, float* S, int64_t task, int role, float* sm) {
+  if constexpr (r < NR) {
+    if (role == r) pair_task<CT, role_row<CT, NR, r>(), role_row<CT, NR, r + 1>()>(c, S, task, sm);
+    else pair_role_dispatch<CT, NR, r + 1>(c, S, task, role, sm);
+  }
+}
+
+// grid (ceil(n_tasks / kPairWarps), pair_roles): warp w of block x runs task x*kPairWarps+w,
+// output rows of role blockIdx.y
 template <int CT>
-__global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* __restrict__ S) {
-  constexpr int NR = pair_roles<CT>();
+__global__ void __launch_bounds__(kPairWarps * 32) k_pairs(Ctx c, float* __restrict__ S) {
   extern __shared__ __align__(16) float sm_dyn[];
-  const int64_t task = blockIdx.x;
-  const int s = c.d.task_seg[task];
-  const int64_t pb = c.d.task_pb[task], pe = c.d.task_pb[task + 1];
-  const int role = threadIdx.x >> 5;
-  if (role == 0) pair_role<CT, role_row<CT, NR, 0>(), role_row<CT, NR, 1>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 1) if (role == 1) pair_role<CT, role_row<CT, NR, 1>(), role_row<CT, NR, 2>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 2) if (role == 2) pair_role<CT, role_row<CT, NR, 2>(), role_row<CT, NR, 3>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 3) if (role == 3) pair_role<CT, role_row<CT, NR, 3>(), role_row<CT, NR, 4>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 4) if (role == 4) pair_role<CT, role_row<CT, NR, 4>(), role_row<CT, NR, 5>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 5) if (role == 5) pair_role<CT, role_row<CT, NR, 5>(), role_row<CT, NR, 6>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 6) if (role == 6) pair_role<CT, role_row<CT, NR, 6>(), role_row<CT, NR, 7>()>(c, S, s, pb, pe, sm_dyn);
-  if constexpr (NR > 7) if (role == 7) pair_role<CT, role_row<CT, NR, 7>(), role_row<CT, NR, 8>()>(c, S, s, pb, pe, sm_dyn);
+  const int warp = threadIdx.x >> 5;
+  const int64_t task = (int64_t)blockIdx.x * kPairWarps + warp;
+  if (task >= c.d.n_tasks) return;                       // warp-uniform
+  float* sm = sm_dyn + warp * pair_warp_floats<CT>();
+  pair_role_dispatch<CT, pair_roles<CT>(), 0>(c, S, task, (int)blockIdx.y, sm);
 }
 
 // ------------------------------------------------------------------------------------
@@ -997,14 +1060,15 @@ int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) 
 
 template <int CT>
 int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
-  const size_t smem = pair_smem_floats<CT>() * sizeof(float);
+  const size_t smem = (size_t)kPairWarps * pair_warp_floats<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
   if (!configured) {
     B3R_TRY(check_cuda(cudaFuncSetAttribute(k_pairs<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "pairs smem attribute"));
     configured = true;
   }
-  k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, smem, s>>>(c, S);
+  const dim3 grid((unsigned)((c.d.n_tasks + kPairWarps - 1) / kPairWarps), (unsigned)pair_roles<CT>());
+  k_pairs<CT><<<grid, kPairWarps * 32, smem, s>>>(c, S);
   return check_launch("pairs pass");
 }
 
