@@ -314,10 +314,16 @@ static int build_pairs(PlanBuild& B) {
   } catch (const std::bad_alloc&) {
     return fail(B3R_E_NOMEM, "cannot allocate %lld observation pairs", (long long)P);
   }
+  // pairs name the elimination records by image-major slot e (the diag pass writes them)
+  std::vector<int> e_of_k(B.perm_t.size(), -1);
+  for (size_t e = 0; e < B.c1_k.size(); ++e)
+    if (B.c1_k[e] >= 0) e_of_k[B.c1_k[e]] = (int)e;
   {
     std::vector<int64_t> fill(B.seg_cnt.begin(), B.seg_cnt.end() - 1);
-    for_pairs([&](int64_t s, int ka, int kb) { B.pairs[fill[s]++] = make_int2(ka, kb); });
+    for_pairs([&](int64_t s, int ka, int kb) { B.pairs[fill[s]++] = make_int2(e_of_k[ka], e_of_k[kb]); });
   }
+  for (const int2& pr : B.pairs)
+    B3R_REQUIRE(pr.x >= 0 && pr.y >= 0, "internal: pair observation without an image-major slot");
   // Tasks: segments cut into <= kPairTask pairs, issued longest first so the short ones
   // fill in behind them (the pair lists stay in segment order; a task is a (segment, range)).
   std::vector<std::pair<int64_t, int64_t>> cuts;   // (first pair, segment)
@@ -539,7 +545,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   P->ws_img = 0;
   P->ws_trec = align256(P->ws_img + sizeof(float) * kImgRecFloats * (size_t)d.n_imgs);
   P->ws_rec = align256(P->ws_trec + sizeof(float) * 24 * (size_t)d.nT_loc);
-  P->ws_rw = align256(P->ws_rec + sizeof(float) * (size_t)d.R * (size_t)d.n_loc);
+  P->ws_rw = align256(P->ws_rec + sizeof(float) * (size_t)d.R * (size_t)d.n_c1);
   P->ws_misc = align256(P->ws_rw + sizeof(float) * 6 * (size_t)d.n_loc);
   const size_t ws_total = P->ws_misc + 256;
 

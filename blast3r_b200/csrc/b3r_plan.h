@@ -65,7 +65,7 @@ struct DevPlan {
   int64_t n_seg, n_pairs, n_tasks;
   const int* seg_dst;     // [n_seg*9] value offset of each (a,b) sub-block, -1 none
   const int* seg_mode;    // [n_seg] 2 bits per sub-block (a*3+b)
-  const int2* pairs;      // [n_pairs] (k_row, k_col)
+  const int2* pairs;      // [n_pairs] (e_row, e_col): image-major slots of the two observations
   const int64_t* task_pb; // [n_tasks] first pair of each task (tasks longest first)
   const int64_t* task_pe; // [n_tasks] end of each task
   const int* task_seg;    // [n_tasks]
@@ -98,7 +98,8 @@ struct b3r_plan {
   void* dev_mem = nullptr;
   size_t dev_bytes = 0;
   // workspace layout (byte offsets): image records | track records (24 floats: Hpp, g_p,
-  // then Cholesky factor and L^-1 g_p) | elimination records | staged r/w | misc scalars
+  // then the Cholesky factor in reciprocal form and L^-1 g_p) | elimination records (one
+  // per image-major slot e) | staged r/w | misc scalars
   size_t ws_img = 0, ws_trec = 0, ws_rec = 0, ws_rw = 0, ws_misc = 0;
   int64_t n_pairs_total = 0;
   bool staged = false;

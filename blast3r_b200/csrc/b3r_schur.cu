@@ -6,12 +6,13 @@
 //   prep      per-image camera records (one 128-byte line per image)
 //   points    track-major, one warp per <=32-observation task: per-track Hpp and g_p by a
 //             segmented warp scan, and the max |diag(Hpp)| for adaptive damping
-//   eliminate track-major: damped guarded 3x3 Cholesky Hpp = L L^T (sfm_jacobian_rigs.cu
-//             :578-617), z = L^-1 g_p, and per observation the elimination record
-//             Y = L^-1 Hpc in reduced form (3 x [f0 f1 tau0..5 zscale]) + its depth channels
-//   diag      image-major: per observation Hcc - Y^T Y and g_c - Y^T z expanded to the
-//             typed blocks of its image, reduced per image chunk in registers, one atomic
-//             per value per chunk; also diag(Hcc) for the damping and preconditioner
+//   factor    per track: damped guarded 3x3 Cholesky Hpp = L L^T (sfm_jacobian_rigs.cu
+//             :578-617), stored in reciprocal form, and z = L^-1 g_p
+//   diag      image-major: per observation the elimination record Y = L^-1 Hpc in reduced
+//             form (3 x [f0 f1 tau0..5 zscale]) + its depth channels, written to its
+//             image-major slot; Hcc - Y^T Y and g_c - Y^T z expanded to the typed blocks of
+//             its image, reduced per image chunk, one atomic per value per chunk; also
+//             diag(Hcc) for the damping and preconditioner
 //   pairs     segment-major: for every image pair (i, i') the sum over shared tracks of
 //             -Y_o^T Y_o' accumulated in registers over up to 512 observation pairs,
 //             records staged through shared memory, one atomic per value per task
@@ -239,30 +240,31 @@ __host__ __device__ constexpr int rec_floats() { return (27 + CT + 3) & ~3; }
 template <int CT>
 __host__ __device__ constexpr int rec_zs() { return 24 + CT; }
 
+// Y = L^-1 Hpc of one observation from the track's factor in reciprocal form
+// li = (1/l00, l10, l20, 1/l11, l21, 1/l22); written as the record of slot e.
 template <int CT>
-__device__ __forceinline__ void write_record(const Ctx& c, int64_t k, const ObsView<CT>& V, const float l[6]) {
+__device__ __forceinline__ void elim_record(const Ctx& c, int64_t e, const ObsView<CT>& V, const float li[6],
+                                            float Y[9][3]) {
   constexpr int R = rec_floats<CT>();
   float rv[R];
 #pragma unroll
   for (int a = 0; a < 9; ++a) {
     float h[3];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      float s = 0.f;
+    for (int j = 0; j < 3; ++j)
+      h[j] = fmaf(V.Jpw[6 + j], V.Jcw[18 + a], fmaf(V.Jpw[3 + j], V.Jcw[9 + a], V.Jpw[j] * V.Jcw[a]));
+    const float y0 = h[0] * li[0];
+    const float y1 = (h[1] - li[1] * y0) * li[3];
+    const float y2 = (h[2] - li[2] * y0 - li[4] * y1) * li[5];
+    Y[a][0] = y0; Y[a][1] = y1; Y[a][2] = y2;
 #pragma unroll
-      for (int i = 0; i < 3; ++i) s += V.Jpw[3 * i + j] * V.Jcw[9 * i + a];
-      h[j] = s;
-    }
-    float y[3];
-    chol3_fwd<float>(l, h, y);
-#pragma unroll
-    for (int r = 0; r < 3; ++r) rv[a < 8 ? 8 * r + a : rec_zs<CT>() + r] = y[r];
+    for (int r = 0; r < 3; ++r) rv[a < 8 ? 8 * r + a : rec_zs<CT>() + r] = Y[a][r];
   }
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) rv[24 + ch] = V.dep[ch];
 #pragma unroll
-  for (int e = 27 + CT; e < R; ++e) rv[e] = 0.f;
-  float4* dst = reinterpret_cast<float4*>(c.rec + k * R);
+  for (int q = 27 + CT; q < R; ++q) rv[q] = 0.f;
+  float4* dst = reinterpret_cast<float4*>(c.rec + e * R);
 #pragma unroll
   for (int q = 0; q < R / 4; ++q) dst[q] = make_float4(rv[4 * q], rv[4 * q + 1], rv[4 * q + 2], rv[4 * q + 3]);
 }
@@ -326,61 +328,24 @@ __global__ void __launch_bounds__(128) k_points(Ctx c) {
   if (lane == 0) atomic_max_nonneg(c.hpp_max, wmax);
 }
 
-// Damped Cholesky factor of a track (BlockDiagMat.dampen_ then chol3x3_solve's guarded
-// factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599).
-__device__ __forceinline__ void track_factor(const Ctx& c, float lam, int tl, float l[6], float z[3]) {
-  const float* t = c.trec + (int64_t)tl * 24;
+// Pass "factor": damped Cholesky factor of every local track (BlockDiagMat.dampen_ then
+// chol3x3_solve's guarded factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599)
+// and z = L^-1 g_p.  The factor is stored in reciprocal form (1/l00, l10, l20, 1/l11,
+// l21, 1/l22) at track-record floats 12..17, z at 18..20, so the per-observation
+// elimination Y = L^-1 Hpc needs no division.
+__global__ void __launch_bounds__(256) k_factor(Ctx c) {
+  const int tl = blockIdx.x * blockDim.x + threadIdx.x;
+  const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
+  if (tl == 0) c.misc[1] = lam;   // point damping, reused by the back-substitution
+  if (tl >= c.d.nT_loc) return;
+  float* t = c.trec + (int64_t)tl * 24;
   const float h00 = t[0] + lam, h01 = t[1], h02 = t[2], h11 = t[3] + lam, h12 = t[4], h22 = t[5] + lam;
+  float l[6], z[3];
   chol3<float>(h00, h01, h02, h01, h11, h12, h02, h12, h22, 1e-12f, l);
   const float g[3] = {t[6], t[7], t[8]};
   chol3_fwd<float>(l, g, z);
-}
-
-// Pass "eliminate": Cholesky factor per track and the per-observation records.
-template <int CT>
-__global__ void __launch_bounds__(128) k_eliminate(Ctx c) {
-  const int task = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  if (task >= c.d.n_pt_tasks) return;
-  const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
-  const int n = ke - kb;
-  const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
-  if (task == 0 && lane == 0) c.misc[1] = lam;   // point damping, reused by the back-substitution
-  if (n <= kWarp) {
-    if (lane >= n) return;
-    const int64_t k = kb + lane;
-    ObsView<CT> V;
-    int tl;
-    view_local<CT>(c, k, V, tl);
-    float l[6], z[3];
-    track_factor(c, lam, tl, l, z);
-    write_record<CT>(c, k, V, l);
-    const bool tail = (lane == n - 1) || (c.d.trk_t[k + 1] != tl);
-    if (tail) {
-      float* t = c.trec + (int64_t)tl * 24;
-#pragma unroll
-      for (int j = 0; j < 6; ++j) t[12 + j] = l[j];
-#pragma unroll
-      for (int j = 0; j < 3; ++j) t[18 + j] = z[j];
-    }
-  } else {
-    const int tl = c.d.trk_t[kb];
-    float l[6], z[3];
-    track_factor(c, lam, tl, l, z);
-    for (int k = kb + lane; k < ke; k += kWarp) {
-      ObsView<CT> V;
-      int tl_k;
-      view_local<CT>(c, k, V, tl_k);
-      write_record<CT>(c, k, V, l);
-    }
-    if (lane == 0) {
-      float* t = c.trec + (int64_t)tl * 24;
-#pragma unroll
-      for (int j = 0; j < 6; ++j) t[12 + j] = l[j];
-#pragma unroll
-      for (int j = 0; j < 3; ++j) t[18 + j] = z[j];
-    }
-  }
+  t[12] = 1.f / l[0]; t[13] = l[1]; t[14] = l[2]; t[15] = 1.f / l[3]; t[16] = l[4]; t[17] = 1.f / l[5];
+  t[18] = z[0]; t[19] = z[1]; t[20] = z[2];
 }
 
 // ------------------------------------------------------------------------------------
@@ -405,7 +370,8 @@ struct DiagLayout {
 __host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - a * (a - 1) / 2 + (b - a); }
 
 template <int CT>
-__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, int64_t k, int tl, float* acc) {
+__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, bool elim, int64_t e, int tl,
+                                           float* acc) {
   using Lay = DiagLayout<CT>;
   float H[9][9];
 #pragma unroll
@@ -432,20 +398,11 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, i
   for (int t = 0; t < 6; ++t) acc[Lay::DA + 2 + t] += H[2 + t][2 + t];
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) acc[Lay::DA + 8 + ch] += H[8][8] * V.dep[ch] * V.dep[ch];
-  if (k >= 0) {                                   // eliminated track: subtract Y^T Y, Y^T z
-    constexpr int R = rec_floats<CT>();
-    const float4* r4 = reinterpret_cast<const float4*>(c.rec + k * R);
-    float Yf[R];
-#pragma unroll
-    for (int q = 0; q < R / 4; ++q) {
-      const float4 v = __ldg(r4 + q);
-      Yf[4 * q] = v.x; Yf[4 * q + 1] = v.y; Yf[4 * q + 2] = v.z; Yf[4 * q + 3] = v.w;
-    }
-    float Y[9][3];   // Y[a][r] = Y[r][a] of the record
-#pragma unroll
-    for (int a = 0; a < 9; ++a)
-#pragma unroll
-      for (int r = 0; r < 3; ++r) Y[a][r] = Yf[a < 8 ? 8 * r + a : rec_zs<CT>() + r];
+  if (elim) {                                     // eliminated track: record Y, subtract Y^T Y, Y^T z
+    const float* tf = c.trec + (int64_t)tl * 24 + 12;
+    const float li[6] = {tf[0], tf[1], tf[2], tf[3], tf[4], tf[5]};
+    float Y[9][3];
+    elim_record<CT>(c, e, V, li, Y);
     const float* tz = c.trec + (int64_t)tl * 24 + 18;
     const float z0 = tz[0], z1 = tz[1], z2 = tz[2];
 #pragma unroll
@@ -519,7 +476,7 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
       const int4 ix = __ldg(c.d.c1_idx + e);     // o, k, track id, local track
       ObsView<CT> V;
       view_image<CT>(c, ix.x, ix.z, img, cam, zc, V);
-      diag_terms<CT>(c, V, ix.y, ix.w, val);
+      diag_terms<CT>(c, V, ix.y >= 0, e, ix.w, val);
     }
 #pragma unroll
     for (int v = 0; v < Lay::N; ++v) rw[v * 33 + lane] = val[v];
@@ -1072,15 +1029,18 @@ int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
   return check_launch("pairs pass");
 }
 
+int launch_factor(const Ctx& c, cudaStream_t s) {
+  k_factor<<<grid_for(std::max(c.d.nT_loc, 1), 256), 256, 0, s>>>(c);   // also records the damping
+  return check_launch("factor pass");
+}
+
 template <int CT>
 int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaStream_t s) {
   switch (pass) {
     case B3R_PASS_POINTS:
       return launch_points<CT>(c, s);
     case B3R_PASS_ELIMINATE:
-      if (c.d.n_pt_tasks == 0) return B3R_OK;
-      k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
-      return check_launch("eliminate pass");
+      return launch_factor(c, s);
     case B3R_PASS_DIAG:
       if (c.d.n_c1_chunks == 0) return B3R_OK;
       return diag_launch<CT>(c, S, b, diagA, s);
@@ -1093,10 +1053,7 @@ int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaSt
 
 template <int CT>
 int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
-  if (c.d.n_pt_tasks > 0) {
-    k_eliminate<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
-    B3R_TRY(check_launch("eliminate pass"));
-  }
+  B3R_TRY(launch_factor(c, s));
   if (c.d.n_c1_chunks > 0) B3R_TRY(diag_launch<CT>(c, S, b, diagA, s));
   if (c.d.n_tasks > 0) B3R_TRY(pairs_launch<CT>(c, S, s));
   return B3R_OK;
