@@ -8,6 +8,7 @@
 // and used by the residual op, the Jacobian op and every pass of the fused
 // linearization, so all of them see identical residuals and weights.
 #pragma once
+#include <cmath>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -84,7 +85,24 @@ struct LinOpts {
   int is_depth_log;
   float weight_z, pnorm, max_pix_err, huber_delta, w_pts_nul;
   float clamp_lo, clamp_hi;
+  // derived by finish_lin_opts: the Huber constants a = p/2 delta^(p-2) and
+  // b = delta^p - a delta^2 (uniform per call, .cu:243-244), and which power law the
+  // per-component terms follow (1: p == 1, rr^p = rr, rr^(p-2) = 1/rr; 2: p == 2,
+  // rr^p = rr*rr, rr^(p-2) = 1; 0: general powf)
+  float huber_a, huber_b;
+  int pmode;
 };
+
+// Fill the derived fields of o (host side, once per call).
+inline void finish_lin_opts(LinOpts& o) {
+  o.pmode = o.pnorm == 1.f ? 1 : (o.pnorm == 2.f ? 2 : 0);
+  o.huber_a = 0.f;
+  o.huber_b = 0.f;
+  if (o.pnorm > 0.f) {
+    o.huber_a = 0.5f * o.pnorm * powf(o.huber_delta, o.pnorm - 2.f);
+    o.huber_b = powf(o.huber_delta, o.pnorm) - o.huber_a * o.huber_delta * o.huber_delta;
+  }
+}
 
 // Everything one observation contributes.
 template <typename T>
@@ -164,16 +182,17 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
     else                L.r[2] = fbar * t_log<T>(guid / z);
     // Huber error and IRLS weight per component (.cu:240-258)
     if (o.pnorm > 0.f) {
-      const float a = 0.5f * o.pnorm * powf(o.huber_delta, o.pnorm - 2.f);
-      const float b = powf(o.huber_delta, o.pnorm) - a * o.huber_delta * o.huber_delta;
+      const float a = o.huber_a, b = o.huber_b;
       const float wz[3] = {1.f, 1.f, o.weight_z};
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         float rr = fabsf((float)L.r[i]);
         rr = (rr > o.max_pix_err) ? o.max_pix_err : rr;
-        L.err[i] = wz[i] * ((rr <= o.huber_delta) ? a * rr * rr : powf(rr, o.pnorm) - b);
+        const float pw = o.pmode == 1 ? rr : (o.pmode == 2 ? rr * rr : powf(rr, o.pnorm));
+        L.err[i] = wz[i] * ((rr <= o.huber_delta) ? a * rr * rr : pw - b);
         rr = (rr < o.huber_delta) ? o.huber_delta : rr;
-        L.w[i] = (rr == o.max_pix_err) ? o.w_pts_nul : wz[i] * powf(rr, o.pnorm - 2.f);
+        const float pw2 = o.pmode == 1 ? 1.f / rr : (o.pmode == 2 ? 1.f : powf(rr, o.pnorm - 2.f));
+        L.w[i] = (rr == o.max_pix_err) ? o.w_pts_nul : wz[i] * pw2;
       }
     } else {
 #pragma unroll

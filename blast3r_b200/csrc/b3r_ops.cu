@@ -149,6 +149,7 @@ LinOpts make_opts(int is_depth_log, float weight_z, float pnorm, float max_pix_e
   o.weight_z = weight_z; o.pnorm = pnorm; o.max_pix_err = max_pix_err;
   o.huber_delta = huber_delta; o.w_pts_nul = w_pts_nul;
   o.clamp_lo = 0.f; o.clamp_hi = 0.f;
+  finish_lin_opts(o);
   return o;
 }
 }  // namespace

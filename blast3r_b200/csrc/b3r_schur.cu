@@ -966,6 +966,7 @@ int make_ctx(b3r_plan* plan, const b3r_params* p, const b3r_lin_opts* o, void* w
   c.o.weight_z = o->weight_z; c.o.pnorm = o->pnorm; c.o.max_pix_err = o->max_pix_err;
   c.o.huber_delta = o->huber_delta; c.o.w_pts_nul = o->w_pts_nul;
   c.o.clamp_lo = o->clamp_w_lo; c.o.clamp_hi = o->clamp_w_hi;
+  finish_lin_opts(c.o);
   B3R_REQUIRE(o->pnorm > 0.f && o->pnorm <= 2.f, "pnorm must be in ]0, 2] for a linearization");
   c.no_grad_f_from_rz = o->no_grad_f_from_rz;
   c.optim_Z0 = o->optim_Z0;

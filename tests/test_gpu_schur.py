@@ -15,7 +15,7 @@ from blast3r_b200 import cujac
 from blast3r_b200.plan import BAPlan
 from blast3r_b200.synthetic import make_scene
 from oracle import ba_oracle as O
-from tests.helpers import TOL_ACC, golden_files, load_golden, rel_err, scene_inputs, to_cuda
+from tests.helpers import TOL_ACC, TOL_OBS, golden_files, load_golden, rel_err, scene_inputs, to_cuda
 
 pytestmark = pytest.mark.gpu
 
@@ -65,11 +65,16 @@ def test_schur_matches_reference_solver(path):
 
 @pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
 def test_general_path_equals_recompute(path):
+    """Residuals/weights handed in (the fixture's, from the reference) vs recomputed in-kernel.
+
+    The in-kernel IRLS weight uses the exact power law (1/rr for pnorm 1) where the
+    reference residual kernel calls powf, so the two agree to a few ulps, not bitwise:
+    the bound is the float32 observation tolerance."""
     inp, opts, _ = load_golden(path)
     _, a = run_plan(inp, opts, recompute=True)
     _, b = run_plan(inp, opts, recompute=False)
-    assert rel_err(b.S_vals.cpu().numpy(), a.S_vals.cpu().numpy()) < 1e-6
-    assert rel_err(b.b.cpu().numpy(), a.b.cpu().numpy()) < 1e-6
+    assert rel_err(b.S_vals.cpu().numpy(), a.S_vals.cpu().numpy()) < TOL_OBS
+    assert rel_err(b.b.cpu().numpy(), a.b.cpu().numpy()) < TOL_OBS
 
 
 SCENES = [(0, None, None), (3, None, None), (1, 60, 6000), (2, 80, 8000), (4, 60, 6000)]
