@@ -102,10 +102,8 @@ template <int CT>
 struct ObsView {
   bool valid;
   float Jpw[9];     // sqrt(W) * d r / d X        (3x3 row-major)
-  float Jp[9];      // d r / d X (unscaled, for g_p = J_p^T W r)
   float Jcw[27];    // sqrt(W) * reduced camera J (3x9 row-major)
-  float Wr[3];      // W * r
-  float Jc2[27];    // unscaled reduced camera J (for g = J^T W r)
+  float sWr[3];     // sqrt(W) * r, so J^T W r = Jw^T sWr
   float dep[CT];    // depth channels as used by J (optim_Z0 / optim_Z_1st_cam applied)
 };
 
@@ -126,8 +124,8 @@ __device__ __forceinline__ void make_view(const Ctx& c, const ObsLin& L, float r
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
     const float W = clampw(w[i], c.o.clamp_lo, c.o.clamp_hi);
-    V.Wr[i] = W * r[i];
     sW[i] = sqrtf(W);
+    V.sWr[i] = sW[i] * r[i];
   }
   const bool mf = mask & 1, mt = mask & 2, mz = mask & 4;
   const float jkf = c.no_grad_f_from_rz ? 0.f : L.Jkf;
@@ -144,9 +142,9 @@ __device__ __forceinline__ void make_view(const Ctx& c, const ObsLin& L, float r
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
 #pragma unroll
-    for (int a = 0; a < 9; ++a) { V.Jc2[9 * i + a] = J[9 * i + a]; V.Jcw[9 * i + a] = J[9 * i + a] * sW[i]; }
+    for (int a = 0; a < 9; ++a) V.Jcw[9 * i + a] = J[9 * i + a] * sW[i];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) { V.Jp[3 * i + j] = L.Jp[3 * i + j]; V.Jpw[3 * i + j] = L.Jp[3 * i + j] * sW[i]; }
+    for (int j = 0; j < 3; ++j) V.Jpw[3 * i + j] = L.Jp[3 * i + j] * sW[i];
   }
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) V.dep[ch] = dep_raw[ch];
@@ -185,31 +183,62 @@ __device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>&
   make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, ix.w, image_mask(d, img), V);
 }
 
-// Load + linearize image-sorted observation o of image img.
+
+
+// Raw inputs of one image-major observation, loaded one batch ahead of their use so
+// that the gathers (track point, track factor) overlap the previous batch's arithmetic.
 template <int CT>
-__device__ __forceinline__ void view_image(const Ctx& c, int64_t o, int pid, int img, const Cam& cam,
-                                           const float* zc, ObsView<CT>& V) {
-  const float X[3] = {__ldg(c.pts3d + 3 * (int64_t)pid), __ldg(c.pts3d + 3 * (int64_t)pid + 1),
-                      __ldg(c.pts3d + 3 * (int64_t)pid + 2)};
+struct ObsIn {
+  int4 ix;          // o, k (-1: track not eliminated), track id, local track
+  float X[3];       // track point
+  float px, py, sx, sy;
   float dep[CT];
+  float4 tf0, tf1;  // track factor (reciprocal form) and z, track-record floats 12..19
+  float tf2;        // track-record float 20
+};
+
+template <int CT>
+__device__ __forceinline__ void load_obs_in(const Ctx& c, int e, int ee, ObsIn<CT>& in) {
+  if (e >= ee) { in.ix = make_int4(0, -1, 0, -1); return; }
+  in.ix = __ldg(c.d.c1_idx + e);
+  const int64_t o = in.ix.x, pid = in.ix.z;
+  in.X[0] = __ldg(c.pts3d + 3 * pid); in.X[1] = __ldg(c.pts3d + 3 * pid + 1); in.X[2] = __ldg(c.pts3d + 3 * pid + 2);
+  const float2 s = __ldg(reinterpret_cast<const float2*>(c.pix2d_std) + o);
+  in.sx = s.x; in.sy = s.y;
+  if (c.pix2d) {
+    const float2 q = __ldg(reinterpret_cast<const float2*>(c.pix2d) + o);
+    in.px = q.x; in.py = q.y;
+  } else {
+    in.px = in.py = 0.f;
+  }
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) dep[ch] = __ldg(c.pix2d_dep + o * CT + ch);
-  const float sx = __ldg(c.pix2d_std + 2 * o), sy = __ldg(c.pix2d_std + 2 * o + 1);
+  for (int ch = 0; ch < CT; ++ch) in.dep[ch] = __ldg(c.pix2d_dep + o * CT + ch);
+  if (in.ix.y >= 0) {
+    // trec is 256-byte aligned with 96-byte records: floats 12..19 are two aligned float4
+    const float4* t4 = reinterpret_cast<const float4*>(c.trec + (int64_t)in.ix.w * 24 + 12);
+    in.tf0 = t4[0]; in.tf1 = t4[1];
+    in.tf2 = c.trec[(int64_t)in.ix.w * 24 + 20];
+  }
+}
+
+// Linearize a prefetched image-major observation of image img.
+template <int CT>
+__device__ __forceinline__ void view_in(const Ctx& c, const ObsIn<CT>& in, int img, const Cam& cam, const float* zc,
+                                        ObsView<CT>& V) {
+  const int64_t o = in.ix.x;
   ObsLin L;
   float r0, r1, r2, w0, w1, w2;
   if (c.pix2d) {
-    linearize_obs<float, true, true, CT>(cam, X, __ldg(c.pix2d + 2 * o), __ldg(c.pix2d + 2 * o + 1), sx, sy,
-                                         dep, zc, CT, c.o, L);
+    linearize_obs<float, true, true, CT>(cam, in.X, in.px, in.py, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
   } else {
-    linearize_obs<float, false, true, CT>(cam, X, 0.f, 0.f, sx, sy, dep, zc, CT, c.o, L);
+    linearize_obs<float, false, true, CT>(cam, in.X, 0.f, 0.f, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = c.res[o * c.rs_n]; r1 = c.res[o * c.rs_n + c.rs_c]; r2 = c.res[o * c.rs_n + 2 * c.rs_c];
     const int64_t wc = c.w_cols == 1 ? 0 : c.ws_c;
     w0 = c.wpt[o * c.ws_n]; w1 = c.wpt[o * c.ws_n + wc]; w2 = c.wpt[o * c.ws_n + 2 * wc];
   }
-  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, dep, o, image_mask(c.d, img), V);
+  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, in.dep, o, image_mask(c.d, img), V);
 }
-
 
 // Hpp (upper: 00 01 02 11 12 22) and g_p of one observation.
 template <int CT>
@@ -226,7 +255,7 @@ __device__ __forceinline__ void point_terms(const ObsView<CT>& V, float v[9]) {
   for (int j = 0; j < 3; ++j) {
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 3; ++i) s += V.Jp[3 * i + j] * V.Wr[i];
+    for (int i = 0; i < 3; ++i) s += V.Jpw[3 * i + j] * V.sWr[i];
     v[6 + j] = s;
   }
 }
@@ -370,8 +399,10 @@ struct DiagLayout {
 __host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - a * (a - 1) / 2 + (b - a); }
 
 template <int CT>
-__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, bool elim, int64_t e, int tl,
-                                           float* acc) {
+__device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, bool elim, int64_t e, float4 tf0,
+                                           float4 tf1, float tf2, float* __restrict__ out) {
+  // value v of this observation goes to out[33 v] (its lane's column of the warp's
+  // transpose buffer), as soon as it is computed
   using Lay = DiagLayout<CT>;
   float H[9][9];
 #pragma unroll
@@ -388,58 +419,56 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
   for (int a = 0; a < 9; ++a) {
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 3; ++i) s += V.Jc2[9 * i + a] * V.Wr[i];
+    for (int i = 0; i < 3; ++i) s += V.Jcw[9 * i + a] * V.sWr[i];
     g[a] = s;
   }
   // undamped diag(A) = diag(Hcc)
-  acc[Lay::DA + 0] += H[0][0];
-  acc[Lay::DA + 1] += H[1][1];
+  out[33 * (Lay::DA + 0)] = H[0][0];
+  out[33 * (Lay::DA + 1)] = H[1][1];
 #pragma unroll
-  for (int t = 0; t < 6; ++t) acc[Lay::DA + 2 + t] += H[2 + t][2 + t];
+  for (int t = 0; t < 6; ++t) out[33 * (Lay::DA + 2 + t)] = H[2 + t][2 + t];
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) acc[Lay::DA + 8 + ch] += H[8][8] * V.dep[ch] * V.dep[ch];
+  for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::DA + 8 + ch)] = H[8][8] * V.dep[ch] * V.dep[ch];
   if (elim) {                                     // eliminated track: record Y, subtract Y^T Y, Y^T z
-    const float* tf = c.trec + (int64_t)tl * 24 + 12;
-    const float li[6] = {tf[0], tf[1], tf[2], tf[3], tf[4], tf[5]};
+    const float li[6] = {tf0.x, tf0.y, tf0.z, tf0.w, tf1.x, tf1.y};
     float Y[9][3];
     elim_record<CT>(c, e, V, li, Y);
-    const float* tz = c.trec + (int64_t)tl * 24 + 18;
-    const float z0 = tz[0], z1 = tz[1], z2 = tz[2];
+    const float z0 = tf1.z, z1 = tf1.w, z2 = tf2;
 #pragma unroll
     for (int a = 0; a < 9; ++a) {
 #pragma unroll
       for (int b = a; b < 9; ++b)
-        H[a][b] -= Y[a][0] * Y[b][0] + Y[a][1] * Y[b][1] + Y[a][2] * Y[b][2];
-      g[a] -= Y[a][0] * z0 + Y[a][1] * z1 + Y[a][2] * z2;
+        H[a][b] = fmaf(-Y[a][2], Y[b][2], fmaf(-Y[a][1], Y[b][1], fmaf(-Y[a][0], Y[b][0], H[a][b])));
+      g[a] = fmaf(-Y[a][2], z2, fmaf(-Y[a][1], z1, fmaf(-Y[a][0], z0, g[a])));
     }
   }
-  acc[Lay::FF + 0] += H[0][0];
-  acc[Lay::FF + 1] += H[0][1];
-  acc[Lay::FF + 2] += H[1][1];
+  out[33 * (Lay::FF + 0)] = H[0][0];
+  out[33 * (Lay::FF + 1)] = H[0][1];
+  out[33 * (Lay::FF + 2)] = H[1][1];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
 #pragma unroll
-    for (int t = 0; t < 6; ++t) acc[Lay::FT + 6 * r + t] += H[r][2 + t];
+    for (int t = 0; t < 6; ++t) out[33 * (Lay::FT + 6 * r + t)] = H[r][2 + t];
 #pragma unroll
-    for (int ch = 0; ch < CT; ++ch) acc[Lay::FZ + CT * r + ch] += H[r][8] * V.dep[ch];
+    for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::FZ + CT * r + ch)] = H[r][8] * V.dep[ch];
   }
 #pragma unroll
   for (int a = 0; a < 6; ++a) {
 #pragma unroll
-    for (int b = a; b < 6; ++b) acc[Lay::TT + sym_idx(a, b, 6)] += H[2 + a][2 + b];
+    for (int b = a; b < 6; ++b) out[33 * (Lay::TT + sym_idx(a, b, 6))] = H[2 + a][2 + b];
 #pragma unroll
-    for (int ch = 0; ch < CT; ++ch) acc[Lay::TZ + CT * a + ch] += H[2 + a][8] * V.dep[ch];
+    for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::TZ + CT * a + ch)] = H[2 + a][8] * V.dep[ch];
   }
 #pragma unroll
   for (int a = 0; a < CT; ++a) {
     const float ha = H[8][8] * V.dep[a];
 #pragma unroll
-    for (int b = a; b < CT; ++b) acc[Lay::ZZ + sym_idx(a, b, CT)] += ha * V.dep[b];
+    for (int b = a; b < CT; ++b) out[33 * (Lay::ZZ + sym_idx(a, b, CT))] = ha * V.dep[b];
   }
 #pragma unroll
-  for (int a = 0; a < 8; ++a) acc[Lay::B + a] += g[a];
+  for (int a = 0; a < 8; ++a) out[33 * (Lay::B + a)] = g[a];
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) acc[Lay::B + 8 + ch] += g[8] * V.dep[ch];
+  for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::B + 8 + ch)] = g[8] * V.dep[ch];
 }
 
 constexpr int kDiagThreads = 64;   // two warps per image chunk
@@ -467,19 +496,19 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
   float run[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) run[j] = 0.f;
+  ObsIn<CT> nxt;
+  load_obs_in<CT>(c, eb + warp * kWarp + lane, ee, nxt);
   for (int base = eb + warp * kWarp; base < ee; base += NW * kWarp) {
     const int e = base + lane;
-    float val[Lay::N];
-#pragma unroll
-    for (int v = 0; v < Lay::N; ++v) val[v] = 0.f;
+    const ObsIn<CT> cur = nxt;
+    if (base + NW * kWarp < ee) load_obs_in<CT>(c, e + NW * kWarp, ee, nxt);   // next batch, warp-uniform
     if (e < ee) {
-      const int4 ix = __ldg(c.d.c1_idx + e);     // o, k, track id, local track
       ObsView<CT> V;
-      view_image<CT>(c, ix.x, ix.z, img, cam, zc, V);
-      diag_terms<CT>(c, V, ix.y >= 0, e, ix.w, val);
+      view_in<CT>(c, cur, img, cam, zc, V);
+      diag_terms<CT>(c, V, cur.ix.y >= 0, e, cur.tf0, cur.tf1, cur.tf2, rw + lane);
+    } else {
+      for (int v = 0; v < Lay::N; ++v) rw[v * 33 + lane] = 0.f;
     }
-#pragma unroll
-    for (int v = 0; v < Lay::N; ++v) rw[v * 33 + lane] = val[v];
     __syncwarp();
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -886,7 +915,7 @@ __device__ __forceinline__ void backsub_terms(const Ctx& c, int64_t k, const flo
     double g = 0.0, cdv = 0.0;
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      g += (double)V.Jp[3 * i + j] * (double)V.Wr[i];
+      g += (double)V.Jpw[3 * i + j] * (double)V.sWr[i];
       cdv += (double)V.Jpw[3 * i + j] * Jv[i];
     }
     u[6 + j] = g - cdv;
@@ -986,6 +1015,8 @@ int make_ctx(b3r_plan* plan, const b3r_params* p, const b3r_lin_opts* o, void* w
     c.K = p->K; c.P_rig2c = p->P_rig2c; c.P_stride = p->P_rig2c_stride; c.P_w2rig = p->P_w2rig;
     c.z_coefs = p->z_coefs; c.pts3d = p->pts3d;
     c.pix2d = p->pix2d; c.pix2d_std = p->pix2d_std; c.pix2d_dep = p->pix2d_dep;
+    B3R_REQUIRE(((uintptr_t)p->pix2d & 7) == 0 && ((uintptr_t)p->pix2d_std & 7) == 0,
+                "pix2d and pix2d_std must be 8-byte aligned (float pairs)");
     if (!p->pix2d) {
       B3R_REQUIRE(p->residuals && p->w_pts, "residuals and w_pts are required when pix2d is NULL");
       B3R_REQUIRE(p->w_cols == 1 || p->w_cols == 3, "w_cols must be 1 or 3");
