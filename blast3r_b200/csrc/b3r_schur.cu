@@ -185,6 +185,50 @@ __device__ __forceinline__ void view_local(const Ctx& c, int64_t k, ObsView<CT>&
 
 
 
+// Raw inputs of one local (track-sorted) observation, loaded one task ahead.
+template <int CT>
+struct LocIn {
+  int4 ix;          // image, global track id, local track, o
+  float X[3];
+  float2 px, sd;
+  float dep[CT];
+};
+
+template <int CT>
+__device__ __forceinline__ void load_loc_in(const Ctx& c, int64_t k, bool valid, LocIn<CT>& in) {
+  if (!valid) { in.ix = make_int4(0, 0, -1, 0); return; }
+  const DevPlan& d = c.d;
+  in.ix = __ldg(d.t_idx + k);
+  const int64_t gid = in.ix.y;
+  in.X[0] = __ldg(c.pts3d + 3 * gid); in.X[1] = __ldg(c.pts3d + 3 * gid + 1); in.X[2] = __ldg(c.pts3d + 3 * gid + 2);
+  in.sd = d.t_std[k];
+  in.px = c.pix2d ? d.t_pix[k] : make_float2(0.f, 0.f);
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) in.dep[ch] = d.t_dep[(int64_t)ch * d.n_loc + k];
+}
+
+// Linearize a prefetched local observation k.
+template <int CT>
+__device__ __forceinline__ void view_loc(const Ctx& c, int64_t k, const LocIn<CT>& in, ObsView<CT>& V) {
+  const int img = in.ix.x;
+  const Cam cam = load_cam(c.img_rec + (int64_t)img * kImgRec);
+  float zc[CT];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
+  ObsLin L;
+  float r0, r1, r2, w0, w1, w2;
+  if (c.pix2d) {
+    linearize_obs<float, true, true, CT>(cam, in.X, in.px.x, in.px.y, in.sd.x, in.sd.y, in.dep, zc, CT, c.o, L);
+    r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
+  } else {
+    linearize_obs<float, false, true, CT>(cam, in.X, 0.f, 0.f, in.sd.x, in.sd.y, in.dep, zc, CT, c.o, L);
+    const int64_t n = c.d.n_loc;
+    r0 = c.t_rw[k]; r1 = c.t_rw[n + k]; r2 = c.t_rw[2 * n + k];
+    w0 = c.t_rw[3 * n + k]; w1 = c.t_rw[4 * n + k]; w2 = c.t_rw[5 * n + k];
+  }
+  make_view<CT>(c, L, r0, r1, r2, w0, w1, w2, in.dep, in.ix.w, image_mask(c.d, img), V);
+}
+
 // Raw inputs of one image-major observation, loaded one batch ahead of their use so
 // that the gathers (track point, track factor) overlap the previous batch's arithmetic.
 template <int CT>
@@ -298,59 +342,74 @@ __device__ __forceinline__ void elim_record(const Ctx& c, int64_t e, const ObsVi
   for (int q = 0; q < R / 4; ++q) dst[q] = make_float4(rv[4 * q], rv[4 * q + 1], rv[4 * q + 2], rv[4 * q + 3]);
 }
 
-// Pass "points": per-track Hpp and g_p, and the max |diag(Hpp)|.
+// Pass "points": per-track Hpp and g_p, and the max |diag(Hpp)|.  Persistent warps walk
+// the point tasks with a stride; a short task (<= 32 observations, one per lane) has its
+// inputs loaded while the warp still works on the previous one.
 template <int CT>
 __global__ void __launch_bounds__(128) k_points(Ctx c) {
-  const int task = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  if (task >= c.d.n_pt_tasks) return;                    // warp-uniform
-  const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
-  const int n = ke - kb;
-  float v[9];
-#pragma unroll
-  for (int j = 0; j < 9; ++j) v[j] = 0.f;
+  const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+  int task = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   float wmax = 0.f;
-  if (n <= kWarp) {
-    const bool act = lane < n;
-    int tl = -1 - lane;
-    if (act) {
-      ObsView<CT> V;
-      view_local<CT>(c, kb + lane, V, tl);
-      point_terms<CT>(V, v);
-    }
-    const int tl_prev = __shfl_up_sync(0xffffffffu, tl, 1);
-    const int tl_next = __shfl_down_sync(0xffffffffu, tl, 1);
-    const bool head = act && (lane == 0 || tl_prev != tl);
-    const bool tail = act && (lane == n - 1 || tl_next != tl);
-    const unsigned heads = __ballot_sync(0xffffffffu, head);
-    const unsigned below = heads & ((2u << lane) - 1u);
-    const int seg_start = act ? 31 - __clz(below) : lane;
+  auto task_in = [&](int t, LocIn<CT>& in) {
+    if (t >= c.d.n_pt_tasks) { in.ix = make_int4(0, 0, -1, 0); return; }
+    const int kb = c.d.pt_task[t], n = c.d.pt_task[t + 1] - kb;
+    load_loc_in<CT>(c, kb + lane, n <= kWarp && lane < n, in);
+  };
+  LocIn<CT> nxt;
+  task_in(task, nxt);
+  for (; task < c.d.n_pt_tasks; task += nw) {             // warp-uniform
+    const LocIn<CT> cur = nxt;
+    task_in(task + nw, nxt);
+    const int kb = c.d.pt_task[task], ke = c.d.pt_task[task + 1];
+    const int n = ke - kb;
+    float v[9];
 #pragma unroll
-    for (int j = 0; j < 9; ++j) v[j] = seg_scan(v[j], lane, seg_start);
-    if (tail) {
-      float* t = c.trec + (int64_t)tl * 24;
+    for (int j = 0; j < 9; ++j) v[j] = 0.f;
+    if (n <= kWarp) {
+      const bool act = lane < n;
+      int tl = -1 - lane;
+      if (act) {
+        ObsView<CT> V;
+        view_loc<CT>(c, kb + lane, cur, V);
+        tl = cur.ix.z;
+        point_terms<CT>(V, v);
+      }
+      const int tl_prev = __shfl_up_sync(0xffffffffu, tl, 1);
+      const int tl_next = __shfl_down_sync(0xffffffffu, tl, 1);
+      const bool head = act && (lane == 0 || tl_prev != tl);
+      const bool tail = act && (lane == n - 1 || tl_next != tl);
+      const unsigned heads = __ballot_sync(0xffffffffu, head);
+      const unsigned below = heads & ((2u << lane) - 1u);
+      const int seg_start = act ? 31 - __clz(below) : lane;
 #pragma unroll
-      for (int j = 0; j < 9; ++j) t[j] = v[j];
-      wmax = fmaxf(v[0], fmaxf(v[3], v[5]));
-    }
-  } else {                                               // one long track, in rounds
-    const int tl = c.d.trk_t[kb];
-    for (int k = kb + lane; k < ke; k += kWarp) {
-      ObsView<CT> V;
-      int tl_k;
-      view_local<CT>(c, k, V, tl_k);
-      float u[9];
-      point_terms<CT>(V, u);
+      for (int j = 0; j < 9; ++j) v[j] = seg_scan(v[j], lane, seg_start);
+      if (tail) {
+        float* t = c.trec + (int64_t)tl * 24;
 #pragma unroll
-      for (int j = 0; j < 9; ++j) v[j] += u[j];
-    }
+        for (int j = 0; j < 9; ++j) t[j] = v[j];
+        wmax = fmaxf(wmax, fmaxf(v[0], fmaxf(v[3], v[5])));
+      }
+    } else {                                             // one long track, in rounds
+      const int tl = c.d.trk_t[kb];
+      for (int k = kb + lane; k < ke; k += kWarp) {
+        LocIn<CT> in;
+        load_loc_in<CT>(c, k, true, in);
+        ObsView<CT> V;
+        view_loc<CT>(c, k, in, V);
+        float u[9];
+        point_terms<CT>(V, u);
 #pragma unroll
-    for (int j = 0; j < 9; ++j) v[j] = warp_sum(v[j]);
-    if (lane == 0) {
-      float* t = c.trec + (int64_t)tl * 24;
+        for (int j = 0; j < 9; ++j) v[j] += u[j];
+      }
 #pragma unroll
-      for (int j = 0; j < 9; ++j) t[j] = v[j];
-      wmax = fmaxf(v[0], fmaxf(v[3], v[5]));
+      for (int j = 0; j < 9; ++j) v[j] = warp_sum(v[j]);
+      if (lane == 0) {
+        float* t = c.trec + (int64_t)tl * 24;
+#pragma unroll
+        for (int j = 0; j < 9; ++j) t[j] = v[j];
+        wmax = fmaxf(wmax, fmaxf(v[0], fmaxf(v[3], v[5])));
+      }
     }
   }
   wmax = warp_max(wmax);
@@ -656,9 +715,11 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
   const int nit = (int)((pe - pb + 31) >> 5);
   const int2* __restrict__ pairs = reinterpret_cast<const int2*>(c.d.pairs);
   int* sidx = reinterpret_cast<int*>(sm + pair_warp_floats<CT>() - 64);
+  // Idle lanes of the last step repeat the task's last pair (a line the step copies anyway:
+  // no shared hot spot); steps past the end copy nothing.
   auto load_kk = [&](int j) -> int2 {
     const int64_t p = pb + lane + 32 * (int64_t)j;
-    return (j < nit && p < pe) ? __ldg(pairs + p) : make_int2(-1, -1);
+    return j < nit ? __ldg(pairs + (p < pe ? p : pe - 1)) : make_int2(0, 0);
   };
   // Copy the records of step j (pair indices kk, one pair per lane) into its buffer:
   // piece g = lane + 32 m of the step is part g % Q of record g / Q (record 2 q + side is
@@ -668,7 +729,9 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
     reinterpret_cast<int2*>(sidx)[lane] = kk;
     __syncwarp();
     float* dst = sm + (j % kPairStages) * STAGE;
-    if constexpr (32 % Q == 0 && Q <= 16) {
+    if (j >= nit) {
+      // nothing to copy
+    } else if constexpr (32 % Q == 0 && Q <= 16) {
       // lane-constant part and record parity; the record advances by 32/Q per piece round
       constexpr int RPM = 32 / Q;
       const int r0 = lane / Q, part = lane % Q;
@@ -676,16 +739,14 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
       const float* s0 = c.rec + 4 * part;
 #pragma unroll
       for (int m = 0; m < 2 * Q; ++m) {
-        const int k = sidx[r0 + RPM * m];
-        if (k >= 0) cp_async16(d0 + (RPM / 2) * m * SLOT, s0 + (int64_t)k * R);
+        cp_async16(d0 + (RPM / 2) * m * SLOT, s0 + (int64_t)sidx[r0 + RPM * m] * R);
       }
     } else {
 #pragma unroll 4
       for (int m = 0; m < 2 * Q; ++m) {
         const int g = lane + 32 * m;
         const int r = g / Q, part = g - r * Q;
-        const int k = sidx[r];
-        if (k >= 0) cp_async16(dst + (r >> 1) * SLOT + (r & 1) * R + 4 * part, c.rec + (int64_t)k * R + 4 * part);
+        cp_async16(dst + (r >> 1) * SLOT + (r & 1) * R + 4 * part, c.rec + (int64_t)sidx[r] * R + 4 * part);
       }
     }
     cp_async_commit();   // one group per step, empty past the end: uniform group counting
@@ -744,9 +805,15 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
         }
       }
 #pragma unroll
-      for (int b = B0; b < B1; ++b) {      // base rows
+      for (int b = B0; b < B1; ++b) {      // base rows, their record values read four rows at a time
         const int a = b - A0;
-        const float t0 = buf[b], t1 = buf[8 + b], t2 = buf[16 + b];
+        const float4 g0 = *reinterpret_cast<const float4*>(buf + (b & ~3));
+        const float4 g1 = *reinterpret_cast<const float4*>(buf + 8 + (b & ~3));
+        const float4 g2 = *reinterpret_cast<const float4*>(buf + 16 + (b & ~3));
+        const int l = b & 3;
+        const float t0 = l == 0 ? g0.x : (l == 1 ? g0.y : (l == 2 ? g0.z : g0.w));
+        const float t1 = l == 0 ? g1.x : (l == 1 ? g1.y : (l == 2 ? g1.z : g1.w));
+        const float t2 = l == 0 ? g2.x : (l == 1 ? g2.y : (l == 2 ? g2.z : g2.w));
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           acc[a][q] = __ffma2_rn(make_float2(t0, t0), yc[0][q], acc[a][q]);
@@ -1030,7 +1097,18 @@ int make_ctx(b3r_plan* plan, const b3r_params* p, const b3r_lin_opts* o, void* w
 template <int CT>
 int launch_points(const Ctx& c, cudaStream_t s) {
   if (c.d.n_pt_tasks == 0) return B3R_OK;
-  k_points<CT><<<grid_for((int64_t)c.d.n_pt_tasks * 32, 128), 128, 0, s>>>(c);
+  // persistent: one full wave of resident blocks, each warp walking tasks with a stride
+  static int per_sm = 0, n_sm = 0;           // one occupancy query per instantiation
+  if (per_sm == 0) {
+    int dev = 0;
+    B3R_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+    B3R_TRY(check_cuda(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev), "SM count"));
+    B3R_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_points<CT>, 128, 0),
+                       "points occupancy"));
+    per_sm = std::max(per_sm, 1);
+  }
+  const int blocks = (int)std::min<int64_t>(grid_for((int64_t)c.d.n_pt_tasks * 32, 128), (int64_t)per_sm * n_sm);
+  k_points<CT><<<blocks, 128, 0, s>>>(c);
   return check_launch("points pass");
 }
 
