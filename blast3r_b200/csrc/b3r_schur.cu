@@ -647,7 +647,6 @@ __global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict_
 // rows for C <= 5; larger C splits the rows over `pair_roles` warps that each stream the
 // task); the lane partials are summed through shared memory at the end of the task, one
 // atomic per value.
-constexpr int kPairWarps = 1;    // independent warps (tasks) per CTA: one, so a finished task frees its slot
 constexpr int kPairStages = 3;   // cp.async ring depth per lane
 
 // 16-byte asynchronous global -> shared copies (cp.async, completion by commit groups)
@@ -679,30 +678,64 @@ __device__ __forceinline__ void emit_pair_value(const Ctx& c, float* __restrict_
   }
 }
 
-// Warps that split the 8+C product rows: a lane holds at most ~170 accumulators.
+// Warps that split the 8+C product rows of a pair task (at most ~100 accumulators per
+// lane), all of them reading the same staged records.
+#ifndef B3R_PAIR_ACC_MAX
+#define B3R_PAIR_ACC_MAX 170   // accumulators per lane that set the number of row roles
+#endif
 template <int CT> __host__ __device__ constexpr int pair_roles() {
-  return CT <= 5 ? 1 : (CT <= 8 ? 2 : ((8 + CT) * (8 + CT) + 119) / 120);
+  return ((8 + CT) * (8 + CT) + B3R_PAIR_ACC_MAX - 1) / B3R_PAIR_ACC_MAX;
 }
-template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() { return r * (8 + CT) / NR; }
+// Issue cost of product row a per pair: a base row ~18 instructions, a depth row ~8, plus
+// ~15 for the z-scale products shared by the depth rows (charged to the first of them).
+__host__ __device__ constexpr int pair_row_cost(int a) { return a < 8 ? 18 : (a == 8 ? 23 : 8); }
+// First row of role r: the rows are cut where the cumulative cost crosses r/NR of the total.
+template <int CT, int NR, int r> __host__ __device__ constexpr int role_row() {
+  constexpr int W = 8 + CT;
+  if (r <= 0) return 0;
+  if (r >= NR) return W;
+  int total = 0;
+  for (int a = 0; a < W; ++a) total += pair_row_cost(a);
+  const int target = r * total / NR;
+  int cum = 0, best = 1;
+  for (int a = 1; a <= W; ++a) {
+    const int prev = cum;
+    cum += pair_row_cost(a - 1);
+    if (cum >= target) { best = (cum - target <= target - prev) ? a : a - 1; break; }
+  }
+  best = best < r ? r : best;                       // every role keeps at least one row
+  return best > W - (NR - r) ? W - (NR - r) : best;
+}
+template <int CT, int NR, int r> __host__ __device__ constexpr int role_rows_max() {
+  if constexpr (r >= NR) {
+    return 0;
+  } else {
+    constexpr int n = role_row<CT, NR, r + 1>() - role_row<CT, NR, r>();
+    constexpr int m = role_rows_max<CT, NR, r + 1>();
+    return n > m ? n : m;
+  }
+}
 template <int CT> __host__ __device__ constexpr int pair_slot_floats() { return 2 * rec_floats<CT>() + 4; }
-template <int CT> __host__ __device__ constexpr int pair_max_rows() {
-  return (8 + CT + pair_roles<CT>() - 1) / pair_roles<CT>();
+// shared memory of a pair CTA: kPairStages step buffers (reused by the per-warp epilogue
+// transposes), then 64 staged record indices per warp
+template <int CT> __host__ __device__ constexpr int pair_stage_area() {
+  constexpr int NR = pair_roles<CT>();
+  constexpr int st = kPairStages * 32 * pair_slot_floats<CT>();
+  constexpr int ep = NR * role_rows_max<CT, NR, 0>() * (8 + CT) * 33;
+  return ((st > ep ? st : ep) + 3) & ~3;
 }
-// per warp: kPairStages step buffers (reused by the epilogue), then 64 staged record
-// indices; a multiple of 4 floats so every warp's region starts 16-byte aligned
-template <int CT> __host__ __device__ constexpr int pair_warp_floats() {
-  return (((kPairStages * 32 * pair_slot_floats<CT>() > pair_max_rows<CT>() * (8 + CT) * 33
-                ? kPairStages * 32 * pair_slot_floats<CT>()
-                : pair_max_rows<CT>() * (8 + CT) * 33) + 3) & ~3) + 64;
+template <int CT> __host__ __device__ constexpr int pair_smem_floats() {
+  return pair_stage_area<CT>() + 64 * pair_roles<CT>();
 }
 
-// Rows [A0, A1) of one pair task, run by one warp over its private shared region `sm`.
-// The products are accumulated with packed float2 FMAs (two neighbouring columns per
-// instruction): row a < 8 of Y_o^T Y_o' is sum_r Y_o[r][a] * Y_o'[r][0..7] plus the depth
-// columns u_a * dep', u_a = sum_r Y_o[r][a] zs'[r]; a depth row is dep[ch] * (zs^T Y_o')
-// plus dep[ch] * (zs^T zs') * dep'.
-template <int CT, int A0, int A1>
-__device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, int64_t task, float* sm) {
+// Rows [A0, A1) (role `role` of NR) of one pair task.  `stg` is the CTA's step buffers,
+// `sidx` this warp's 64 staged record indices.  The products are accumulated with packed
+// float2 FMAs (two neighbouring columns per instruction): row a < 8 of Y_o^T Y_o' is
+// sum_r Y_o[r][a] * Y_o'[r][0..7] plus the depth columns u_a * dep', u_a = sum_r
+// Y_o[r][a] zs'[r]; a depth row is dep[ch] * (zs^T Y_o') plus dep[ch] * (zs^T zs') * dep'.
+template <int CT, int A0, int A1, int NR>
+__device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, int64_t task, float* stg, int* sidx,
+                                          int role) {
   constexpr int R = rec_floats<CT>(), SLOT = pair_slot_floats<CT>(), Q = R / 4, ZS = rec_zs<CT>();
   constexpr int W = 8 + CT, NA = A1 - A0;
   constexpr int NZ2 = CT / 2, ODD = CT & 1, NC2 = 4 + NZ2;   // float2 columns per row
@@ -714,21 +747,22 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
   const int64_t pb = c.d.task_pb[task], pe = c.d.task_pe[task];
   const int nit = (int)((pe - pb + 31) >> 5);
   const int2* __restrict__ pairs = reinterpret_cast<const int2*>(c.d.pairs);
-  int* sidx = reinterpret_cast<int*>(sm + pair_warp_floats<CT>() - 64);
   // Idle lanes of the last step repeat the task's last pair (a line the step copies anyway:
   // no shared hot spot); steps past the end copy nothing.
   auto load_kk = [&](int j) -> int2 {
     const int64_t p = pb + lane + 32 * (int64_t)j;
     return j < nit ? __ldg(pairs + (p < pe ? p : pe - 1)) : make_int2(0, 0);
   };
-  // Copy the records of step j (pair indices kk, one pair per lane) into its buffer:
+  // Copy this role's share of the records of step j (pair indices kk, one pair per lane):
   // piece g = lane + 32 m of the step is part g % Q of record g / Q (record 2 q + side is
-  // side `side` of pair q), so consecutive lanes read consecutive 16 bytes of a record.
+  // side `side` of pair q), so consecutive lanes read consecutive 16 bytes of a record;
+  // role w copies the piece rounds m in [M0, M1).
   auto stage = [&](int j, int2 kk) {
-    __syncwarp();                        // every lane is done with the buffer and the indices
+    __syncwarp();                        // this warp is done with its previous indices
     reinterpret_cast<int2*>(sidx)[lane] = kk;
     __syncwarp();
-    float* dst = sm + (j % kPairStages) * STAGE;
+    float* dst = stg + (j % kPairStages) * STAGE;
+    const int M0 = role * 2 * Q / NR, M1 = (role + 1) * 2 * Q / NR;
     if (j >= nit) {
       // nothing to copy
     } else if constexpr (32 % Q == 0 && Q <= 16) {
@@ -737,13 +771,11 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
       const int r0 = lane / Q, part = lane % Q;
       float* d0 = dst + (r0 >> 1) * SLOT + (r0 & 1) * R + 4 * part;
       const float* s0 = c.rec + 4 * part;
-#pragma unroll
-      for (int m = 0; m < 2 * Q; ++m) {
-        cp_async16(d0 + (RPM / 2) * m * SLOT, s0 + (int64_t)sidx[r0 + RPM * m] * R);
-      }
+#pragma unroll 4
+      for (int m = M0; m < M1; ++m) cp_async16(d0 + (RPM / 2) * m * SLOT, s0 + (int64_t)sidx[r0 + RPM * m] * R);
     } else {
 #pragma unroll 4
-      for (int m = 0; m < 2 * Q; ++m) {
+      for (int m = M0; m < M1; ++m) {
         const int g = lane + 32 * m;
         const int r = g / Q, part = g - r * Q;
         cp_async16(dst + (r >> 1) * SLOT + (r & 1) * R + 4 * part, c.rec + (int64_t)sidx[r] * R + 4 * part);
@@ -763,25 +795,41 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
   stage(1, load_kk(1));
   int2 kk_next = load_kk(2);
   for (int j = 0; j < nit; ++j) {
+    cp_async_wait<kPairStages - 2>();     // this thread's copies of step j have landed
+    // every role's copies of step j are visible, and every role is done with step j-1,
+    // whose buffer step j+2 reuses
+    if constexpr (NR > 1) __syncthreads(); else __syncwarp();
     stage(j + 2, kk_next);
     kk_next = load_kk(j + 3);
-    cp_async_wait<kPairStages - 1>();     // this lane's copies of step j have landed
-    __syncwarp();                         // ... and every other lane's
     if (pb + lane + 32 * (int64_t)j < pe) {
-      const float* buf = sm + (j % kPairStages) * STAGE + lane * SLOT;
-      const float2* pc2 = reinterpret_cast<const float2*>(buf + R);
-      float2 yc[3][4];                    // column record, Y'[r][2q .. 2q+1]
+      const float* buf = stg + (j % kPairStages) * STAGE + lane * SLOT;
+      // column record through 16-byte reads, split into register pairs
+      float cv[R];
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(buf + R + 4 * q);
+        cv[4 * q] = v.x; cv[4 * q + 1] = v.y; cv[4 * q + 2] = v.z; cv[4 * q + 3] = v.w;
+      }
+      float2 yc[3][4];                    // Y'[r][2q .. 2q+1]
 #pragma unroll
       for (int r = 0; r < 3; ++r)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) yc[r][q] = pc2[4 * r + q];
+        for (int q = 0; q < 4; ++q) yc[r][q] = make_float2(cv[8 * r + 2 * q], cv[8 * r + 2 * q + 1]);
       float2 dc[NZ2 > 0 ? NZ2 : 1];       // column depth channels, paired
 #pragma unroll
-      for (int q = 0; q < NZ2; ++q) dc[q] = pc2[12 + q];
-      const float dco = ODD ? buf[R + 24 + CT - 1] : 0.f;
-      const float zc0 = buf[R + ZS], zc1 = buf[R + ZS + 1], zc2 = buf[R + ZS + 2];
+      for (int q = 0; q < NZ2; ++q) dc[q] = make_float2(cv[24 + 2 * q], cv[24 + 2 * q + 1]);
+      const float dco = ODD ? cv[24 + CT - 1] : 0.f;
+      const float zc0 = cv[ZS], zc1 = cv[ZS + 1], zc2 = cv[ZS + 2];
       if constexpr (Z1 > 0) {             // depth rows: dep[ch] * (zs^T Y'), dep[ch] * sz * dep'
-        const float zr0 = buf[ZS], zr1 = buf[ZS + 1], zr2 = buf[ZS + 2];
+        float rv[8];                      // row record floats 24..31: depth channels, z-scale column
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(buf + 24 + 4 * q);
+          rv[4 * q] = v.x; rv[4 * q + 1] = v.y; rv[4 * q + 2] = v.z; rv[4 * q + 3] = v.w;
+        }
+        const float zr0 = ZS + 2 < 32 ? rv[(ZS - 24) & 7] : buf[ZS];
+        const float zr1 = ZS + 2 < 32 ? rv[(ZS + 1 - 24) & 7] : buf[ZS + 1];
+        const float zr2 = ZS + 2 < 32 ? rv[(ZS + 2 - 24) & 7] : buf[ZS + 2];
         float2 qz[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -793,7 +841,7 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
 #pragma unroll
         for (int z = Z0; z < Z1; ++z) {
           const int a = 8 + z - A0;
-          const float dr = buf[24 + z];
+          const float dr = 24 + z < 32 ? rv[z & 7] : buf[24 + z];
           const float2 d2 = make_float2(dr, dr);
 #pragma unroll
           for (int q = 0; q < 4; ++q) acc[a][q] = __ffma2_rn(d2, qz[q], acc[a][q]);
@@ -829,9 +877,11 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
     }
   }
   cp_async_wait<0>();
-  __syncwarp();
-  // epilogue: transpose the lane partials through shared memory (stride 33: conflict-free),
-  // then each lane sums values lane, lane+32, ... over the 32 lanes and emits them
+  if constexpr (NR > 1) __syncthreads(); else __syncwarp();   // step buffers free for the epilogue
+  // epilogue: transpose the lane partials through this role's part of the step buffers
+  // (stride 33: conflict-free), then each lane sums values lane, lane+32, ... over the 32
+  // lanes and emits them
+  float* sm = stg + role * (role_rows_max<CT, NR, 0>() * W * 33);
 #pragma unroll
   for (int a = 0; a < NA; ++a) {
 #pragma unroll
@@ -850,24 +900,23 @@ __device__ __forceinline__ void pair_task(const Ctx& c, float* __restrict__ S, i
   }
 }
 
+
 template <int CT, int NR, int r>
-__device__ __forceinline__ void pair_role_dispatch(const Ctx& c, float* S, int64_t task, int role, float* sm) {
+__device__ __forceinline__ void pair_role_dispatch(const Ctx& c, float* S, int64_t task, int role, float* stg,
+                                                   int* sidx) {
   if constexpr (r < NR) {
-    if (role == r) pair_task<CT, role_row<CT, NR, r>(), role_row<CT, NR, r + 1>()>(c, S, task, sm);
-    else pair_role_dispatch<CT, NR, r + 1>(c, S, task, role, sm);
+    if (role == r) pair_task<CT, role_row<CT, NR, r>(), role_row<CT, NR, r + 1>(), NR>(c, S, task, stg, sidx, role);
+    else pair_role_dispatch<CT, NR, r + 1>(c, S, task, role, stg, sidx);
   }
 }
 
-// grid (ceil(n_tasks / kPairWarps), pair_roles): warp w of block x runs task x*kPairWarps+w,
-// output rows of role blockIdx.y
+// One CTA per pair task (tasks longest first), one warp per row role.
 template <int CT>
-__global__ void __launch_bounds__(kPairWarps * 32) k_pairs(Ctx c, float* __restrict__ S) {
+__global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* __restrict__ S) {
   extern __shared__ __align__(16) float sm_dyn[];
-  const int warp = threadIdx.x >> 5;
-  const int64_t task = (int64_t)blockIdx.x * kPairWarps + warp;
-  if (task >= c.d.n_tasks) return;                       // warp-uniform
-  float* sm = sm_dyn + warp * pair_warp_floats<CT>();
-  pair_role_dispatch<CT, pair_roles<CT>(), 0>(c, S, task, (int)blockIdx.y, sm);
+  const int role = threadIdx.x >> 5;
+  int* sidx = reinterpret_cast<int*>(sm_dyn + pair_stage_area<CT>()) + 64 * role;
+  pair_role_dispatch<CT, pair_roles<CT>(), 0>(c, S, (int64_t)blockIdx.x, role, sm_dyn, sidx);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1127,15 +1176,14 @@ int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) 
 
 template <int CT>
 int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
-  const size_t smem = (size_t)kPairWarps * pair_warp_floats<CT>() * sizeof(float);
+  const size_t smem = (size_t)pair_smem_floats<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
   if (!configured) {
     B3R_TRY(check_cuda(cudaFuncSetAttribute(k_pairs<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "pairs smem attribute"));
     configured = true;
   }
-  const dim3 grid((unsigned)((c.d.n_tasks + kPairWarps - 1) / kPairWarps), (unsigned)pair_roles<CT>());
-  k_pairs<CT><<<grid, kPairWarps * 32, smem, s>>>(c, S);
+  k_pairs<CT><<<(unsigned)c.d.n_tasks, pair_roles<CT>() * 32, smem, s>>>(c, S);
   return check_launch("pairs pass");
 }
 
