@@ -210,29 +210,27 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
   Jpc[3] = 0; Jpc[4] = fy * inv_z; Jpc[5] = cy * inv_z - P1 * inv_z2;
   Jpc[6] = 0; Jpc[7] = 0;          Jpc[8] = -fbar * inv_z;
   Jpc[0] /= sx; Jpc[2] /= sx; Jpc[4] /= sy; Jpc[5] /= sy;
-  T Jr[9];   // J_proj_rig = Jpc @ R_cr
+  // J_proj_rig = Jpc @ R_cr, skipping the structural zeros of Jpc (entries 1, 3, 6, 7):
+  // the same value as the dense product (adding 0 or 0 * x changes no finite sum)
+  T Jr[9];
 #pragma unroll
-  for (int r = 0; r < 3; ++r)
+  for (int c = 0; c < 3; ++c) {
+    Jr[c] = Jpc[0] * cam.R_cr[c] + Jpc[2] * cam.R_cr[6 + c];
+    Jr[3 + c] = Jpc[4] * cam.R_cr[3 + c] + Jpc[5] * cam.R_cr[6 + c];
+    Jr[6 + c] = Jpc[8] * cam.R_cr[6 + c];
+  }
+  // J_tau = Jr @ [-[X_r]x , I] (columns 0..2 rotation, 3..5 translation), written out
+  // term by term without the zero and unit entries of the generator matrix
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      T s = 0;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) s += Jpc[3 * r + k] * cam.R_cr[3 * k + c];
-      Jr[3 * r + c] = s;
-    }
-  // J_tau = Jr @ [-[X_r]x , I]   (columns 0..2 rotation, 3..5 translation)
-  const T Jrt[18] = {0,       X_r[2],  -X_r[1], 1, 0, 0,
-                     -X_r[2], 0,       X_r[0],  0, 1, 0,
-                     X_r[1],  -X_r[0], 0,       0, 0, 1};
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 6; ++c) {
-      T s = 0;
-#pragma unroll
-      for (int k = 0; k < 3; ++k) s += Jr[3 * r + k] * Jrt[6 * k + c];
-      L.Jt[6 * r + c] = s;
-    }
+  for (int r = 0; r < 3; ++r) {
+    const T j0 = Jr[3 * r], j1 = Jr[3 * r + 1], j2 = Jr[3 * r + 2];
+    L.Jt[6 * r + 0] = j1 * (-X_r[2]) + j2 * X_r[1];
+    L.Jt[6 * r + 1] = j0 * X_r[2] + j2 * (-X_r[0]);
+    L.Jt[6 * r + 2] = j0 * (-X_r[1]) + j1 * X_r[0];
+    L.Jt[6 * r + 3] = j0;
+    L.Jt[6 * r + 4] = j1;
+    L.Jt[6 * r + 5] = j2;
+  }
 #pragma unroll
   for (int r = 0; r < 3; ++r)
 #pragma unroll

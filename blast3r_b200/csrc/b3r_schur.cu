@@ -107,6 +107,11 @@ struct ObsView {
   float dep[CT];    // depth channels as used by J (optim_Z0 / optim_Z_1st_cam applied)
 };
 
+// Structural non-zeros of the reduced camera Jacobian: row 0 (x) has fx and tau, row 1 (y)
+// fy and tau, row 2 (depth) every column.  Products skip the zero entries (the same values
+// as the dense products for finite inputs).
+__host__ __device__ constexpr bool jc_nz(int i, int a) { return i == 2 || (a >= 2 && a < 8) || a == i; }
+
 // Masks of the image's blocks: bit 0 foc, 1 tau, 2 zcf active.
 __device__ __forceinline__ int image_mask(const DevPlan& d, int img) {
   return (d.img_bk[3 * img] >= 0 ? 1 : 0) | (d.img_bk[3 * img + 1] >= 0 ? 2 : 0) |
@@ -324,8 +329,12 @@ __device__ __forceinline__ void elim_record(const Ctx& c, int64_t e, const ObsVi
   for (int a = 0; a < 9; ++a) {
     float h[3];
 #pragma unroll
-    for (int j = 0; j < 3; ++j)
-      h[j] = fmaf(V.Jpw[6 + j], V.Jcw[18 + a], fmaf(V.Jpw[3 + j], V.Jcw[9 + a], V.Jpw[j] * V.Jcw[a]));
+    for (int j = 0; j < 3; ++j) {
+      float s = V.Jpw[6 + j] * V.Jcw[18 + a];
+      if (jc_nz(1, a)) s = fmaf(V.Jpw[3 + j], V.Jcw[9 + a], s);
+      if (jc_nz(0, a)) s = fmaf(V.Jpw[j], V.Jcw[a], s);
+      h[j] = s;
+    }
     const float y0 = h[0] * li[0];
     const float y1 = (h[1] - li[1] * y0) * li[3];
     const float y2 = (h[2] - li[2] * y0 - li[4] * y1) * li[5];
@@ -468,17 +477,19 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
   for (int a = 0; a < 9; ++a)
 #pragma unroll
     for (int b = a; b < 9; ++b) {
-      float s = 0.f;
+      float s = V.Jcw[18 + a] * V.Jcw[18 + b];
 #pragma unroll
-      for (int i = 0; i < 3; ++i) s += V.Jcw[9 * i + a] * V.Jcw[9 * i + b];
+      for (int i = 1; i >= 0; --i)
+        if (jc_nz(i, a) && jc_nz(i, b)) s = fmaf(V.Jcw[9 * i + a], V.Jcw[9 * i + b], s);
       H[a][b] = s;
     }
   float g[9];
 #pragma unroll
   for (int a = 0; a < 9; ++a) {
-    float s = 0.f;
+    float s = V.Jcw[18 + a] * V.sWr[2];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) s += V.Jcw[9 * i + a] * V.sWr[i];
+    for (int i = 1; i >= 0; --i)
+      if (jc_nz(i, a)) s = fmaf(V.Jcw[9 * i + a], V.sWr[i], s);
     g[a] = s;
   }
   // undamped diag(A) = diag(Hcc)
@@ -537,7 +548,7 @@ constexpr int kDiagThreads = 64;   // two warps per image chunk
 // free), and each lane keeps running sums of values lane, lane+32, lane+64, ... only, so
 // the 8+C..117 values never sit in every thread's registers across observations.
 template <int CT>
-__global__ void __launch_bounds__(kDiagThreads) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
+__global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
                                                        float* __restrict__ diagA) {
   using Lay = DiagLayout<CT>;
   constexpr int NW = kDiagThreads / kWarp;
