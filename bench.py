@@ -235,7 +235,7 @@ def run_b200(args):
     clocks = clk.summary()
 
     # per-pass device time on this rank (same workload, events between the launches)
-    names = ['prep', 'points', 'eliminate', 'diag', 'pairs', 'finalize']
+    names = ['prep', 'points', 'factor', 'diag', 'pairs', 'finalize']
     acc = {k: 0.0 for k in names}
     R = 5
     s = torch.cuda.current_stream().cuda_stream
@@ -247,7 +247,7 @@ def run_b200(args):
             if nm == 'finalize':
                 plan.lin_stage('finalize', p, lo, outs)
             else:
-                pas = dict(prep=L.PASS_PREP, points=L.PASS_POINTS, eliminate=L.PASS_ELIMINATE, diag=L.PASS_DIAG,
+                pas = dict(prep=L.PASS_PREP, points=L.PASS_POINTS, factor=L.PASS_FACTOR, diag=L.PASS_DIAG,
                            pairs=L.PASS_PAIRS)[nm]
                 plan.lin_pass(pas, p, lo, outs)
             ev[j + 1].record()
@@ -325,7 +325,7 @@ def run_b200(args):
         fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
         roof = {'bound': 'hbm', 'achieved': round(achieved, 2), 'peak': peak, 'unit': 'GB/s',
                 'frac': round(achieved / peak, 4), 'traffic': read_traffic(args.config, world),
-                'kernel': 'fused linearization step (prep, points, eliminate, diag, pairs, finalize)',
+                'kernel': 'fused linearization step (prep, points, factor, diag, pairs, finalize)',
                 'algorithmic_bytes_per_step': int(B), 'peak_kind': f'of {peak_kind}',
                 'fp32': {'flops_per_step': flops, 'achieved_tflops': round(flops / (ms_step * 1e-3) / 1e12, 2),
                          'peak_tflops_at_median_clock': round(fp32_peak, 1),
@@ -341,7 +341,7 @@ def run_b200(args):
                            'l2': 'inputs larger than L2 (observation arrays ~260 MB), no flush'},
                 'roofline': roof, 'clocks': clocks,
                 'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
-                'gpu_launches': 7 * args.steps}   # prep, points, eliminate, diag, pairs, fin_max, fin_apply (rank 0)
+                'gpu_launches': 7 * args.steps}   # prep, points, factor, diag, pairs, fin_max, fin_apply (rank 0)
         if lm_info is not None:
             line['ms_per_lm_iteration'] = lm_info
         if world == 1 and not args.no_cpu_baseline:

@@ -12,7 +12,8 @@ LIB_PATH = os.path.join(_HERE, 'libb3r.so')
 B3R_OK = 0
 B3R_F32, B3R_F64 = 0, 1
 ENABLE_ALL, ENABLE_ZERO, ENABLE_MASK = 0, 1, 2
-PASS_PREP, PASS_POINTS, PASS_ELIMINATE, PASS_DIAG, PASS_PAIRS = 0, 1, 2, 3, 4
+PASS_PREP, PASS_POINTS, PASS_FACTOR, PASS_DIAG, PASS_PAIRS = 0, 1, 2, 3, 4
+PASS_ELIMINATE = PASS_FACTOR   # former name
 
 _i32, _i64, _f32, _f64, _vp = C.c_int32, C.c_int64, C.c_float, C.c_double, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)

@@ -324,15 +324,23 @@ static int build_pairs(PlanBuild& B) {
   }
   for (const int2& pr : B.pairs)
     B3R_REQUIRE(pr.x >= 0 && pr.y >= 0, "internal: pair observation without an image-major slot");
-  // Tasks: segments cut into <= kPairTask pairs, issued longest first so the short ones
-  // fill in behind them (the pair lists stay in segment order; a task is a (segment, range)).
+  // Tasks: segments cut into <= kPairTask pairs, in segment order (row image major) so that
+  // the records of a row image and of its window of partner images stay in L2 while its
+  // tasks run; within one row image the longest tasks go first so the short ones fill in
+  // behind them.  The pair lists stay in segment order; a task is a (segment, range).
   std::vector<std::pair<int64_t, int64_t>> cuts;   // (first pair, segment)
   for (int64_t s = 0; s < S; ++s)
     for (int64_t p = B.seg_cnt[s]; p < B.seg_cnt[s + 1]; p += kPairTask) cuts.emplace_back(p, s);
   std::vector<int64_t> ord(cuts.size());
   std::iota(ord.begin(), ord.end(), 0);
   auto len = [&](int64_t t) { return std::min<int64_t>(B.seg_cnt[cuts[t].second + 1] - cuts[t].first, kPairTask); };
-  std::stable_sort(ord.begin(), ord.end(), [&](int64_t a, int64_t b) { return len(a) > len(b); });
+  std::vector<int> row_of_seg(S);
+  for (int i = 0; i + 1 < (int)B.seg_row_ptr.size(); ++i)
+    for (int s2 = B.seg_row_ptr[i]; s2 < B.seg_row_ptr[i + 1]; ++s2) row_of_seg[s2] = i;
+  std::stable_sort(ord.begin(), ord.end(), [&](int64_t a, int64_t b) {
+    const int ra = row_of_seg[cuts[a].second], rb = row_of_seg[cuts[b].second];
+    return ra != rb ? ra < rb : len(a) > len(b);
+  });
   B.task_pb.resize(cuts.size() + 1);
   B.task_pe.resize(cuts.size());
   B.task_seg.resize(cuts.size());

@@ -209,7 +209,7 @@ class BAPlan:
         return torch.from_numpy(D).to(S_vals.device)
 
     def lin_pass(self, pass_id, params, opts, outputs, stream=None):
-        """One pass (b3r_lin_pass): PASS_PREP/POINTS/ELIMINATE/DIAG/PAIRS of _lib."""
+        """One pass (b3r_lin_pass): PASS_PREP/POINTS/FACTOR/DIAG/PAIRS of _lib, in that order."""
         S, b, dA, pc, hm = outputs
         out = L.Outputs(S_vals=S.data_ptr(), b=b.data_ptr(), diagA=dA.data_ptr(),
                         precond=pc.data_ptr() if pc is not None else None, hpp_max=hm.data_ptr())

@@ -239,7 +239,8 @@ int b3r_linearize_schur_noalloc(b3r_plan* plan, const b3r_params* params, const 
  * blocks needs the max over ALL tracks: sharded callers all-reduce it before stage 2). */
 int b3r_lin_points(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
                    void* workspace, const b3r_outputs* out, void* stream);
-/* Stage 2: point elimination, per-image diagonal blocks, pair products, b and diag(A).
+/* Stage 2: per-track factors, elimination records with the per-image diagonal blocks,
+ * pair products, b and diag(A).
  * Zeroes and accumulates out->S_vals, out->b, out->diagA (partial sums on each rank). */
 int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,
                      void* workspace, const b3r_outputs* out, void* stream);
@@ -249,12 +250,16 @@ int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
                      const b3r_outputs* out, void* stream);
 
 /* One pass of b3r_lin_points/b3r_lin_assemble on its own (profiling and custom
- * pipelines): B3R_PASS_PREP (per-image records), _POINTS, _ELIMINATE, _DIAG, _PAIRS.
- * Outputs are NOT zeroed here; the caller keeps the order prep, points, eliminate, then
- * diag and pairs on zeroed S_vals / b / diagA. */
+ * pipelines): B3R_PASS_PREP (per-image records), _POINTS (per-track Hpp, g_p), _FACTOR
+ * (damped per-track Cholesky factors), _DIAG (elimination records and per-image diagonal
+ * blocks, b, diag(A)), _PAIRS (off-diagonal pair products, which read the records _DIAG
+ * writes).  Outputs are NOT zeroed here; the caller keeps the order prep, points, factor,
+ * diag, pairs on zeroed S_vals / b / diagA.  B3R_PASS_ELIMINATE is the former name of
+ * B3R_PASS_FACTOR (same value). */
 #define B3R_PASS_PREP 0
 #define B3R_PASS_POINTS 1
-#define B3R_PASS_ELIMINATE 2
+#define B3R_PASS_FACTOR 2
+#define B3R_PASS_ELIMINATE B3R_PASS_FACTOR
 #define B3R_PASS_DIAG 3
 #define B3R_PASS_PAIRS 4
 int b3r_lin_pass(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts, void* workspace,
