@@ -323,13 +323,27 @@ def run_b200(args):
         flops = fp32_flops(L_t)
         sm_mhz = clocks['sm_mhz'] or 1965.0
         fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
-        roof = {'bound': 'hbm', 'achieved': round(achieved, 2), 'peak': peak, 'unit': 'GB/s',
-                'frac': round(achieved / peak, 4), 'traffic': read_traffic(args.config, world),
-                'kernel': 'fused linearization step (prep, points, factor, diag, pairs, finalize)',
-                'algorithmic_bytes_per_step': int(B), 'peak_kind': f'of {peak_kind}',
-                'fp32': {'flops_per_step': flops, 'achieved_tflops': round(flops / (ms_step * 1e-3) / 1e12, 2),
+        # dominant kernel: the pairs pass (segment-major pair products).  Its compulsory
+        # bytes are every elimination record read once, the pair list, and the S values it
+        # adds to; its time is the live CUDA-event time of the pass on the launch stream.
+        R = int(plan.info.record_floats)
+        pairs_B = 4 * R * int(plan.info.n_obs_local) + 8 * int(plan.info.n_pairs) + 4 * nnz_upper
+        pairs_ms = passes['pairs']['ms']
+        pairs_ach = pairs_B / (pairs_ms * 1e-3) / 1e9
+        pairs_flops = 6.0 * 13 * 13 * int(plan.info.n_pairs)      # dense-equivalent Y_o^T Y_o' (w = 13)
+        roof = {'bound': 'hbm', 'kernel': f"k_pairs (pairs pass, {passes['pairs']['share']:.2f} of the step)",
+                'achieved': round(pairs_ach, 2), 'peak': peak, 'unit': 'GB/s', 'frac': round(pairs_ach / peak, 4),
+                'traffic': read_traffic(args.config, world, 'pairs_dram_bytes_per_launch'),
+                'algorithmic_bytes_per_launch': int(pairs_B), 'launch_ms': pairs_ms, 'peak_kind': f'of {peak_kind}',
+                'fp32': {'flops_per_launch': pairs_flops,
+                         'achieved_tflops': round(pairs_flops / (pairs_ms * 1e-3) / 1e12, 2),
                          'peak_tflops_at_median_clock': round(fp32_peak, 1),
-                         'frac': round(flops / (ms_step * 1e-3) / 1e12 / fp32_peak, 4)},
+                         'frac': round(pairs_flops / (pairs_ms * 1e-3) / 1e12 / fp32_peak, 4)},
+                # the whole linearization step against HBM (bytes per observation x observations)
+                'step': {'achieved': round(achieved, 2), 'frac': round(achieved / peak, 4),
+                         'algorithmic_bytes': int(B),
+                         'traffic': read_traffic(args.config, world, 'dram_bytes_per_step'),
+                         'fp32_flops': flops, 'fp32_frac': round(flops / (ms_step * 1e-3) / 1e12 / fp32_peak, 4)},
                 'passes': passes}
         line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'strong',
@@ -353,14 +367,14 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
-def read_traffic(cfg, world):
-    """DRAM bytes per step from the committed ncu summary (profiles/), or None."""
-    path = os.path.join(ROOT, 'profiles', f'traffic_cfg{cfg}.txt')   # measured DRAM bytes of one step
+def read_traffic(cfg, world, key):
+    """DRAM bytes (`key`) from the committed ncu summary profiles/traffic_cfg<cfg>.txt, or None."""
+    path = os.path.join(ROOT, 'profiles', f'traffic_cfg{cfg}.txt')   # measured DRAM bytes
     if world != 1 or not os.path.isfile(path):
         return None
     with open(path) as f:
         for line in f:
-            if line.startswith('dram_bytes_per_step:'):
+            if line.startswith(key + ':'):
                 return float(line.split(':', 1)[1])
     return None
 
