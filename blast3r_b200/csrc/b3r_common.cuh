@@ -173,6 +173,8 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
   const T fbar = T(0.5) * (fx + fy);
   if (WANT_R) {
     // projection and reprojection residual (.cu:217-228)
+    // the quotients exactly as the reference forms them: p - k cancels, so the residual
+    // keeps the reference's rounding of p
     const T p0 = (fx * X_c[0] + cx * X_c[2]) / z;
     const T p1 = (fy * X_c[1] + cy * X_c[2]) / z;
     L.r[0] = (p0 - (T)kx) / sx;
@@ -201,7 +203,9 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
   }
   if (!WANT_J) return;
   // Jacobians (.cu:410-508)
-  const T inv_z = T(1.0f) / z;
+  // the Jacobian's divisions by z, sx, sy (.cu:410-480) become products with one
+  // reciprocal each (within an ulp of the quotients; no cancellation follows them)
+  const T inv_z = T(1.0f) / z, rsx = T(1.0f) / sx, rsy = T(1.0f) / sy;
   const T inv_z2 = inv_z * inv_z;
   const T P0 = fx * X_c[0] + cx * X_c[2];
   const T P1 = fy * X_c[1] + cy * X_c[2];
@@ -209,7 +213,7 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
   Jpc[0] = fx * inv_z;             Jpc[1] = 0; Jpc[2] = cx * inv_z - P0 * inv_z2;
   Jpc[3] = 0; Jpc[4] = fy * inv_z; Jpc[5] = cy * inv_z - P1 * inv_z2;
   Jpc[6] = 0; Jpc[7] = 0;          Jpc[8] = -fbar * inv_z;
-  Jpc[0] /= sx; Jpc[2] /= sx; Jpc[4] /= sy; Jpc[5] /= sy;
+  Jpc[0] *= rsx; Jpc[2] *= rsx; Jpc[4] *= rsy; Jpc[5] *= rsy;
   // J_proj_rig = Jpc @ R_cr, skipping the structural zeros of Jpc (entries 1, 3, 6, 7):
   // the same value as the dense product (adding 0 or 0 * x changes no finite sum)
   T Jr[9];
@@ -240,8 +244,8 @@ __device__ __forceinline__ void linearize_obs(const CamT<T>& cam, const T X[3], 
       for (int k = 0; k < 3; ++k) s += Jr[3 * r + k] * cam.R_rw[3 * k + c];
       L.Jp[3 * r + c] = s;
     }
-  L.Jf0 = X_c[0] * inv_z / sx;
-  L.Jf1 = X_c[1] * inv_z / sy;
+  L.Jf0 = X_c[0] * inv_z * rsx;
+  L.Jf1 = X_c[1] * inv_z * rsy;
   float jkf = 0.f;
   if (guid > 0) jkf = o.is_depth_log ? (float)(0.5f * (guid + t_log<T>(inv_z))) : (float)(0.5f * t_log<T>(guid * inv_z));
   L.Jkf = jkf;
