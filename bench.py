@@ -38,6 +38,8 @@ def parse_args():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--config', type=int, default=2)
+    ap.add_argument('--tracks', type=int, default=None,
+                    help='override the configuration\'s track count (same generator; smaller profiling cases)')
     ap.add_argument('--cpu-sample-tracks', type=int, default=20000,
                     help='tracks in the bounded CPU-baseline sample (same generator)')
     ap.add_argument('--ref-step-tracks', type=int, default=4000,
@@ -191,7 +193,7 @@ def run_b200(args):
     dev = torch.device('cuda', local)
     if world > 1:
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
-    sc = make_scene(args.config)
+    sc = make_scene(args.config, n_tracks=args.tracks)
     t0, t1, n_local = shard_tracks(sc.pids, sc.n_tracks, world, rank)
     o = sc.options
     plan = BAPlan(sc.infos, sc.pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
@@ -348,7 +350,7 @@ def run_b200(args):
         line = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
                 'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'strong',
                 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded generator of the configuration)',
-                'config': {'workload': f'configs[{args.config}]', 'n_obs': sc.n_obs, 'n_tracks': sc.n_tracks,
+                'config': {'workload': f'configs[{args.config}]' + (f' with {args.tracks} tracks' if args.tracks else ''), 'n_obs': sc.n_obs, 'n_tracks': sc.n_tracks,
                            'n_imgs': sc.n_imgs, 'mean_track_length': sc.meta['mean_track_length'],
                            'n_obs_pairs': int(plan.info.n_pairs), 'nnz_S': nnz,
                            'parallelism': f'track-sharded x{world}' + (' + NCCL reduce of S, b' if world > 1 else ''),
