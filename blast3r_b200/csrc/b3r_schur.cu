@@ -469,8 +469,8 @@ __host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - 
 template <int CT>
 __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, bool elim, int64_t e, float4 tf0,
                                            float4 tf1, float tf2, float* __restrict__ out) {
-  // value v of this observation goes to out[33 v] (its lane's column of the warp's
-  // transpose buffer), as soon as it is computed
+  // value v of this observation goes to out[v] (its lane's row of the warp's transpose
+  // buffer), as soon as it is computed
   using Lay = DiagLayout<CT>;
   float H[9][9];
 #pragma unroll
@@ -493,12 +493,12 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
     g[a] = s;
   }
   // undamped diag(A) = diag(Hcc)
-  out[33 * (Lay::DA + 0)] = H[0][0];
-  out[33 * (Lay::DA + 1)] = H[1][1];
+  out[Lay::DA + 0] = H[0][0];
+  out[Lay::DA + 1] = H[1][1];
 #pragma unroll
-  for (int t = 0; t < 6; ++t) out[33 * (Lay::DA + 2 + t)] = H[2 + t][2 + t];
+  for (int t = 0; t < 6; ++t) out[Lay::DA + 2 + t] = H[2 + t][2 + t];
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::DA + 8 + ch)] = H[8][8] * V.dep[ch] * V.dep[ch];
+  for (int ch = 0; ch < CT; ++ch) out[Lay::DA + 8 + ch] = H[8][8] * V.dep[ch] * V.dep[ch];
   if (elim) {                                     // eliminated track: record Y, subtract Y^T Y, Y^T z
     const float li[6] = {tf0.x, tf0.y, tf0.z, tf0.w, tf1.x, tf1.y};
     float Y[9][3];
@@ -512,48 +512,57 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
       g[a] = fmaf(-Y[a][2], z2, fmaf(-Y[a][1], z1, fmaf(-Y[a][0], z0, g[a])));
     }
   }
-  out[33 * (Lay::FF + 0)] = H[0][0];
-  out[33 * (Lay::FF + 1)] = H[0][1];
-  out[33 * (Lay::FF + 2)] = H[1][1];
+  out[Lay::FF + 0] = H[0][0];
+  out[Lay::FF + 1] = H[0][1];
+  out[Lay::FF + 2] = H[1][1];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
 #pragma unroll
-    for (int t = 0; t < 6; ++t) out[33 * (Lay::FT + 6 * r + t)] = H[r][2 + t];
+    for (int t = 0; t < 6; ++t) out[Lay::FT + 6 * r + t] = H[r][2 + t];
 #pragma unroll
-    for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::FZ + CT * r + ch)] = H[r][8] * V.dep[ch];
+    for (int ch = 0; ch < CT; ++ch) out[Lay::FZ + CT * r + ch] = H[r][8] * V.dep[ch];
   }
 #pragma unroll
   for (int a = 0; a < 6; ++a) {
 #pragma unroll
-    for (int b = a; b < 6; ++b) out[33 * (Lay::TT + sym_idx(a, b, 6))] = H[2 + a][2 + b];
+    for (int b = a; b < 6; ++b) out[Lay::TT + sym_idx(a, b, 6)] = H[2 + a][2 + b];
 #pragma unroll
-    for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::TZ + CT * a + ch)] = H[2 + a][8] * V.dep[ch];
+    for (int ch = 0; ch < CT; ++ch) out[Lay::TZ + CT * a + ch] = H[2 + a][8] * V.dep[ch];
   }
 #pragma unroll
   for (int a = 0; a < CT; ++a) {
     const float ha = H[8][8] * V.dep[a];
 #pragma unroll
-    for (int b = a; b < CT; ++b) out[33 * (Lay::ZZ + sym_idx(a, b, CT))] = ha * V.dep[b];
+    for (int b = a; b < CT; ++b) out[Lay::ZZ + sym_idx(a, b, CT)] = ha * V.dep[b];
   }
 #pragma unroll
-  for (int a = 0; a < 8; ++a) out[33 * (Lay::B + a)] = g[a];
+  for (int a = 0; a < 8; ++a) out[Lay::B + a] = g[a];
 #pragma unroll
-  for (int ch = 0; ch < CT; ++ch) out[33 * (Lay::B + 8 + ch)] = g[8] * V.dep[ch];
+  for (int ch = 0; ch < CT; ++ch) out[Lay::B + 8 + ch] = g[8] * V.dep[ch];
 }
 
 constexpr int kDiagThreads = 64;   // two warps per image chunk
 
+// Row stride (floats) of a warp's transpose buffer: >= N and 28 mod 32, so that the lanes'
+// 16-byte row stores and the 16-byte column-group reads are both free of bank conflicts.
+template <int CT> __host__ __device__ constexpr int diag_row_stride() {
+  return DiagLayout<CT>::N + ((28 - DiagLayout<CT>::N) % 32 + 32) % 32;
+}
+
 // Per-image reduction of the per-observation values: each warp takes 32 observations at a
-// time (lane = observation), writes their values to shared memory (stride 33: conflict-
-// free), and each lane keeps running sums of values lane, lane+32, lane+64, ... only, so
-// the 8+C..117 values never sit in every thread's registers across observations.
+// time (lane = observation) and writes each observation's N values as one row of its
+// transpose buffer; then each lane sums a group of four neighbouring values down the 32
+// rows with 16-byte reads and keeps the running sums, so the N values never sit in every
+// thread's registers across observations.
 template <int CT>
 __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
                                                        float* __restrict__ diagA) {
   using Lay = DiagLayout<CT>;
   constexpr int NW = kDiagThreads / kWarp;
-  constexpr int NV = (Lay::N + 31) / 32;           // values per lane
-  extern __shared__ __align__(16) float red_dyn[];   // [NW][N * 33]
+  constexpr int RS = diag_row_stride<CT>();
+  constexpr int NG = (Lay::N + 3) / 4;             // groups of four values
+  constexpr int NGL = (NG + 31) / 32;              // groups per lane
+  extern __shared__ __align__(16) float red_dyn[];   // [NW][32 rows][RS]
   const int chunk = blockIdx.x;
   const int img = c.d.c1_img[chunk];
   const int eb = c.d.c1_chunk[chunk], ee = c.d.c1_chunk[chunk + 1];
@@ -562,10 +571,10 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* rw = red_dyn + warp * (Lay::N * 33);
-  float run[NV];
+  float* rw = red_dyn + warp * (32 * RS);
+  float4 run[NGL];
 #pragma unroll
-  for (int j = 0; j < NV; ++j) run[j] = 0.f;
+  for (int j = 0; j < NGL; ++j) run[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   ObsIn<CT> nxt;
   load_obs_in<CT>(c, eb + warp * kWarp + lane, ee, nxt);
   for (int base = eb + warp * kWarp; base < ee; base += NW * kWarp) {
@@ -575,28 +584,31 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     if (e < ee) {
       ObsView<CT> V;
       view_in<CT>(c, cur, img, cam, zc, V);
-      diag_terms<CT>(c, V, cur.ix.y >= 0, e, cur.tf0, cur.tf1, cur.tf2, rw + lane);
+      diag_terms<CT>(c, V, cur.ix.y >= 0, e, cur.tf0, cur.tf1, cur.tf2, rw + lane * RS);
     } else {
-      for (int v = 0; v < Lay::N; ++v) rw[v * 33 + lane] = 0.f;
+      for (int v = 0; v < Lay::N; ++v) rw[lane * RS + v] = 0.f;
     }
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int v = lane + 32 * j;
-      if (v < Lay::N) {
-        float t = 0.f;
+    for (int j = 0; j < NGL; ++j) {
+      const int g = lane + 32 * j;
+      if (g < NG) {                 // columns 4g..4g+3 (those >= N are never emitted)
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-        for (int l = 0; l < 32; ++l) t += rw[v * 33 + l];
-        run[j] += t;
+        for (int l = 0; l < 32; ++l) {
+          const float4 x = *reinterpret_cast<const float4*>(rw + l * RS + 4 * g);
+          t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+        }
+        run[j].x += t.x; run[j].y += t.y; run[j].z += t.z; run[j].w += t.w;
       }
     }
     __syncwarp();
   }
   // cross-warp sum, then one atomic per destination entry
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int v = lane + 32 * j;
-    if (v < Lay::N) rw[v] = run[j];
+  for (int j = 0; j < NGL; ++j) {
+    const int g = lane + 32 * j;
+    if (g < NG) *reinterpret_cast<float4*>(rw + 4 * g) = run[j];
   }
   __syncthreads();
   const int* dst = c.d.img_dst + 6 * img;
@@ -638,7 +650,7 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     if (addr) {
       float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) t += red_dyn[w * (Lay::N * 33) + v];
+      for (int w = 0; w < NW; ++w) t += red_dyn[w * (32 * RS) + v];
       atomicAdd(addr, t);
     }
   }
@@ -1174,7 +1186,7 @@ int launch_points(const Ctx& c, cudaStream_t s) {
 
 template <int CT>
 int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
-  const size_t smem = (size_t)(kDiagThreads / kWarp) * DiagLayout<CT>::N * 33 * sizeof(float);
+  const size_t smem = (size_t)(kDiagThreads / kWarp) * 32 * diag_row_stride<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
   if (!configured) {
     B3R_TRY(check_cuda(cudaFuncSetAttribute(k_diag<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
