@@ -86,6 +86,9 @@ _SIGS = {
     'b3r_schur_spmv': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     'b3r_schur_spmv_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     'b3r_backsub': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, _vp, _vp, _vp]),
+    'b3r_pcg_work_bytes': (_i64, [_vp]),
+    'b3r_pcg': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
+    'b3r_pcg_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
 }
 
 _lib = None

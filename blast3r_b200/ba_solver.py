@@ -8,8 +8,9 @@ running a matrix-free PCG on the implicit Schur complement (ba_solver.py:184-206
    once per phase and cached: ``BAPlan``);
 2. ``solve_delta`` runs the fused B200 linearization (residual, Jacobians, IRLS weights,
    per-track Hpp inversion, Schur assembly into the block-sparse S and b, per-type
-   adaptive damping), then the reference's PCG on the explicit S, then the point
-   back-substitution delta_p = D^-1 (g_p - C delta_c).
+   adaptive damping), then the reference's PCG on the explicit S (one cooperative device
+   kernel, same iteration and stopping rule), then the point back-substitution
+   delta_p = D^-1 (g_p - C delta_c).
 
 ``compute_jacobians`` accepts one extra keyword, ``pix2d``: with it the kernels recompute
 residuals and weights in-kernel (identical values: one shared device function); without
@@ -17,7 +18,6 @@ it they read the ``residuals`` / ``w_pts`` handed to ``solve_delta``, as the ref
 """
 import torch
 
-from .pcg import pcg
 from .plan import BAPlan
 
 N_FOC = 2
@@ -132,9 +132,8 @@ class GaussNewtonSolver:
             raise NotImplementedError('dense tangent prior (z_prior) is not supported by the fused path yet')
         s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw)
         dt = torch.float64 if self.dtype == torch.float64 else torch.float32
-        b = s.b.to(dt)
-        M = s.precond.to(dt)
-        delta_c, niter, conv = pcg(lambda v: s.matvec(v), b, M_mv=lambda v: v / M, tol=1e-6, maxiter=300)
+        # the reference's PCG (ba_solver.py:202, 1197-1238) as one device kernel on the explicit S
+        delta_c, niter, conv = s.plan.pcg(s.S_vals, s.precond, s.b.to(dt), tol=1e-6, maxiter=300)
         delta_p = s.backsub(delta_c.to(torch.float32))
         self.last_solve = dict(iters=niter, converged=conv)
         return torch.cat([delta_c.to(torch.float32), delta_p])

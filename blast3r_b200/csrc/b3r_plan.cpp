@@ -79,6 +79,7 @@ struct PlanBuild {
   std::vector<int> row_ptr, col_idx, val_off;
   std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
   std::vector<int4> t_idx, c1_idx;
+  std::vector<int> sym_ptr, sym_ent;
   int64_t nnz = 0;
 };
 
@@ -435,6 +436,27 @@ static int build_pattern(PlanBuild& B) {
       const int p = B.img_bk[3 * i + AB[j][0]], q = B.img_bk[3 * i + AB[j][1]];
       if (p >= 0 && q >= 0) B.img_dst[6 * i + j] = pat_lookup(B, p, q);
     }
+  // symmetric block rows: row p holds its stored blocks (p, q >= p), then the transposes of
+  // the stored blocks (q, p), q < p
+  {
+    const int64_t nnzb = (int64_t)B.col_idx.size();
+    std::vector<int> cnt(nb + 1, 0);
+    for (int pr = 0; pr < nb; ++pr)
+      for (int j = B.row_ptr[pr]; j < B.row_ptr[pr + 1]; ++j) {
+        cnt[pr + 1]++;
+        if (B.col_idx[j] != pr) cnt[B.col_idx[j] + 1]++;
+      }
+    for (int pr = 0; pr < nb; ++pr) cnt[pr + 1] += cnt[pr];
+    B.sym_ptr = cnt;
+    B.sym_ent.assign(cnt[nb], 0);
+    std::vector<int> fill(cnt.begin(), cnt.end() - 1);
+    for (int pr = 0; pr < nb; ++pr)
+      for (int j = B.row_ptr[pr]; j < B.row_ptr[pr + 1]; ++j) B.sym_ent[fill[pr]++] = 2 * j;
+    for (int pr = 0; pr < nb; ++pr)
+      for (int j = B.row_ptr[pr]; j < B.row_ptr[pr + 1]; ++j)
+        if (B.col_idx[j] != pr) B.sym_ent[fill[B.col_idx[j]]++] = 2 * j + 1;
+    B3R_REQUIRE((int64_t)B.sym_ent.size() == 2 * nnzb - nb || nb == 0, "internal: symmetric rows");
+  }
   // diagonal scalar positions
   const int ncp = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
   B.sdiag_pos.resize(ncp);
@@ -542,6 +564,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.bsize, &d.bsize); A.add(B.boff, &d.boff); A.add(B.sdiag_pos, &d.sdiag_pos);
   A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);
   A.add(B.t_idx, &d.t_idx); A.add(B.c1_idx, &d.c1_idx);
+  A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
   if (!host_only) {
     int rc = A.upload(&P->dev_mem);
     cudaSetDevice(prev_dev);

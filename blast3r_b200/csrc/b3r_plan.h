@@ -82,6 +82,11 @@ struct DevPlan {
   const int* trk_ptr;     // [nT_loc+1] first k of each local track
   const int4* t_idx;      // [n_loc] (image, global track id, tl, o) of local observation k
   const int4* c1_idx;     // [n_c1] (o, k or -1, track id, tl or -1) of image-major entry e
+  // the full (symmetric) block rows of S for an atomic-free matvec: entries of block row p
+  // are sym_ent[sym_ptr[p] .. sym_ptr[p+1]), each 2 * stored block + 1 if it is the
+  // transpose of a stored block (q, p) with q < p
+  const int* sym_ptr;     // [nb+1]
+  const int* sym_ent;     // [2*nnzb - nb]
 };
 
 struct HostPattern {

@@ -184,6 +184,22 @@ class BAPlan:
         L.call(name, self._h, S_vals.data_ptr(), x.contiguous().data_ptr(), y.data_ptr(), s)
         return y
 
+    def pcg(self, S_vals, precond, b, tol=1e-6, maxiter=300):
+        """Solve S x = b on the device (b3r_pcg[_f64]): the reference's PCG iteration and
+        stopping rule, one cooperative kernel.  Returns (x, iterations, converged)."""
+        assert b.dtype in (torch.float32, torch.float64)
+        b = b.contiguous()
+        x = torch.empty_like(b)
+        work = torch.empty(int(L.lib().b3r_pcg_work_bytes(self._h)) // 8 + 32, dtype=torch.float64, device=b.device)
+        res = torch.zeros(4, dtype=torch.int32, device=b.device)
+        name = 'b3r_pcg_f64' if b.dtype == torch.float64 else 'b3r_pcg'
+        L.call(name, self._h, S_vals.data_ptr(), precond.contiguous().data_ptr(), b.data_ptr(), x.data_ptr(),
+               float(tol), int(maxiter), work.data_ptr(), res.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        it, conv, err = res[:3].tolist()
+        if err:
+            raise L.B3RError('b3r_pcg: a grid barrier of the PCG kernel gave up')
+        return x, int(it), bool(conv)
+
     def backsub(self, params, opts, workspace_ptr, delta_c, delta_p=None):
         if delta_p is None:
             delta_p = torch.zeros(3 * self.info.n_points, dtype=torch.float32, device=self.device)

@@ -249,6 +249,22 @@ int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const b3r_lin_opt
 int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
                      const b3r_outputs* out, void* stream);
 
+/* Preconditioned conjugate gradient on the assembled S (the reference's _pcg,
+ * inference/ba_solver.py:1197-1238, as solve_delta calls it at :202): solves S x = b from
+ * x0 = 0 with the Jacobi preconditioner precond (out->precond of the linearization),
+ * stopping at the first iterate with ||r|| <= tol ||b|| (converged, returned), breaking on a
+ * non-finite r.z, else returning the best-so-far iterate after maxiter iterations.  One
+ * cooperative kernel runs the whole loop on `stream`.  `work` is a 256-byte aligned device
+ * buffer of b3r_pcg_work_bytes(plan) bytes; `result` is a device int[3] receiving
+ * (iterations, converged, device error) -- read it after synchronising the stream.
+ * b3r_pcg uses float vectors, b3r_pcg_f64 double vectors; S stays float either way.
+ * Replaces the reference's per-iteration Python loop; no counterpart in its native ops. */
+int64_t b3r_pcg_work_bytes(const b3r_plan* plan);
+int b3r_pcg(const b3r_plan* plan, const float* S_vals, const float* precond, const float* b, float* x,
+            double tol, int maxiter, void* work, int* result, void* stream);
+int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond, const double* b, double* x,
+                double tol, int maxiter, void* work, int* result, void* stream);
+
 /* One pass of b3r_lin_points/b3r_lin_assemble on its own (profiling and custom
  * pipelines): B3R_PASS_PREP (per-image records), _POINTS (per-track Hpp, g_p), _FACTOR
  * (damped per-track Cholesky factors), _DIAG (elimination records and per-image diagonal
