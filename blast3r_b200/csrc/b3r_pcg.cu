@@ -9,7 +9,8 @@
 // cooperative launch) separates
 //   phase A  the decisions on the previous iterate (best-so-far copy, convergence,
 //            non-finite break, beta), p = z + beta p computed on the fly inside the matvec
-//            Ap = S p (symmetric block rows, no atomics) and the partial sums of p.Ap
+//            Ap = S p (symmetric block rows cut into <= 64-entry warp tasks; a row of several
+//            tasks adds its parts atomically) and the partial sums of p.Ap
 //   phase B  x += alpha p, r -= alpha Ap, z = r / M and the partial sums of r.r and r.z
 // so an iteration costs two barriers.  Vectors are float or double (the solver's dtype);
 // reductions accumulate in double.
@@ -78,27 +79,37 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   return t;   // valid on thread 0
 }
 
-// The lanes of a warp compute y_p = sum over the symmetric block row p of A x_q, with
-// x_q = z_q + beta * pold_q formed on the fly; every lane returns y_p[r] (r < bp) in yo.
+// The lanes of a warp compute the part of y_p = sum_q A_pq x_q over the symmetric entries
+// [e0, e1) of block row p, with x_q = z_q + beta * pold_q formed on the fly (all of an
+// entry's column values are loaded before its products); every lane returns the partial
+// y_p[r] (r < bp) in yo.
 template <typename T, int MAXB>
-__device__ __forceinline__ void row_matvec(const DevPlan& d, const float* __restrict__ S, int p, int bp,
-                                           const T* __restrict__ z, const T* __restrict__ pold, T beta, int lane,
-                                           T yo[MAXB]) {
+__device__ __forceinline__ void task_matvec(const DevPlan& d, const float* __restrict__ S, int bp, int e0, int e1,
+                                            const T* __restrict__ z, const T* __restrict__ pold, T beta, int lane,
+                                            T yo[MAXB]) {
   T y[MAXB];
 #pragma unroll
   for (int r = 0; r < MAXB; ++r) y[r] = T(0);
-  for (int e = d.sym_ptr[p] + lane; e < d.sym_ptr[p + 1]; e += 32) {
-    const int ent = d.sym_ent[e];
-    const int blk = ent >> 1;
-    const bool tr = ent & 1;
-    const int q = tr ? d.blk_row[blk] : d.col_idx[blk];
-    const int bq = d.bsize[q], oq = d.boff[q];
-    const float* A = S + d.val_off[blk];
-    for (int cc = 0; cc < bq; ++cc) {
-      const T xq = __ldcg(z + oq + cc) + beta * __ldcg(pold + oq + cc);   // other blocks wrote them
+  for (int e = e0 + lane; e < e1; e += 32) {
+    const int4 en = __ldg(d.mv_ent + e);                 // value offset, column offset, bq, transposed
+    const float* A = S + en.x;
+    const int oq = en.y, bq = en.z;
+    T xq[MAXB];
+#pragma unroll
+    for (int cc = 0; cc < MAXB; ++cc)                    // other blocks wrote z and pold: L2 reads
+      xq[cc] = cc < bq ? __ldcg(z + oq + cc) + beta * __ldcg(pold + oq + cc) : T(0);
+    if (en.w) {
+#pragma unroll
+      for (int cc = 0; cc < MAXB; ++cc)
+#pragma unroll
+        for (int r = 0; r < MAXB; ++r)
+          if (cc < bq && r < bp) y[r] += (T)__ldg(A + cc * bp + r) * xq[cc];
+    } else {
 #pragma unroll
       for (int r = 0; r < MAXB; ++r)
-        if (r < bp) y[r] += (T)(tr ? A[cc * bp + r] : A[r * bq + cc]) * xq;
+#pragma unroll
+        for (int cc = 0; cc < MAXB; ++cc)
+          if (cc < bq && r < bp) y[r] += (T)__ldg(A + r * bq + cc) * xq[cc];
     }
   }
 #pragma unroll
@@ -134,7 +145,7 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
   double s_rz = 0.0, s_bb = 0.0;
   for (int i = tid; i < n; i += nth) {
     const T bi = b[i], zi = bi / (T)M[i];
-    x[i] = T(0); r[i] = bi; z[i] = zi; pbuf0[i] = T(0); pbuf1[i] = T(0); bx[i] = T(0);
+    x[i] = T(0); r[i] = bi; z[i] = zi; pbuf0[i] = T(0); pbuf1[i] = T(0); bx[i] = T(0); Ap[i] = T(0);
     s_rz += (double)bi * (double)zi;
     s_bb += (double)bi * (double)bi;
   }
@@ -170,17 +181,20 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
     T* pnew = (k & 1) ? pbuf1 : pbuf0;
     const T tb = (T)beta;
     double s_pap = 0.0;
-    for (int p = gw; p < d.nb; p += nwarps) {            // warp per symmetric block row
-      const int bp = d.bsize[p], op = d.boff[p];
+    for (int task = gw; task < d.n_mv_tasks; task += nwarps) {   // warp per matvec task
+      const int4 tk = __ldg(d.mv_task + task);           // block row, entries [e0, e1), single
+      const int p = tk.x, bp = d.bsize[p], op = d.boff[p];
       T yo[MAXB];
-      row_matvec<T, MAXB>(d, S, p, bp, z, pold, tb, lane, yo);
+      task_matvec<T, MAXB>(d, S, bp, tk.y, tk.z, z, pold, tb, lane, yo);
+      const bool first = tk.y == d.sym_ptr[p];
 #pragma unroll
       for (int rr = 0; rr < MAXB; ++rr) {
         if (lane == rr && rr < bp) {
           const T pn = __ldcg(z + op + rr) + tb * __ldcg(pold + op + rr);
-          Ap[op + rr] = yo[rr];
-          pnew[op + rr] = pn;
-          s_pap += (double)pn * (double)yo[rr];
+          if (tk.w) Ap[op + rr] = yo[rr];                // the row is one task
+          else atomicAdd(Ap + op + rr, yo[rr]);          // zeroed by the previous phase B
+          if (first) pnew[op + rr] = pn;
+          s_pap += (double)pn * (double)yo[rr];          // p.Ap is linear in the row's tasks
         }
       }
     }
@@ -195,6 +209,7 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
     for (int i = tid; i < n; i += nth) {
       const T xi = x[i] + ta * __ldcg(pnew + i);
       const T ri = r[i] - ta * __ldcg(Ap + i);
+      Ap[i] = T(0);                                      // for the next matvec's atomics
       const T zi = ri / (T)M[i];
       x[i] = xi; r[i] = ri; z[i] = zi;
       s_rr += (double)ri * (double)ri;
@@ -233,7 +248,7 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
                        "pcg occupancy"));
     B3R_REQUIRE(per_sm >= 1, "the PCG kernel does not fit on an SM");
   }
-  const int want = (d.nb * 32 + kPcgThreads - 1) / kPcgThreads;   // one warp per block row
+  const int want = (d.n_mv_tasks * 32 + kPcgThreads - 1) / kPcgThreads;   // one warp per matvec task
   const int grid = std::max(1, std::min(want, per_sm * n_sm));     // all co-resident
   PcgScalars* sc = reinterpret_cast<PcgScalars*>(work);
   T* vec = reinterpret_cast<T*>(reinterpret_cast<char*>(work) + 256);

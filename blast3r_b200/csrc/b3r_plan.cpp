@@ -80,6 +80,7 @@ struct PlanBuild {
   std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
   std::vector<int4> t_idx, c1_idx;
   std::vector<int> sym_ptr, sym_ent;
+  std::vector<int4> mv_task, mv_ent;
   int64_t nnz = 0;
 };
 
@@ -456,6 +457,17 @@ static int build_pattern(PlanBuild& B) {
       for (int j = B.row_ptr[pr]; j < B.row_ptr[pr + 1]; ++j)
         if (B.col_idx[j] != pr) B.sym_ent[fill[B.col_idx[j]]++] = 2 * j + 1;
     B3R_REQUIRE((int64_t)B.sym_ent.size() == 2 * nnzb - nb || nb == 0, "internal: symmetric rows");
+    B.mv_ent.resize(B.sym_ent.size());
+    for (size_t e = 0; e < B.sym_ent.size(); ++e) {
+      const int blk = B.sym_ent[e] >> 1, tr = B.sym_ent[e] & 1;
+      const int q = tr ? B.blk_row[blk] : B.col_idx[blk];
+      B.mv_ent[e] = make_int4(B.val_off[blk], B.boff[q], B.bsize[q], tr);
+    }
+    for (int pr = 0; pr < nb; ++pr) {
+      const int e0 = B.sym_ptr[pr], e1 = B.sym_ptr[pr + 1];
+      const int single = (e1 - e0) <= kMvTask;
+      for (int e = e0; e < e1; e += kMvTask) B.mv_task.push_back(make_int4(pr, e, std::min(e + kMvTask, e1), single));
+    }
   }
   // diagonal scalar positions
   const int ncp = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
@@ -565,6 +577,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);
   A.add(B.t_idx, &d.t_idx); A.add(B.c1_idx, &d.c1_idx);
   A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
+  A.add(B.mv_task, &d.mv_task); A.add(B.mv_ent, &d.mv_ent);
+  d.n_mv_tasks = (int)B.mv_task.size();
   if (!host_only) {
     int rc = A.upload(&P->dev_mem);
     cudaSetDevice(prev_dev);

@@ -22,6 +22,7 @@ constexpr int kPairTask = 2048;    // max observation pairs per pair task
 constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal chunk
 constexpr int kPointTask = 32;     // max observations per point task (one warp)
 constexpr int kImgRecFloats = 32;  // floats per per-image camera record
+constexpr int kMvTask = 64;        // max symmetric entries per matvec task
 
 // sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
 constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
@@ -87,6 +88,12 @@ struct DevPlan {
   // transpose of a stored block (q, p) with q < p
   const int* sym_ptr;     // [nb+1]
   const int* sym_ent;     // [2*nnzb - nb]
+  // matvec work: symmetric block rows cut into tasks of <= kMvTask entries (a dense row,
+  // e.g. the shared focal block of a mono-camera rig, spreads over many warps)
+  int n_mv_tasks;
+  const int4* mv_task;    // [n_mv_tasks] (block row, first entry, end entry, row is one task)
+  const int4* mv_ent;     // [2*nnzb - nb] (value offset, column scalar offset, column block size,
+                          //  1 if the entry is the transpose of the stored block)
 };
 
 struct HostPattern {

