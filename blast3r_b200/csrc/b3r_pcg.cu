@@ -9,8 +9,9 @@
 // cooperative launch) separates
 //   phase A  the decisions on the previous iterate (best-so-far copy, convergence,
 //            non-finite break, beta), p = z + beta p computed on the fly inside the matvec
-//            Ap = S p (symmetric block rows cut into <= 64-entry warp tasks; a row of several
-//            tasks adds its parts atomically) and the partial sums of p.Ap
+//            Ap = S p (row panels of the symmetric S, built once per solve, cut into
+//            <= 256-column warp tasks; a row of several tasks adds its parts atomically)
+//            and the partial sums of p.Ap
 //   phase B  x += alpha p, r -= alpha Ap, z = r / M and the partial sums of r.r and r.z
 // so an iteration costs two barriers.  Vectors are float or double (the solver's dtype);
 // reductions accumulate in double.
@@ -26,46 +27,70 @@ namespace {
 constexpr int kPcgThreads = 256;
 constexpr int kBarrierSpins = 1 << 24;   // polls before a grid barrier gives up
 
-// Scalars and barrier words at the start of the work buffer (doubles).
-struct PcgScalars {
-  double pAp[2], rr[2], rz[2];   // partial-sum slots, by iteration parity
-  double bb, rz0;                // ||b||^2 and r0.z0 of the prologue
-  unsigned int bar_count, bar_gen, abort_flag, pad;
+// Work buffer layout: barrier words | per-block arrival flags | per-block partial sums |
+// the seven vectors.  Same-address atomics from every block serialise at one L2 slice, so
+// neither the barrier nor the reductions use them: each block writes its own flag and its
+// own partial sums, and every block sums all partials in the same fixed order.
+constexpr int kPcgMaxBlocks = 1024;
+constexpr size_t kPcgFlagsOff = 256, kPcgPartOff = kPcgFlagsOff + 4 * kPcgMaxBlocks;
+constexpr size_t kPcgVecOff = kPcgPartOff + 4 * 8 * kPcgMaxBlocks;
+
+inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the seven vectors
+  return (kPcgVecOff + 7 * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
+}
+
+struct PcgWords {
+  unsigned int bar_gen, abort_flag;
+};
+// per-block partial sums: [0] p.Ap, [1] r.r, [2] r.z (prologue: b.b and r0.z0)
+struct PcgPart {
+  double v[4];
 };
 
-// Sense-counting grid barrier for a cooperative launch: the last block to arrive resets the
-// count and bumps the generation; the others poll the generation, at most kBarrierSpins
-// times.  Returns false (and raises abort_flag) if the poll gave up; every block checks
-// abort_flag after each barrier, so all of them leave the loop together.
-__device__ __forceinline__ bool grid_barrier(PcgScalars* sc, unsigned int& gen) {
+// Grid barrier for a cooperative launch: every block publishes its arrival as flags[block] =
+// target; block 0 waits until every flag holds the target, then publishes bar_gen = target,
+// which the other blocks wait for.  Every poll is bounded (kBarrierSpins); a poll that
+// gives up raises abort_flag, which every block checks after each barrier, so all of them
+// leave the loop together.
+__device__ __forceinline__ bool grid_barrier(PcgWords* w, volatile unsigned int* flags, unsigned int target) {
   __shared__ int ok_s;
-  __syncthreads();
+  __syncthreads();                                       // the block's writes precede its arrival
   if (threadIdx.x == 0) {
-    int ok = 1;
-    const unsigned int g = gen;
     __threadfence();
-    const unsigned int arrived = atomicAdd(&sc->bar_count, 1u) + 1u;
-    if (arrived == gridDim.x) {
-      atomicExch(&sc->bar_count, 0u);
-      __threadfence();
-      atomicAdd(&sc->bar_gen, 1u);
-    } else {
-      volatile unsigned int* vg = &sc->bar_gen;
+    flags[blockIdx.x] = target;
+    ok_s = 1;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
       int spins = 0;
-      while (*vg == g) {
-        if (++spins > kBarrierSpins) { ok = 0; atomicExch(&sc->abort_flag, 1u); break; }
-        __nanosleep(64);
+      while (flags[b] < target) {
+        if (++spins > kBarrierSpins) { atomicExch(&w->abort_flag, 1u); ok_s = 0; break; }
+        __nanosleep(32);
       }
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      *(volatile unsigned int*)&w->bar_gen = target;
+    }
+  } else if (threadIdx.x == 0) {
+    volatile unsigned int* vg = &w->bar_gen;
+    int spins = 0;
+    while (*vg < target) {
+      if (++spins > kBarrierSpins) { atomicExch(&w->abort_flag, 1u); ok_s = 0; break; }
+      __nanosleep(32);
+    }
+  }
+  if (threadIdx.x == 0) {
     __threadfence();
-    gen = g + 1;
-    ok_s = ok && (*(volatile unsigned int*)&sc->abort_flag == 0u);
+    if (*(volatile unsigned int*)&w->abort_flag != 0u) ok_s = 0;
   }
   __syncthreads();
   return ok_s != 0;
 }
 
-template <typename T>
+// Sum of v over the block (valid on thread 0).
 __device__ __forceinline__ double block_sum(double v, double* red) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
@@ -76,41 +101,69 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   double t = 0.0;
   if (threadIdx.x == 0)
     for (int i = 0; i < kPcgThreads / 32; ++i) t += red[i];
-  return t;   // valid on thread 0
+  return t;
 }
 
-// The lanes of a warp compute the part of y_p = sum_q A_pq x_q over the symmetric entries
-// [e0, e1) of block row p, with x_q = z_q + beta * pold_q formed on the fly (all of an
-// entry's column values are loaded before its products); every lane returns the partial
-// y_p[r] (r < bp) in yo.
+// Sum over blocks of partial field f, the same fixed order in every block; broadcast to
+// every thread of the block.
+__device__ __forceinline__ double grid_sum(const PcgPart* part, int f, double* red, double* bcast) {
+  double v = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) v += __ldcg(&part[b].v[f]);
+  const double t = block_sum(v, red);
+  if (threadIdx.x == 0) *bcast = t;
+  __syncthreads();
+  return *bcast;
+}
+
+// Row panels of the symmetric S (once per solve, before the PCG kernel): warp per
+// symmetric entry, copying its block (transposed when the entry is the transpose of the
+// stored block) into its block row's panel.
+__global__ void __launch_bounds__(256) k_build_panels(DevPlan d, const float* __restrict__ S, float* __restrict__ pan) {
+  const int e = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n_ent = d.sym_ptr[d.nb];
+  if (e >= n_ent) return;
+  const int4 en = d.mv_ent[e];                           // value offset, column offset, bq, transposed
+  const int p = d.ent_row[e], bp = d.bsize[p], bq = en.z, W = d.pan_w[p];
+  float* dst = pan + d.pan_off[p] + d.ent_col[e];
+  for (int t = lane; t < bp * bq; t += 32) {
+    const int r = t / bq, c = t - r * bq;
+    dst[(int64_t)r * W + c] = S[en.x + (en.w ? c * bp + r : r * bq + c)];
+  }
+}
+
+// The lanes of a warp compute the part of y_p = sum_c panel_p[r][c] x[col_c] over panel
+// columns [c0, c1) of block row p (at most kMvCols = 512, so at most 16 per lane), with
+// x = z + beta * pold formed on the fly.  The panel rows are read coalesced (consecutive
+// lanes, consecutive columns) and so mostly are the x values (a block's columns are
+// consecutive scalars).  Every lane returns the partial y_p[r] (r < bp) in yo.
 template <typename T, int MAXB>
-__device__ __forceinline__ void task_matvec(const DevPlan& d, const float* __restrict__ S, int bp, int e0, int e1,
-                                            const T* __restrict__ z, const T* __restrict__ pold, T beta, int lane,
-                                            T yo[MAXB]) {
+__device__ __forceinline__ void panel_matvec(const DevPlan& d, const float* __restrict__ pan, int p, int bp, int c0,
+                                             int c1, const T* __restrict__ z, const T* __restrict__ pold, T beta,
+                                             int lane, T yo[MAXB]) {
+  constexpr int CPL = kMvCols / 32;                      // columns per lane
+  const int W = d.pan_w[p];
+  const float* P = pan + d.pan_off[p];
+  const int* cols = d.pan_col + d.col_off[p];
+  T xc[CPL];
+  bool has[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int c = c0 + lane + 32 * j;
+    has[j] = c < c1;
+    const int col = has[j] ? __ldg(cols + c) : 0;
+    xc[j] = has[j] ? __ldcg(z + col) + beta * __ldcg(pold + col) : T(0);   // other blocks wrote them
+  }
   T y[MAXB];
 #pragma unroll
   for (int r = 0; r < MAXB; ++r) y[r] = T(0);
-  for (int e = e0 + lane; e < e1; e += 32) {
-    const int4 en = __ldg(d.mv_ent + e);                 // value offset, column offset, bq, transposed
-    const float* A = S + en.x;
-    const int oq = en.y, bq = en.z;
-    T xq[MAXB];
 #pragma unroll
-    for (int cc = 0; cc < MAXB; ++cc)                    // other blocks wrote z and pold: L2 reads
-      xq[cc] = cc < bq ? __ldcg(z + oq + cc) + beta * __ldcg(pold + oq + cc) : T(0);
-    if (en.w) {
+  for (int j = 0; j < CPL; ++j) {
+    if (!has[j]) continue;
+    const int c = c0 + lane + 32 * j;
 #pragma unroll
-      for (int cc = 0; cc < MAXB; ++cc)
-#pragma unroll
-        for (int r = 0; r < MAXB; ++r)
-          if (cc < bq && r < bp) y[r] += (T)__ldg(A + cc * bp + r) * xq[cc];
-    } else {
-#pragma unroll
-      for (int r = 0; r < MAXB; ++r)
-#pragma unroll
-        for (int cc = 0; cc < MAXB; ++cc)
-          if (cc < bq && r < bp) y[r] += (T)__ldg(A + r * bq + cc) * xq[cc];
-    }
+    for (int r = 0; r < MAXB; ++r)
+      if (r < bp) y[r] += (T)__ldg(P + (int64_t)r * W + c) * xc[j];
   }
 #pragma unroll
   for (int r = 0; r < MAXB; ++r) {
@@ -124,22 +177,26 @@ __device__ __forceinline__ void task_matvec(const DevPlan& d, const float* __res
 template <typename T, int MAXB>
 __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __restrict__ S,
                                                      const float* __restrict__ M, const T* __restrict__ b,
-                                                     T* __restrict__ xo, double tol, int maxiter, T* vec,
-                                                     PcgScalars* sc, int* result) {
+                                                     T* __restrict__ xo, double tol, int maxiter, char* work,
+                                                     const float* __restrict__ pan, int* result) {
   __shared__ double red[kPcgThreads / 32];
+  __shared__ double bc;
+  PcgWords* w = reinterpret_cast<PcgWords*>(work);
+  volatile unsigned int* flags = reinterpret_cast<volatile unsigned int*>(work + kPcgFlagsOff);
+  PcgPart* part = reinterpret_cast<PcgPart*>(work + kPcgPartOff);
+  T* vec = reinterpret_cast<T*>(work + kPcgVecOff);
   const int n = d.n_cam_params;
-  T* x = vec;                 // iterate (each element owned by one thread)
-  T* r = vec + n;             // residual (owned)
-  T* z = vec + 2 * (int64_t)n;        // preconditioned residual (owned; read by the matvec)
-  T* Ap = vec + 3 * (int64_t)n;       // S p (written by the matvec warps)
-  T* pbuf0 = vec + 4 * (int64_t)n;    // search direction, double-buffered by iteration parity
+  T* x = vec;                          // iterate (each element owned by one thread)
+  T* r = vec + n;                      // residual (owned)
+  T* z = vec + 2 * (int64_t)n;         // preconditioned residual (owned; read by the matvec)
+  T* Ap = vec + 3 * (int64_t)n;        // S p (written by the matvec warps)
+  T* pbuf0 = vec + 4 * (int64_t)n;     // search direction, double-buffered by iteration parity
   T* pbuf1 = vec + 5 * (int64_t)n;
-  T* bx = vec + 6 * (int64_t)n;       // best-so-far iterate (owned)
+  T* bx = vec + 6 * (int64_t)n;        // best-so-far iterate (owned)
   const int tid = blockIdx.x * blockDim.x + threadIdx.x, nth = gridDim.x * blockDim.x;
   const int lane = threadIdx.x & 31;
   const int gw = tid >> 5, nwarps = nth >> 5;
-  unsigned int gen = 0;
-  if (threadIdx.x == 0) gen = *(volatile unsigned int*)&sc->bar_gen;
+  unsigned int target = 0;
 
   // prologue: x0 = 0, r0 = b - S x0 = b, z0 = M^-1 r0, p = z0 (formed on the fly from p_old = 0)
   double s_rz = 0.0, s_bb = 0.0;
@@ -149,14 +206,15 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
     s_rz += (double)bi * (double)zi;
     s_bb += (double)bi * (double)bi;
   }
-  double t = block_sum<T>(s_rz, red);
-  if (threadIdx.x == 0) atomicAdd(&sc->rz0, t);
-  t = block_sum<T>(s_bb, red);
-  if (threadIdx.x == 0) atomicAdd(&sc->bb, t);
-  bool ok = grid_barrier(sc, gen);
+  double t = block_sum(s_bb, red);
+  if (threadIdx.x == 0) part[blockIdx.x].v[1] = t;
+  t = block_sum(s_rz, red);
+  if (threadIdx.x == 0) part[blockIdx.x].v[2] = t;
+  bool ok = grid_barrier(w, flags, ++target);
+  const double bnorm = fmax(sqrt(grid_sum(part, 1, red, &bc)), 1e-12);
+  double rz_old = grid_sum(part, 2, red, &bc);
+  double rn = 0.0, rz_new = 0.0;
 
-  double rz_old = __ldcg(&sc->rz0);
-  const double bnorm = fmax(sqrt(__ldcg(&sc->bb)), 1e-12);
   double best = __longlong_as_double(0x7ff0000000000000LL);   // +inf
   int best_k = 0, k_stop = 0;
   bool converged = false;
@@ -164,8 +222,6 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
     // ---- phase A: decisions on iterate k-1 (identical in every thread) ----
     double beta = 0.0;
     if (k > 1) {
-      const double rn = sqrt(__ldcg(&sc->rr[(k - 1) & 1]));
-      const double rz_new = __ldcg(&sc->rz[(k - 1) & 1]);
       if (rn < best) {                                   // best-so-far iterate
         best = rn;
         best_k = k - 1;
@@ -182,27 +238,28 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
     const T tb = (T)beta;
     double s_pap = 0.0;
     for (int task = gw; task < d.n_mv_tasks; task += nwarps) {   // warp per matvec task
-      const int4 tk = __ldg(d.mv_task + task);           // block row, entries [e0, e1), single
+      const int4 tk = __ldg(d.mv_task + task);           // block row, panel columns [c0, c1), flags
       const int p = tk.x, bp = d.bsize[p], op = d.boff[p];
+      const bool single = tk.w & 1, first = tk.w & 2;
+      // this lane's scalar of the row (lane < bp): its new search direction, loaded early
+      const T pn = lane < bp ? __ldcg(z + op + lane) + tb * __ldcg(pold + op + lane) : T(0);
       T yo[MAXB];
-      task_matvec<T, MAXB>(d, S, bp, tk.y, tk.z, z, pold, tb, lane, yo);
-      const bool first = tk.y == d.sym_ptr[p];
+      panel_matvec<T, MAXB>(d, pan, p, bp, tk.y, tk.z, z, pold, tb, lane, yo);
 #pragma unroll
       for (int rr = 0; rr < MAXB; ++rr) {
         if (lane == rr && rr < bp) {
-          const T pn = __ldcg(z + op + rr) + tb * __ldcg(pold + op + rr);
-          if (tk.w) Ap[op + rr] = yo[rr];                // the row is one task
+          if (single) Ap[op + rr] = yo[rr];              // the row is one task
           else atomicAdd(Ap + op + rr, yo[rr]);          // zeroed by the previous phase B
           if (first) pnew[op + rr] = pn;
           s_pap += (double)pn * (double)yo[rr];          // p.Ap is linear in the row's tasks
         }
       }
     }
-    t = block_sum<T>(s_pap, red);
-    if (threadIdx.x == 0) atomicAdd(&sc->pAp[k & 1], t);
-    if (!(ok = grid_barrier(sc, gen))) break;
-    // ---- phase B: x, r, z and the partial sums of r.r, r.z ----
-    const double alpha = rz_old / fmax(__ldcg(&sc->pAp[k & 1]), 1e-32);
+    t = block_sum(s_pap, red);
+    if (threadIdx.x == 0) part[blockIdx.x].v[0] = t;
+    if (!(ok = grid_barrier(w, flags, ++target))) break;
+    // ---- phase B: x, r, z and the partial sums of r.r and r.z ----
+    const double alpha = rz_old / fmax(grid_sum(part, 0, red, &bc), 1e-32);
     const T ta = (T)alpha;
     double s_rr = 0.0;
     s_rz = 0.0;
@@ -215,16 +272,13 @@ __global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __r
       s_rr += (double)ri * (double)ri;
       s_rz += (double)ri * (double)zi;
     }
-    if (tid == 0) {            // the slots the next iteration accumulates into (last read before now)
-      sc->pAp[(k + 1) & 1] = 0.0;
-      sc->rr[(k + 1) & 1] = 0.0;
-      sc->rz[(k + 1) & 1] = 0.0;
-    }
-    t = block_sum<T>(s_rr, red);
-    if (threadIdx.x == 0) atomicAdd(&sc->rr[k & 1], t);
-    t = block_sum<T>(s_rz, red);
-    if (threadIdx.x == 0) atomicAdd(&sc->rz[k & 1], t);
-    ok = grid_barrier(sc, gen);
+    t = block_sum(s_rr, red);
+    if (threadIdx.x == 0) part[blockIdx.x].v[1] = t;
+    t = block_sum(s_rz, red);
+    if (threadIdx.x == 0) part[blockIdx.x].v[2] = t;
+    if (!(ok = grid_barrier(w, flags, ++target))) break;
+    rn = sqrt(grid_sum(part, 1, red, &bc));
+    rz_new = grid_sum(part, 2, red, &bc);
   }
   // the converging iterate, else the best-so-far one (zeros if none improved)
   for (int i = tid; i < n; i += nth) xo[i] = ok ? (converged ? x[i] : bx[i]) : T(0);
@@ -249,12 +303,22 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
     B3R_REQUIRE(per_sm >= 1, "the PCG kernel does not fit on an SM");
   }
   const int want = (d.n_mv_tasks * 32 + kPcgThreads - 1) / kPcgThreads;   // one warp per matvec task
-  const int grid = std::max(1, std::min(want, per_sm * n_sm));     // all co-resident
-  PcgScalars* sc = reinterpret_cast<PcgScalars*>(work);
-  T* vec = reinterpret_cast<T*>(reinterpret_cast<char*>(work) + 256);
-  B3R_TRY(check_cuda(cudaMemsetAsync(sc, 0, sizeof(PcgScalars), s), "clear PCG scalars"));
+#ifndef B3R_PCG_BLOCKS_PER_SM
+#define B3R_PCG_BLOCKS_PER_SM 0   // 0: as many as fit (more blocks make each grid barrier dearer)
+#endif
+  const int cap = B3R_PCG_BLOCKS_PER_SM > 0 ? std::min(per_sm, B3R_PCG_BLOCKS_PER_SM) : per_sm;
+  const int grid = std::max(1, std::min(want, cap * n_sm));        // all co-resident
+  B3R_REQUIRE(grid <= kPcgMaxBlocks, "internal: PCG grid %d > %d", grid, kPcgMaxBlocks);
+  // barrier words and arrival flags start at zero (targets count up from 1 in every launch)
+  B3R_TRY(check_cuda(cudaMemsetAsync(work, 0, kPcgPartOff, s), "clear PCG barrier words"));
   DevPlan dv = d;
-  void* args[] = {&dv, &S, &M, &b, &xo, &tol, &maxiter, &vec, &sc, &result};
+  char* wk = reinterpret_cast<char*>(work);
+  float* pan = reinterpret_cast<float*>(wk + pcg_panel_off(d));
+  const int n_ent = (int)(2 * d.nnzb - d.nb);             // symmetric entries
+  k_build_panels<<<grid_for((int64_t)n_ent * 32, 256), 256, 0, s>>>(dv, S, pan);
+  B3R_TRY(check_launch("pcg panels"));
+  const float* panc = pan;
+  void* args[] = {&dv, &S, &M, &b, &xo, &tol, &maxiter, &wk, &panc, &result};
   B3R_TRY(check_cuda(cudaLaunchCooperativeKernel((const void*)k_pcg<T, MAXB>, dim3(grid), dim3(kPcgThreads), args,
                                                  0, s),
                      "pcg cooperative launch"));
@@ -286,7 +350,7 @@ using namespace b3r;
 
 extern "C" int64_t b3r_pcg_work_bytes(const b3r_plan* plan) {
   if (!plan) return -1;
-  return 256 + 7 * 8 * (int64_t)plan->d.n_cam_params;
+  return (int64_t)pcg_panel_off(plan->d) + 4 * plan->d.pan_floats;
 }
 
 extern "C" int b3r_pcg(const b3r_plan* plan, const float* S_vals, const float* precond, const float* b, float* x,

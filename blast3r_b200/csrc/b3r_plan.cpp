@@ -81,6 +81,9 @@ struct PlanBuild {
   std::vector<int4> t_idx, c1_idx;
   std::vector<int> sym_ptr, sym_ent;
   std::vector<int4> mv_task, mv_ent;
+  std::vector<int64_t> pan_off;
+  std::vector<int> pan_w, col_off, pan_col, ent_col, ent_row;
+  int64_t pan_floats = 0;
   int64_t nnz = 0;
 };
 
@@ -463,11 +466,30 @@ static int build_pattern(PlanBuild& B) {
       const int q = tr ? B.blk_row[blk] : B.col_idx[blk];
       B.mv_ent[e] = make_int4(B.val_off[blk], B.boff[q], B.bsize[q], tr);
     }
+    // row panels and matvec tasks (column chunks of <= kMvCols)
+    B.pan_off.resize(nb); B.pan_w.resize(nb); B.col_off.resize(nb);
+    B.ent_col.resize(B.sym_ent.size()); B.ent_row.resize(B.sym_ent.size());
+    int64_t poff = 0;
+    int coff = 0;
     for (int pr = 0; pr < nb; ++pr) {
-      const int e0 = B.sym_ptr[pr], e1 = B.sym_ptr[pr + 1];
-      const int single = (e1 - e0) <= kMvTask;
-      for (int e = e0; e < e1; e += kMvTask) B.mv_task.push_back(make_int4(pr, e, std::min(e + kMvTask, e1), single));
+      int w = 0;
+      for (int e = B.sym_ptr[pr]; e < B.sym_ptr[pr + 1]; ++e) {
+        B.ent_col[e] = w;
+        B.ent_row[e] = pr;
+        const int q = B.mv_ent[e].y;                      // column scalar offset
+        for (int c2 = 0; c2 < B.mv_ent[e].z; ++c2) B.pan_col.push_back(q + c2);
+        w += B.mv_ent[e].z;
+      }
+      B.pan_w[pr] = w;
+      B.col_off[pr] = coff;
+      B.pan_off[pr] = poff;
+      coff += w;
+      poff += ((int64_t)B.bsize[pr] * w + 3) & ~int64_t(3);   // 16-byte aligned panels
+      const int single = w <= kMvCols ? 1 : 0;
+      for (int c0 = 0; c0 < w; c0 += kMvCols)
+        B.mv_task.push_back(make_int4(pr, c0, std::min(c0 + kMvCols, w), single | (c0 == 0 ? 2 : 0)));
     }
+    B.pan_floats = poff;
   }
   // diagonal scalar positions
   const int ncp = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
@@ -579,6 +601,9 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
   A.add(B.mv_task, &d.mv_task); A.add(B.mv_ent, &d.mv_ent);
   d.n_mv_tasks = (int)B.mv_task.size();
+  A.add(B.pan_off, &d.pan_off); A.add(B.pan_w, &d.pan_w); A.add(B.col_off, &d.col_off);
+  A.add(B.pan_col, &d.pan_col); A.add(B.ent_col, &d.ent_col); A.add(B.ent_row, &d.ent_row);
+  d.pan_floats = B.pan_floats;
   if (!host_only) {
     int rc = A.upload(&P->dev_mem);
     cudaSetDevice(prev_dev);

@@ -22,7 +22,7 @@ constexpr int kPairTask = 2048;    // max observation pairs per pair task
 constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal chunk
 constexpr int kPointTask = 32;     // max observations per point task (one warp)
 constexpr int kImgRecFloats = 32;  // floats per per-image camera record
-constexpr int kMvTask = 64;        // max symmetric entries per matvec task
+constexpr int kMvCols = 256;       // max panel columns per matvec task (8 per lane)
 
 // sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
 constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
@@ -91,9 +91,20 @@ struct DevPlan {
   // matvec work: symmetric block rows cut into tasks of <= kMvTask entries (a dense row,
   // e.g. the shared focal block of a mono-camera rig, spreads over many warps)
   int n_mv_tasks;
-  const int4* mv_task;    // [n_mv_tasks] (block row, first entry, end entry, row is one task)
+  const int4* mv_task;    // [n_mv_tasks] (block row, first panel column, end panel column,
+                          //  1 if the row is one task | 2 if this is the row's first task)
   const int4* mv_ent;     // [2*nnzb - nb] (value offset, column scalar offset, column block size,
                           //  1 if the entry is the transpose of the stored block)
+  // row panels of the symmetric S for the PCG matvec: block row p is a dense bp x W_p
+  // row-major panel (its entries' blocks side by side, transposes already flipped) at
+  // float offset pan_off[p], with the W_p scalar columns at pan_col[col_off[p] ..]
+  int64_t pan_floats;
+  const int64_t* pan_off; // [nb]
+  const int* pan_w;       // [nb] W_p
+  const int* col_off;     // [nb]
+  const int* pan_col;     // [sum W_p]
+  const int* ent_col;     // [2*nnzb - nb] first panel column of each symmetric entry
+  const int* ent_row;     // [2*nnzb - nb] block row of each symmetric entry
 };
 
 struct HostPattern {
