@@ -165,6 +165,22 @@ class BAPlan:
         L.call('b3r_linearize_schur', self._h, C.byref(params), C.byref(opts), ws, C.byref(out), s)
         return SchurSystem(self, S, b, dA, pc, hm, ws, params, opts)
 
+    def capture(self, params, opts, outputs=None):
+        """CUDA graph of one full linearization on fixed buffers (the tensors `params` points
+        at and the outputs): each replay relinearizes at those tensors' current values with one
+        launch from the host.  For latency-bound problems (online windows), where the seven
+        kernel launches and three clears cost as much as the work.  Returns (graph, system)."""
+        outs = outputs if outputs is not None else self.new_outputs()
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.linearize(params, opts, outs)     # one-time setup (attributes, staging) outside the graph
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            system = self.linearize(params, opts, outs)
+        return g, system
+
     def lin_stage(self, name, params, opts, outputs, stream=None):
         """One stage ('points', 'assemble', 'finalize') of a sharded linearization."""
         S, b, dA, pc, hm = outputs
