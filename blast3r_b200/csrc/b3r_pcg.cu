@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(256) k_build_panels(DevPlan d, const float* __
 }
 
 // The lanes of a warp compute the part of y_p = sum_c panel_p[r][c] x[col_c] over panel
-// columns [c0, c1) of block row p (at most kMvCols = 512, so at most 16 per lane), with
+// columns [c0, c1) of block row p (at most kMvCols = 256, so at most eight per lane), with
 // x = z + beta * pold formed on the fly.  The panel rows are read coalesced (consecutive
 // lanes, consecutive columns) and so mostly are the x values (a block's columns are
 // consecutive scalars).  Every lane returns the partial y_p[r] (r < bp) in yo.

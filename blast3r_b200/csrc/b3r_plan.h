@@ -88,7 +88,7 @@ struct DevPlan {
   // transpose of a stored block (q, p) with q < p
   const int* sym_ptr;     // [nb+1]
   const int* sym_ent;     // [2*nnzb - nb]
-  // matvec work: symmetric block rows cut into tasks of <= kMvTask entries (a dense row,
+  // matvec work: row panels cut into tasks of <= kMvCols columns (a dense row,
   // e.g. the shared focal block of a mono-camera rig, spreads over many warps)
   int n_mv_tasks;
   const int4* mv_task;    // [n_mv_tasks] (block row, first panel column, end panel column,
