@@ -174,8 +174,11 @@ __device__ __forceinline__ void panel_matvec(const DevPlan& d, const float* __re
   }
 }
 
+// Three blocks per SM (<= 85 registers): more resident warps than matvec tasks leaves fewer
+// warps with two tasks, and the slowest warp sets each iteration's pace (8.0 vs 9.8 ms for
+// the cfg2 solve with two blocks per SM).
 template <typename T, int MAXB>
-__global__ void __launch_bounds__(kPcgThreads) k_pcg(DevPlan d, const float* __restrict__ S,
+__global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* __restrict__ S,
                                                      const float* __restrict__ M, const T* __restrict__ b,
                                                      T* __restrict__ xo, double tol, int maxiter, char* work,
                                                      const float* __restrict__ pan, int* result) {
