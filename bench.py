@@ -420,6 +420,34 @@ def run_b200(args):
                    'loss': [float(last['st'].init_loss), float(last['st'].new_loss)],
                    'what': 'engine.lm_step: residual op, fused linearization, PCG on S (tol 1e-6, <=300 it), '
                            'back-substitution, line search'}
+    else:
+        # the sharded step: sharded linearization, PCG on the root, delta_c broadcast, local
+        # back-substitution, delta_p all-reduced, the line search on every rank
+        from blast3r_b200.distributed import sharded_lm_step
+        last = {}
+
+        def lm():
+            _, st = sharded_lm_step(sharded, t['rigs'], t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], t['K'],
+                                    t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], pnorm=o['pnorm'],
+                                    clip_pix_err=o['clip_pix_err'], huber_delta=o['huber_delta'],
+                                    weight_z=o['weight_z'], dtype=torch.float64)
+            last['st'] = st
+        plan.stage_obs(t['pix2d'], t['pix2d_std'], t['pix2d_dep'])
+        lm()
+        torch.cuda.synchronize()
+        dist.barrier()
+        n_lm = 3
+        e0.record()
+        for _ in range(n_lm):
+            lm()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_lm = torch.tensor([e0.elapsed_time(e1) / n_lm], dtype=torch.float64, device=dev)
+        dist.all_reduce(ms_lm, op=dist.ReduceOp.MAX)
+        lm_info = {'ms': float(ms_lm.item()), 'loss': [float(last['st'].init_loss), float(last['st'].new_loss)],
+                   'what': 'distributed.sharded_lm_step: residual op, track-sharded linearization with the NCCL '
+                           'reduce, PCG on S on rank 0, delta_c broadcast, local back-substitution, delta_p '
+                           'all-reduce, line search (max over ranks)'}
 
     if rank == 0:
         peak, peak_kind = measured_peaks()

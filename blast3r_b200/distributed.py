@@ -57,3 +57,54 @@ class ShardedSchur:
         if self.rank == self.root:
             self.plan.lin_stage('finalize', params, opts, self.outputs)
         return self
+
+
+def sharded_lm_step(sharded, rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_coefs, pts3d,
+                    depth_mode='log', pnorm=1, clip_pix_err=100, huber_delta=0.5, min_reproj=0.01, dampen=1e-12,
+                    min_loss_delta=1e-4, weight_z=1, dtype=torch.float32, verbose=False):
+    """One Levenberg-Marquardt step (engine.py:206-334) over track-sharded ranks.
+
+    Every rank holds all inputs.  The linearization is sharded (``ShardedSchur``); the root
+    solves S delta_c = b with the device PCG and broadcasts delta_c; each rank back-substitutes
+    its own tracks' points and one all-reduce (SUM) assembles delta_p; the objective (the
+    residual op over all observations, cheap next to the linearization) is evaluated on every
+    rank, so the line search takes the same decisions everywhere and every rank ends with the
+    same parameters.  The plan must enable whole parameter types (bool optim flags, the
+    reference's default), not masks.  Returns (update, BA_Status) like ``engine.lm_step``.
+    """
+    from .cujac import residuals_with_rigs as residual_func
+    from .engine import BA_Status, line_search
+    from .plan import BAPlan
+    plan = sharded.plan
+    is_log = depth_mode == 'log'
+
+    def objective(K, P_w2rig, pts3d, z_coefs):
+        res, err, w = residual_func(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep,
+                                    is_log, weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
+        return err.mean(), res, w
+
+    init_loss, init_residuals, _ = objective(K, P_w2rig, pts3d, z_coefs)
+    lo = BAPlan.lin_opts(is_depth_log=is_log, weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err,
+                         huber_delta=huber_delta, dampen=dampen)
+    p = plan.params(K, P_rig2cam, P_w2rig, z_coefs, pts3d, pix2d_std, pix2d_dep, pix2d=pix2d)
+    sharded.linearize(p, lo)
+    dt = torch.float64 if dtype == torch.float64 else torch.float32
+    if sharded.rank == sharded.root:
+        dc, _, _ = plan.pcg(sharded.S, sharded.precond, sharded.b.to(dt), tol=1e-6, maxiter=300)
+    else:
+        dc = torch.empty(plan.n_cam_params, dtype=dt, device=plan.device)
+    if sharded.world > 1:
+        dist.broadcast(dc, src=sharded.root, group=sharded.group)
+    dp = plan.backsub(p, lo, plan.workspace(), dc)        # this rank's tracks, zeros elsewhere
+    if sharded.world > 1:
+        dist.all_reduce(dp, op=dist.ReduceOp.SUM, group=sharded.group)
+    delta = torch.cat([dc.to(torch.float32), dp])
+    i = plan.info
+    n_cams, n_nodes, n_imgs, n_pts, C = i.nb_K, i.nb_P, i.nb_Z, i.n_points, plan.C
+    sizes = [2 * n_cams, 6 * n_nodes, C * n_imgs, 3 * n_pts]
+    assert delta.numel() == sum(sizes)
+    dK, dP, dZ, dX = delta.split(sizes)
+    update, new_loss, new_res = line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, dK.view(n_cams, 2),
+                                            dP.view(n_nodes, 6), dZ.view(n_imgs, C), dX.view(n_pts, 3), init_loss,
+                                            init_residuals, min_reproj, min_loss_delta, verbose)
+    return update, BA_Status(init_loss, init_residuals, new_loss, new_res)

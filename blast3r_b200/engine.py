@@ -46,6 +46,40 @@ def reproj_score(res):
     return reproj_err[:n80].mean()
 
 
+def line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P, delta_zcf, delta_pts, init_loss,
+                init_residuals, min_reproj=0.01, min_loss_delta=1e-4, verbose=False):
+    """The reference's step-size search (engine.py:303-333): scales 1, 1/2, 1/4, 1/8, 1/64,
+    1/512, 1/4096, 0 of `delta` (whose views are delta_K, delta_P, delta_zcf, delta_pts), the
+    first that lowers the loss without collapsing the reprojection residual.  Returns
+    (update, new_loss, new_residuals)."""
+    update = dict()
+    last_a = 1
+    new_loss, new_residuals = init_loss, init_residuals
+    for a in [0.5, 0.25, 0.125, 1 / 64, 1 / 512, 1 / 4096, 0]:
+        update['K'] = update_K(K, delta_K)
+        update['P_w2rig'] = (exp_se3(-delta_P) @ P_w2rig).contiguous()
+        update['z_coefs'] = (z_coefs - delta_zcf).contiguous()
+        update['pts3d'] = (pts3d - delta_pts).contiguous()
+        new_loss, new_residuals, _ = objective(**update)
+        if new_loss.isnan():
+            if verbose:
+                print('Warning: loss is NaN')
+            new_loss = init_loss
+        new_loss = new_loss + min_loss_delta
+        new_reproj = float(reproj_score(new_residuals))
+        degenerate = new_reproj < min_reproj
+        if degenerate and verbose:
+            print(f'Rejecting step: reprojection residual collapsed to {new_reproj:.2e}')
+        if new_loss < init_loss and not degenerate:
+            break
+        delta *= a / last_a          # scales (delta_K, ..., delta_pts): they are views of delta
+        last_a = a
+    else:
+        if verbose:
+            print('Warning: loss is not decreasing')
+    return update, new_loss, new_residuals
+
+
 def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_coefs, pts3d, depth_mode='log',
             pnorm=1, clip_pix_err=100, huber_delta=0.5, min_reproj=0.01, dampen=1e-12, min_loss_delta=1e-4,
             weight_z=1, log_depth_maps=None, conf=None, pts3d_ref=None, weight_tan=0.0, tan_stride=4,
@@ -94,29 +128,7 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
     delta = jac.solve_delta(J, init_residuals, w_pts, lin_kw=lin_kw)
     delta_K, delta_P, delta_zcf, delta_pts = jac.unpack_delta_inplace(delta)
 
-    update = dict()
-    last_a = 1
-    new_loss, new_residuals = init_loss, init_residuals
-    for a in [0.5, 0.25, 0.125, 1 / 64, 1 / 512, 1 / 4096, 0]:
-        update['K'] = update_K(K, delta_K)
-        update['P_w2rig'] = (exp_se3(-delta_P) @ P_w2rig).contiguous()
-        update['z_coefs'] = (z_coefs - delta_zcf).contiguous()
-        update['pts3d'] = (pts3d - delta_pts).contiguous()
-        new_loss, new_residuals, _ = objective(**update)
-        if new_loss.isnan():
-            if verbose:
-                print('Warning: loss is NaN')
-            new_loss = init_loss
-        new_loss = new_loss + min_loss_delta
-        new_reproj = float(reproj_score(new_residuals))
-        degenerate = new_reproj < min_reproj
-        if degenerate and verbose:
-            print(f'Rejecting step: reprojection residual collapsed to {new_reproj:.2e}')
-        if new_loss < init_loss and not degenerate:
-            break
-        delta *= a / last_a          # scales (delta_K, ..., delta_pts): they are views of delta
-        last_a = a
-    else:
-        if verbose:
-            print('Warning: loss is not decreasing')
+    update, new_loss, new_residuals = line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P,
+                                                  delta_zcf, delta_pts, init_loss, init_residuals, min_reproj,
+                                                  min_loss_delta, verbose)
     return update, BA_Status(init_loss, init_residuals, new_loss, new_residuals)

@@ -71,3 +71,52 @@ def test_two_gpu_sharded_schur_equals_single_gpu(cfg, tmp_path):
     mp.spawn(_rank_main, args=(2, _free_port(), cfg, out), nprocs=2, join=True)
     errs = np.load(out)
     assert (errs < 1e-4).all(), errs
+
+
+def _lm_rank_main(rank, world, port, result_path):
+    from blast3r_b200.distributed import ShardedSchur, shard_tracks, sharded_lm_step
+    from blast3r_b200.engine import lm_step
+    from blast3r_b200.plan import BAPlan
+    from blast3r_b200.synthetic import make_scene
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
+    torch.cuda.set_device(rank)
+    dev = torch.device('cuda', rank)
+    dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        sc = make_scene(1, n_imgs=60, n_tracks=6000)
+        o = sc.options
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
+        t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+        plan = BAPlan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, track_range=(t0, t1),
+                      device=dev)
+        args = (t['rigs'], t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], t['K'], t['P_rig2cam'],
+                t['P_w2rig'], t['z_coefs'], t['pts3d'])
+        kw = dict(pnorm=o['pnorm'], clip_pix_err=o['clip_pix_err'], huber_delta=o['huber_delta'],
+                  weight_z=o['weight_z'], dtype=torch.float64)
+        upd, st = sharded_lm_step(ShardedSchur(plan), *args, **kw)
+        torch.cuda.synchronize()
+        if rank == 0:
+            ref, st_ref = lm_step(*args, **kw)
+            torch.cuda.synchronize()
+
+            def step_err(key):
+                a = (upd[key] - t[key]).double().cpu().numpy()
+                b = (ref[key] - t[key]).double().cpu().numpy()
+                return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+            loss_err = abs(float(st.new_loss) - float(st_ref.new_loss)) / abs(float(st_ref.init_loss))
+            np.save(result_path, np.array([step_err(k) for k in ('K', 'P_w2rig', 'z_coefs', 'pts3d')] + [loss_err]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+def test_two_gpu_lm_step_equals_single_gpu(tmp_path):
+    """The sharded LM step (PCG on rank 0, delta_c broadcast, local back-substitution,
+    delta_p all-reduced) against the one-GPU lm_step: the same update within the spread of
+    two float summation orders of S."""
+    out = str(tmp_path / 'lm_errs.npy')
+    mp.spawn(_lm_rank_main, args=(2, _free_port(), out), nprocs=2, join=True)
+    errs = np.load(out)
+    assert (errs < 1e-3).all(), errs
