@@ -114,9 +114,14 @@ def _lm_rank_main(rank, world, port, result_path):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
 def test_two_gpu_lm_step_equals_single_gpu(tmp_path):
     """The sharded LM step (PCG on rank 0, delta_c broadcast, local back-substitution,
-    delta_p all-reduced) against the one-GPU lm_step: the same update within the spread of
-    two float summation orders of S."""
+    delta_p all-reduced) against the one-GPU lm_step.  The two S differ only in the float
+    summation order of the partial systems; the step moves by that rounding times the
+    conditioning: K, poses and points within 1e-3, the depth coefficients (weakly
+    constrained at omega = 1e-4: the reference's own float32 step lies 2.8e-3 from its
+    float64 step on the mono golden case) within 1e-2, and the same new loss (1e-5)."""
     out = str(tmp_path / 'lm_errs.npy')
     mp.spawn(_lm_rank_main, args=(2, _free_port(), out), nprocs=2, join=True)
-    errs = np.load(out)
-    assert (errs < 1e-3).all(), errs
+    e_K, e_P, e_Z, e_X, e_loss = np.load(out)
+    assert e_K < 1e-3 and e_P < 1e-3 and e_X < 1e-3, (e_K, e_P, e_X)
+    assert e_Z < 1e-2, e_Z
+    assert e_loss < 1e-5, e_loss
