@@ -436,14 +436,18 @@ __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
   if (tl == 0) c.misc[1] = lam;   // point damping, reused by the back-substitution
   if (tl >= c.d.nT_loc) return;
-  float* t = c.trec + (int64_t)tl * 24;
-  const float h00 = t[0] + lam, h01 = t[1], h02 = t[2], h11 = t[3] + lam, h12 = t[4], h22 = t[5] + lam;
+  // the 96-byte track record as 16-byte pieces (the workspace is 256-byte aligned)
+  float4* t4 = reinterpret_cast<float4*>(c.trec + (int64_t)tl * 24);
+  const float4 a = t4[0], b = t4[1];
+  const float g8 = c.trec[(int64_t)tl * 24 + 8];
+  const float h00 = a.x + lam, h01 = a.y, h02 = a.z, h11 = a.w + lam, h12 = b.x, h22 = b.y + lam;
   float l[6], z[3];
   chol3<float>(h00, h01, h02, h01, h11, h12, h02, h12, h22, 1e-12f, l);
-  const float g[3] = {t[6], t[7], t[8]};
+  const float g[3] = {b.z, b.w, g8};
   chol3_fwd<float>(l, g, z);
-  t[12] = 1.f / l[0]; t[13] = l[1]; t[14] = l[2]; t[15] = 1.f / l[3]; t[16] = l[4]; t[17] = 1.f / l[5];
-  t[18] = z[0]; t[19] = z[1]; t[20] = z[2];
+  t4[3] = make_float4(1.f / l[0], l[1], l[2], 1.f / l[3]);    // floats 12..15
+  t4[4] = make_float4(l[4], 1.f / l[5], z[0], z[1]);          // floats 16..19
+  t4[5] = make_float4(z[2], 0.f, 0.f, 0.f);                   // floats 20..23 (21..23 unused)
 }
 
 // ------------------------------------------------------------------------------------
