@@ -87,6 +87,8 @@ _SIGS = {
     'b3r_schur_spmv_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     'b3r_backsub': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp, _vp, _vp, _vp]),
     'b3r_pcg_work_bytes': (_i64, [_vp]),
+    'b3r_reproj_score_work_bytes': (_i64, [_i64]),
+    'b3r_reproj_score': (C.c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     'b3r_pcg': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
     'b3r_pcg_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
 }

@@ -12,6 +12,7 @@ from collections import namedtuple
 
 import torch
 
+from . import _lib as L
 from .ba_solver import GaussNewtonSolver
 from .cujac import exp_se3, residuals_with_rigs as residual_func
 
@@ -39,11 +40,20 @@ def update_K(K0, delta_focal, min_f=100):
 
 
 def reproj_score(res):
-    """Mean of the best 80% reprojection errors (engine.py:357-361)."""
-    reproj_err = res[:, :2].norm(dim=-1)
-    reproj_err = reproj_err.sort().values
-    n80 = len(reproj_err) * 80 // 100
-    return reproj_err[:n80].mean()
+    """Mean of the best 80% reprojection errors ||res[i, :2]|| (engine.py:357-361), on the
+    device without a sort: the library's exact radix select (b3r_reproj_score) finds the
+    k-th smallest error and sums the ones below it.  `res` is an (n, >=2) float32 CUDA tensor
+    of any strides (the residual op's output is a component-major view).  Returns a 0-d
+    device tensor."""
+    assert res.is_cuda and res.dtype == torch.float32 and res.dim() == 2, 'an (n, >=2) float32 CUDA tensor'
+    n = res.shape[0]
+    work = torch.empty(int(L.lib().b3r_reproj_score_work_bytes(n)) // 4 + 64, dtype=torch.float32, device=res.device)
+    ptr = work.data_ptr()
+    ptr += (-ptr) % 256
+    out = torch.empty(1, dtype=torch.float32, device=res.device)
+    L.call('b3r_reproj_score', res.data_ptr(), n, max(res.stride(0), 1), max(res.stride(1), 1), ptr,
+           out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    return out[0]
 
 
 def line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P, delta_zcf, delta_pts, init_loss,

@@ -265,6 +265,18 @@ int b3r_pcg(const b3r_plan* plan, const float* S_vals, const float* precond, con
 int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond, const double* b, double* x,
                 double tol, int maxiter, void* work, int* result, void* stream);
 
+/* The line search's reprojection score (the reference's reproj_score, inference/engine.py
+ * :357-361, used by its step reject at :308-333): the mean of the floor(0.8 n) smallest
+ * per-observation errors sqrt(x_i^2 + y_i^2), x_i = residuals[i * stride_obs],
+ * y_i = residuals[i * stride_obs + stride_comp] (b3r_residuals_with_rigs writes component-
+ * major rows: stride_obs 1, stride_comp n_obs).  Found by an exact radix select instead of
+ * a sort.  `work`: 256-byte aligned device buffer of
+ * b3r_reproj_score_work_bytes(n_obs) bytes; `score`: one device float (NaN when
+ * floor(0.8 n) == 0, like the reference's empty mean). */
+int64_t b3r_reproj_score_work_bytes(int64_t n_obs);
+int b3r_reproj_score(const float* residuals, int64_t n_obs, int64_t stride_obs, int64_t stride_comp, void* work,
+                     float* score, void* stream);
+
 /* One pass of b3r_lin_points/b3r_lin_assemble on its own (profiling and custom
  * pipelines): B3R_PASS_PREP (per-image records), _POINTS (per-track Hpp, g_p), _FACTOR
  * (damped per-track Cholesky factors), _DIAG (elimination records and per-image diagonal
