@@ -11,7 +11,8 @@
 //   k_score_hist   level 0: compute each error (written once, compact) and histogram its top
 //                  11 bits; levels 1, 2: histogram the next bits of the errors whose higher
 //                  bits match the selected prefix (block-private shared-memory histograms)
-//   k_score_pick   one block: find the bin holding the k-th error, extend the prefix
+//   k_score_pick   one block: find the bin holding the k-th error (block prefix sum over the
+//                  bins), extend the prefix
 //   k_score_sum    sum and count of the errors below the k-th; the last block writes the score
 #include <algorithm>
 #include "b3r_common.cuh"
@@ -55,7 +56,7 @@ __global__ void __launch_bounds__(kScoreThreads) k_score_hist(const float* __res
     } else {
       e = err[i];
     }
-    const unsigned int u = __float_as_uint(e);
+    const unsigned int u = __float_as_uint(e) & 0x7FFFFFFFu;   // a NaN's sign bit aside, e >= 0
     if (level == 0 || (u >> hs) == prefix) atomicAdd(&h[(u >> sh) & (nb - 1)], 1u);
   }
   __syncthreads();
@@ -64,19 +65,42 @@ __global__ void __launch_bounds__(kScoreThreads) k_score_hist(const float* __res
 }
 
 // One block: the bin of this level that holds the rank-th error; rank becomes the rank
-// within that bin and the prefix gains the bin's digit.
-__global__ void __launch_bounds__(32) k_score_pick(ScoreState* st, int level, int64_t k) {
-  if (threadIdx.x != 0) return;
-  const int nb = digit_bins(level);
-  unsigned long long r = level == 0 ? (unsigned long long)k : st->rank, acc = 0;
-  int bin = nb - 1;
-  for (int b = 0; b < nb; ++b) {
-    const unsigned long long c = st->hist[level][b];
-    if (acc + c >= r) { bin = b; break; }
-    acc += c;
+// within that bin and the prefix gains the bin's digit.  Each thread owns a run of
+// consecutive bins (8 at 11-bit levels, 2 at the last); a block-wide prefix sum of the run
+// totals tells the one thread whose run holds the rank-th error, which walks its run.  A
+// rank beyond every count (errors that fell out of the prefix test) selects the last bin.
+constexpr int kPickThreads = 256;
+__global__ void __launch_bounds__(kPickThreads) k_score_pick(ScoreState* st, int level, int64_t k) {
+  __shared__ unsigned long long wsum[kPickThreads / 32];
+  const int nb = digit_bins(level), per = nb / kPickThreads, b0 = threadIdx.x * per;
+  const unsigned long long r = level == 0 ? (unsigned long long)k : st->rank;
+  unsigned long long c[kBins / kPickThreads], tot = 0;
+#pragma unroll
+  for (int j = 0; j < kBins / kPickThreads; ++j) {
+    c[j] = j < per ? (unsigned long long)st->hist[level][b0 + j] : 0ull;
+    tot += c[j];
   }
-  st->rank = r - acc;
-  st->prefix = (level == 0 ? 0u : st->prefix << (level == 1 ? 11 : 9)) | (unsigned int)bin;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  unsigned long long inc = tot;                          // inclusive scan within the warp
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += v;
+  }
+  if (lane == 31) wsum[w] = inc;
+  __syncthreads();
+  unsigned long long acc = inc - tot;                    // errors in the bins before this run
+  for (int i = 0; i < w; ++i) acc += wsum[i];
+  const bool last = threadIdx.x == kPickThreads - 1;
+  if ((acc < r && r <= acc + tot) || (last && r > acc + tot)) {
+    int bin = b0 + per - 1;
+    for (int j = 0; j < per; ++j) {
+      if (acc + c[j] >= r) { bin = b0 + j; break; }
+      acc += c[j];
+    }
+    st->rank = r - acc;
+    st->prefix = (level == 0 ? 0u : st->prefix << (level == 1 ? 11 : 9)) | (unsigned int)bin;
+  }
 }
 
 __global__ void __launch_bounds__(kScoreThreads) k_score_sum(const float* __restrict__ err, int64_t n, int64_t k,
@@ -139,7 +163,7 @@ extern "C" int b3r_reproj_score(const float* residuals, int64_t n_obs, int64_t s
   for (int level = 0; level < 3; ++level) {
     k_score_hist<<<grid, kScoreThreads, 0, s>>>(residuals, n_obs, stride_obs, stride_comp, err, st, level);
     B3R_TRY(check_launch("score histogram"));
-    k_score_pick<<<1, 32, 0, s>>>(st, level, k);
+    k_score_pick<<<1, kPickThreads, 0, s>>>(st, level, k);
     B3R_TRY(check_launch("score pick"));
   }
   k_score_sum<<<grid, kScoreThreads, 0, s>>>(err, n_obs, k, st, score);

@@ -21,7 +21,8 @@ def sort_score(res):
 
 
 @pytest.mark.parametrize('n,kind', [(1, 'gauss'), (2, 'gauss'), (5, 'gauss'), (1000, 'gauss'), (1000, 'ties'),
-                                    (1000, 'zeros'), (1 << 20, 'gauss'), (1 << 20, 'ties'), (300001, 'wide')])
+                                    (1000, 'zeros'), (1 << 20, 'gauss'), (1 << 20, 'ties'), (300001, 'wide'),
+                                    (1000, 'fewnan'), (1000, 'mostnan')])
 def test_score_matches_sort(n, kind):
     g = torch.Generator(device='cpu').manual_seed(n)
     if kind == 'gauss':
@@ -30,13 +31,16 @@ def test_score_matches_sort(n, kind):
         r = torch.randint(0, 4, (n, 9), generator=g).float()
     elif kind == 'zeros':
         r = torch.zeros(n, 9)
-    else:                          # errors spread over many decades
+    elif kind == 'wide':           # errors spread over many decades
         r = torch.randn(n, 9, generator=g) * torch.exp(8 * torch.randn(n, 1, generator=g))
+    else:                          # NaN errors sort last: a few leave a finite score, many a NaN one
+        r = torch.randn(n, 9, generator=g)
+        r[torch.rand(n, generator=g) < (0.05 if kind == 'fewnan' else 0.5), 0] = float('nan')
     r = r.cuda()
     view = r.view(-1, 3, 3).unbind(dim=1)[0]           # the residual columns, row stride 9
     got = float(reproj_score(view))
     want = sort_score(view)
-    if n * 80 // 100 == 0:
+    if n * 80 // 100 == 0 or math.isnan(want):
         assert math.isnan(got) and math.isnan(want)
     else:
         assert abs(got - want) <= 1e-6 * max(abs(want), 1e-30), (got, want)
