@@ -40,51 +40,68 @@ inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the seven
 }
 
 struct PcgWords {
-  unsigned int bar_gen, abort_flag;
+  unsigned int bar_gen, unused;
 };
 // per-block partial sums: [0] p.Ap, [1] r.r, [2] r.z (prologue: b.b and r0.z0)
 struct PcgPart {
   double v[4];
 };
 
-// Grid barrier for a cooperative launch: every block publishes its arrival as flags[block] =
-// target; block 0 waits until every flag holds the target, then publishes bar_gen = target,
-// which the other blocks wait for.  Every poll is bounded (kBarrierSpins); a poll that
-// gives up raises abort_flag, which every block checks after each barrier, so all of them
-// leave the loop together.
-__device__ __forceinline__ bool grid_barrier(PcgWords* w, volatile unsigned int* flags, unsigned int target) {
+constexpr unsigned int kGenAbort = 0x80000000u;   // in bar_gen: the barrier was abandoned
+constexpr unsigned int kFlagAbort = 0xFFFFFFFFu;  // a block's flag once it gave up waiting
+
+__device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier for a cooperative launch: after a block-wide __syncthreads, thread 0 of every
+// block publishes its arrival with a release store flags[block] = target; block 0's threads
+// acquire-poll the flags, then thread 0 of block 0 release-stores bar_gen = target, which
+// thread 0 of every other block acquire-polls before a block-wide __syncthreads (the
+// release/acquire pair and the CTA barriers order every thread's writes before the barrier
+// with every thread's reads after it).  Every poll is bounded (kBarrierSpins).  A block
+// that gives up waiting for bar_gen leaves with false and sets its flag to kFlagAbort; block
+// 0, seeing such a flag or giving up on one, publishes bar_gen with kGenAbort, and every
+// block that reads it leaves with false, so all of them leave the loop at this barrier or
+// the next one.
+__device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, unsigned int target) {
   __shared__ int ok_s;
   __syncthreads();                                       // the block's writes precede its arrival
   if (threadIdx.x == 0) {
-    __threadfence();
-    flags[blockIdx.x] = target;
     ok_s = 1;
+    st_release(flags + blockIdx.x, target);
   }
   __syncthreads();
   if (blockIdx.x == 0) {
+    bool bad = false;
     for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
       int spins = 0;
-      while (flags[b] < target) {
-        if (++spins > kBarrierSpins) { atomicExch(&w->abort_flag, 1u); ok_s = 0; break; }
+      unsigned int f;
+      while ((f = ld_acquire(flags + b)) < target) {
+        if (++spins > kBarrierSpins) break;
         __nanosleep(32);
       }
+      if (f < target || f == kFlagAbort) bad = true;
     }
+    if (bad) ok_s = 0;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      *(volatile unsigned int*)&w->bar_gen = target;
-    }
+    if (threadIdx.x == 0) st_release(&w->bar_gen, target | (ok_s ? 0u : kGenAbort));
   } else if (threadIdx.x == 0) {
-    volatile unsigned int* vg = &w->bar_gen;
     int spins = 0;
-    while (*vg < target) {
-      if (++spins > kBarrierSpins) { atomicExch(&w->abort_flag, 1u); ok_s = 0; break; }
+    unsigned int g;
+    while (((g = ld_acquire(&w->bar_gen)) & ~kGenAbort) < target) {
+      if (++spins > kBarrierSpins) break;
       __nanosleep(32);
     }
-  }
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (*(volatile unsigned int*)&w->abort_flag != 0u) ok_s = 0;
+    if ((g & ~kGenAbort) < target || (g & kGenAbort)) {
+      ok_s = 0;
+      st_release(flags + blockIdx.x, kFlagAbort);
+    }
   }
   __syncthreads();
   return ok_s != 0;
@@ -110,6 +127,37 @@ __device__ __forceinline__ double grid_sum(const PcgPart* part, int f, double* r
   double v = 0.0;
   for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) v += __ldcg(&part[b].v[f]);
   const double t = block_sum(v, red);
+  if (threadIdx.x == 0) *bcast = t;
+  __syncthreads();
+  return *bcast;
+}
+
+// Sums of (u, v) over the block (valid on thread 0).
+__device__ __forceinline__ double2 block_sum2(double u, double v, double2* red2) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    u += __shfl_xor_sync(0xffffffffu, u, d);
+    v += __shfl_xor_sync(0xffffffffu, v, d);
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red2[w] = make_double2(u, v);
+  __syncthreads();
+  double2 t = make_double2(0.0, 0.0);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPcgThreads / 32; ++i) { t.x += red2[i].x; t.y += red2[i].y; }
+  return t;
+}
+
+// Sums over blocks of partial fields f and f + 1 in one pass, the same fixed order in every
+// block; broadcast to every thread of the block.
+__device__ __forceinline__ double2 grid_sum2(const PcgPart* part, int f, double2* red2, double2* bcast) {
+  double u = 0.0, v = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    u += __ldcg(&part[b].v[f]);
+    v += __ldcg(&part[b].v[f + 1]);
+  }
+  const double2 t = block_sum2(u, v, red2);
   if (threadIdx.x == 0) *bcast = t;
   __syncthreads();
   return *bcast;
@@ -184,8 +232,10 @@ __global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* 
                                                      const float* __restrict__ pan, int* result) {
   __shared__ double red[kPcgThreads / 32];
   __shared__ double bc;
+  __shared__ double2 red2[kPcgThreads / 32];
+  __shared__ double2 bc2;
   PcgWords* w = reinterpret_cast<PcgWords*>(work);
-  volatile unsigned int* flags = reinterpret_cast<volatile unsigned int*>(work + kPcgFlagsOff);
+  unsigned int* flags = reinterpret_cast<unsigned int*>(work + kPcgFlagsOff);
   PcgPart* part = reinterpret_cast<PcgPart*>(work + kPcgPartOff);
   T* vec = reinterpret_cast<T*>(work + kPcgVecOff);
   const int n = d.n_cam_params;
@@ -209,13 +259,12 @@ __global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* 
     s_rz += (double)bi * (double)zi;
     s_bb += (double)bi * (double)bi;
   }
-  double t = block_sum(s_bb, red);
-  if (threadIdx.x == 0) part[blockIdx.x].v[1] = t;
-  t = block_sum(s_rz, red);
-  if (threadIdx.x == 0) part[blockIdx.x].v[2] = t;
+  double2 t2 = block_sum2(s_bb, s_rz, red2);
+  if (threadIdx.x == 0) { part[blockIdx.x].v[1] = t2.x; part[blockIdx.x].v[2] = t2.y; }
   bool ok = grid_barrier(w, flags, ++target);
-  const double bnorm = fmax(sqrt(grid_sum(part, 1, red, &bc)), 1e-12);
-  double rz_old = grid_sum(part, 2, red, &bc);
+  t2 = grid_sum2(part, 1, red2, &bc2);
+  const double bnorm = fmax(sqrt(t2.x), 1e-12);
+  double rz_old = t2.y;
   double rn = 0.0, rz_new = 0.0;
 
   double best = __longlong_as_double(0x7ff0000000000000LL);   // +inf
@@ -258,7 +307,7 @@ __global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* 
         }
       }
     }
-    t = block_sum(s_pap, red);
+    const double t = block_sum(s_pap, red);
     if (threadIdx.x == 0) part[blockIdx.x].v[0] = t;
     if (!(ok = grid_barrier(w, flags, ++target))) break;
     // ---- phase B: x, r, z and the partial sums of r.r and r.z ----
@@ -275,13 +324,12 @@ __global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* 
       s_rr += (double)ri * (double)ri;
       s_rz += (double)ri * (double)zi;
     }
-    t = block_sum(s_rr, red);
-    if (threadIdx.x == 0) part[blockIdx.x].v[1] = t;
-    t = block_sum(s_rz, red);
-    if (threadIdx.x == 0) part[blockIdx.x].v[2] = t;
+    t2 = block_sum2(s_rr, s_rz, red2);
+    if (threadIdx.x == 0) { part[blockIdx.x].v[1] = t2.x; part[blockIdx.x].v[2] = t2.y; }
     if (!(ok = grid_barrier(w, flags, ++target))) break;
-    rn = sqrt(grid_sum(part, 1, red, &bc));
-    rz_new = grid_sum(part, 2, red, &bc);
+    t2 = grid_sum2(part, 1, red2, &bc2);
+    rn = sqrt(t2.x);
+    rz_new = t2.y;
   }
   // the converging iterate, else the best-so-far one (zeros if none improved)
   for (int i = tid; i < n; i += nth) xo[i] = ok ? (converged ? x[i] : bx[i]) : T(0);
