@@ -181,18 +181,15 @@ __global__ void __launch_bounds__(256) k_build_panels(DevPlan d, const float* __
 }
 
 // The lanes of a warp compute the part of y_p = sum_c panel_p[r][c] x[col_c] over panel
-// columns [c0, c1) of block row p (at most kMvCols = 256, so at most eight per lane), with
+// columns [c0, c1) of block row p (panel P of width W, column list cols) (at most kMvCols = 256, so at most eight per lane), with
 // x = z + beta * pold formed on the fly.  The panel rows are read coalesced (consecutive
 // lanes, consecutive columns) and so mostly are the x values (a block's columns are
 // consecutive scalars).  Every lane returns the partial y_p[r] (r < bp) in yo.
 template <typename T, int MAXB>
-__device__ __forceinline__ void panel_matvec(const DevPlan& d, const float* __restrict__ pan, int p, int bp, int c0,
-                                             int c1, const T* __restrict__ z, const T* __restrict__ pold, T beta,
-                                             int lane, T yo[MAXB]) {
+__device__ __forceinline__ void panel_matvec(const float* __restrict__ P, const int* __restrict__ cols, int W, int bp,
+                                             int c0, int c1, const T* __restrict__ z, const T* __restrict__ pold,
+                                             T beta, int lane, T yo[MAXB]) {
   constexpr int CPL = kMvCols / 32;                      // columns per lane
-  const int W = d.pan_w[p];
-  const float* P = pan + d.pan_off[p];
-  const int* cols = d.pan_col + d.col_off[p];
   T xc[CPL];
   bool has[CPL];
 #pragma unroll
@@ -291,12 +288,13 @@ __global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* 
     double s_pap = 0.0;
     for (int task = gw; task < d.n_mv_tasks; task += nwarps) {   // warp per matvec task
       const int4 tk = __ldg(d.mv_task + task);           // block row, panel columns [c0, c1), flags
-      const int p = tk.x, bp = d.bsize[p], op = d.boff[p];
+      const int4 rw = __ldg(d.mv_row + task);            // boff, W, panel offset / 4, column-list offset
+      const int bp = tk.w >> 8, op = rw.x;
       const bool single = tk.w & 1, first = tk.w & 2;
       // this lane's scalar of the row (lane < bp): its new search direction, loaded early
       const T pn = lane < bp ? __ldcg(z + op + lane) + tb * __ldcg(pold + op + lane) : T(0);
       T yo[MAXB];
-      panel_matvec<T, MAXB>(d, pan, p, bp, tk.y, tk.z, z, pold, tb, lane, yo);
+      panel_matvec<T, MAXB>(pan + 4 * (int64_t)rw.z, d.pan_col + rw.w, rw.y, bp, tk.y, tk.z, z, pold, tb, lane, yo);
 #pragma unroll
       for (int rr = 0; rr < MAXB; ++rr) {
         if (lane == rr && rr < bp) {

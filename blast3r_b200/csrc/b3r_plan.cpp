@@ -80,7 +80,7 @@ struct PlanBuild {
   std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
   std::vector<int4> t_idx, c1_idx;
   std::vector<int> sym_ptr, sym_ent;
-  std::vector<int4> mv_task, mv_ent;
+  std::vector<int4> mv_task, mv_row, mv_ent;
   std::vector<int64_t> pan_off;
   std::vector<int> pan_w, col_off, pan_col, ent_col, ent_row;
   int64_t pan_floats = 0;
@@ -486,8 +486,12 @@ static int build_pattern(PlanBuild& B) {
       coff += w;
       poff += ((int64_t)B.bsize[pr] * w + 3) & ~int64_t(3);   // 16-byte aligned panels
       const int single = w <= kMvCols ? 1 : 0;
-      for (int c0 = 0; c0 < w; c0 += kMvCols)
-        B.mv_task.push_back(make_int4(pr, c0, std::min(c0 + kMvCols, w), single | (c0 == 0 ? 2 : 0)));
+      B3R_REQUIRE((B.pan_off[pr] >> 2) <= INT32_MAX, "PCG row panels beyond 2^33 floats");
+      for (int c0 = 0; c0 < w; c0 += kMvCols) {
+        B.mv_task.push_back(make_int4(pr, c0, std::min(c0 + kMvCols, w),
+                                      single | (c0 == 0 ? 2 : 0) | (B.bsize[pr] << 8)));
+        B.mv_row.push_back(make_int4(B.boff[pr], w, (int)(B.pan_off[pr] >> 2), B.col_off[pr]));
+      }
     }
     B.pan_floats = poff;
   }
@@ -599,7 +603,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.blk_row, &d.blk_row); A.add(B.trk_ptr, &d.trk_ptr);
   A.add(B.t_idx, &d.t_idx); A.add(B.c1_idx, &d.c1_idx);
   A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
-  A.add(B.mv_task, &d.mv_task); A.add(B.mv_ent, &d.mv_ent);
+  A.add(B.mv_task, &d.mv_task); A.add(B.mv_row, &d.mv_row); A.add(B.mv_ent, &d.mv_ent);
   d.n_mv_tasks = (int)B.mv_task.size();
   A.add(B.pan_off, &d.pan_off); A.add(B.pan_w, &d.pan_w); A.add(B.col_off, &d.col_off);
   A.add(B.pan_col, &d.pan_col); A.add(B.ent_col, &d.ent_col); A.add(B.ent_row, &d.ent_row);

@@ -92,7 +92,10 @@ struct DevPlan {
   // e.g. the shared focal block of a mono-camera rig, spreads over many warps)
   int n_mv_tasks;
   const int4* mv_task;    // [n_mv_tasks] (block row, first panel column, end panel column,
-                          //  1 if the row is one task | 2 if this is the row's first task)
+                          //  1 if the row is one task | 2 if this is the row's first task |
+                          //  the row's block size << 8)
+  const int4* mv_row;     // [n_mv_tasks] the task's row fields, loaded beside mv_task so that no
+                          //  load waits on another: (boff, W_p, pan_off / 4, col_off)
   const int4* mv_ent;     // [2*nnzb - nb] (value offset, column scalar offset, column block size,
                           //  1 if the entry is the transpose of the stored block)
   // row panels of the symmetric S for the PCG matvec: block row p is a dense bp x W_p
