@@ -19,12 +19,17 @@ from .cujac import exp_se3, residuals_with_rigs as residual_func
 BA_Status = namedtuple('BA_Status', 'init_loss, init_residuals, new_loss, new_residuals')
 
 
-def shape_of(tensor, is_contiguous=True):
-    """Input checks of the reference (engine.py:340-344)."""
+def shape_of(tensor, is_contiguous=True, finite=None):
+    """Input checks of the reference (engine.py:340-344).  Given a list `finite`, the
+    all-finite flag goes into it as a device tensor, for the caller to check for every input
+    with one host synchronisation, instead of being checked here."""
     assert tensor.dtype in (torch.float32, torch.int32)
     if is_contiguous:
         assert tensor.is_contiguous()
-    assert tensor.isfinite().all()
+    if finite is None:
+        assert tensor.isfinite().all()
+    else:
+        finite.append(tensor.isfinite().all())
     return tensor.shape
 
 
@@ -71,16 +76,18 @@ def line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P, 
         update['z_coefs'] = (z_coefs - delta_zcf).contiguous()
         update['pts3d'] = (pts3d - delta_pts).contiguous()
         new_loss, new_residuals, _ = objective(**update)
-        if new_loss.isnan():
-            if verbose:
-                print('Warning: loss is NaN')
-            new_loss = init_loss
-        new_loss = new_loss + min_loss_delta
-        new_reproj = float(reproj_score(new_residuals))
+        # the reference's NaN fallback, loss margin and comparison, on the device, read back
+        # with the score in one synchronisation
+        isnan = new_loss.isnan()
+        new_loss = torch.where(isnan, init_loss, new_loss) + min_loss_delta
+        was_nan, lower, new_reproj = torch.stack([isnan.float(), (new_loss < init_loss).float(),
+                                                  reproj_score(new_residuals)]).tolist()
+        if was_nan and verbose:
+            print('Warning: loss is NaN')
         degenerate = new_reproj < min_reproj
         if degenerate and verbose:
             print(f'Rejecting step: reprojection residual collapsed to {new_reproj:.2e}')
-        if new_loss < init_loss and not degenerate:
+        if lower and not degenerate:
             break
         delta *= a / last_a          # scales (delta_K, ..., delta_pts): they are views of delta
         last_a = a
@@ -103,21 +110,23 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
         raise NotImplementedError('the dense tangent prior is not supported by the B200 solver')
     is_depth_log = depth_mode == 'log'
     n_imgs = rigs.shape[1]
-    assert shape_of(rigs) == (3, n_imgs)
+    fin = []                 # the inputs' all-finite flags, checked together below
+    assert shape_of(rigs, finite=fin) == (3, n_imgs)
     n_cams = len(K)
-    assert shape_of(K) == (n_cams, 3, 3)
-    assert shape_of(P_rig2cam, is_contiguous=False) == (n_cams, 4, 4)
+    assert shape_of(K, finite=fin) == (n_cams, 3, 3)
+    assert shape_of(P_rig2cam, is_contiguous=False, finite=fin) == (n_cams, 4, 4)
     n_nodes = len(P_w2rig)
-    assert shape_of(P_w2rig) == (n_nodes, 4, 4)
+    assert shape_of(P_w2rig, finite=fin) == (n_nodes, 4, 4)
     n_zcf = z_coefs.shape[1]
-    assert shape_of(z_coefs) == (n_imgs, n_zcf)
+    assert shape_of(z_coefs, finite=fin) == (n_imgs, n_zcf)
     n_tracks = len(pts3d)
-    assert shape_of(pts3d) == (n_tracks, 3)
+    assert shape_of(pts3d, finite=fin) == (n_tracks, 3)
     n_obs = len(pids)
-    assert shape_of(pids) == (n_obs,)
-    assert shape_of(pix2d) == (n_obs, 2)
-    assert shape_of(pix2d_std) == (n_obs, 2)
-    assert shape_of(pix2d_dep) == (n_obs, n_zcf)
+    assert shape_of(pids, finite=fin) == (n_obs,)
+    assert shape_of(pix2d, finite=fin) == (n_obs, 2)
+    assert shape_of(pix2d_std, finite=fin) == (n_obs, 2)
+    assert shape_of(pix2d_dep, finite=fin) == (n_obs, n_zcf)
+    assert bool(torch.stack(fin).all()), 'non-finite input'
     assert 0 <= weight_z <= 10
     assert n_obs >= n_tracks, 'there must be more 2d kpts than tracks'
     assert huber_delta >= 0.1
