@@ -34,6 +34,7 @@ constexpr int kBarrierSpins = 1 << 24;   // polls before a grid barrier gives up
 constexpr int kPcgMaxBlocks = 1024;
 constexpr size_t kPcgFlagsOff = 256, kPcgPartOff = kPcgFlagsOff + 4 * kPcgMaxBlocks;
 constexpr size_t kPcgVecOff = kPcgPartOff + 4 * 8 * kPcgMaxBlocks;
+static_assert(kPcgMaxBlocks % kPcgThreads == 0, "barrier flags per polling thread");
 
 inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the seven vectors
   return (kPcgVecOff + 7 * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
@@ -78,15 +79,26 @@ __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, u
   }
   __syncthreads();
   if (blockIdx.x == 0) {
+    // each thread polls its (up to kPcgMaxBlocks / kPcgThreads) flags with loads issued
+    // together, so a thread's second flag costs no extra round trip
+    constexpr int kPer = kPcgMaxBlocks / kPcgThreads;
     bool bad = false;
-    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
-      int spins = 0;
-      unsigned int f;
-      while ((f = ld_acquire(flags + b)) < target) {
-        if (++spins > kBarrierSpins) break;
-        __nanosleep(32);
+    for (int spins = 0;; ++spins) {
+      unsigned int f[kPer];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int b = threadIdx.x + j * kPcgThreads;
+        f[j] = b < (int)gridDim.x ? ld_acquire(flags + b) : target;
       }
-      if (f < target || f == kFlagAbort) bad = true;
+      bool all = true;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (f[j] == kFlagAbort) bad = true;
+        if (f[j] < target) all = false;
+      }
+      if (all) break;
+      if (spins >= kBarrierSpins) { bad = true; break; }
+      __nanosleep(32);
     }
     if (bad) ok_s = 0;
     __syncthreads();
