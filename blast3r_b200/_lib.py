@@ -25,7 +25,7 @@ class PlanDesc(C.Structure):
                 ('n_obs', _i64), ('C', _i32), ('infos', _pi32), ('pids', _pi32),
                 ('mode_K', _i32), ('mode_P', _i32), ('mode_Z', _i32), ('mode_X', _i32),
                 ('mask_K', _pu8), ('mask_P', _pu8), ('mask_Z', _pu8), ('mask_X', _pu8),
-                ('track_begin', _i32), ('track_end', _i32), ('device', _i32)]
+                ('track_begin', _i32), ('track_end', _i32), ('device', _i32), ('obs_local', _i32)]
 
 
 class PlanInfo(C.Structure):
@@ -34,7 +34,8 @@ class PlanInfo(C.Structure):
                 ('nnzb', _i64), ('nnz', _i64), ('n_pairs', _i64), ('n_segments', _i64),
                 ('n_pair_tasks', _i64), ('n_point_tasks', _i64), ('n_diag_chunks', _i64),
                 ('workspace_bytes', _i64), ('nb_K', _i32), ('nb_P', _i32), ('nb_Z', _i32),
-                ('off_P', _i32), ('off_Z', _i32), ('record_floats', _i32)]
+                ('off_P', _i32), ('off_Z', _i32), ('record_floats', _i32), ('n_obs_input', _i64),
+                ('depth_stitch', _i32)]
 
 
 class Params(C.Structure):
@@ -76,6 +77,7 @@ _SIGS = {
     'b3r_plan_get_info': (C.c_int, [_vp, C.POINTER(PlanInfo)]),
     'b3r_plan_get_pattern': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
     'b3r_plan_stage_obs': (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    'b3r_plan_get_input_obs': (C.c_int, [_vp, _vp]),
     'b3r_linearize_schur': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), _vp,
                                       C.POINTER(Outputs), _vp]),
     'b3r_linearize_schur_noalloc': (C.c_int, [_vp, C.POINTER(Params), C.POINTER(LinOpts), C.POINTER(Outputs), _vp]),

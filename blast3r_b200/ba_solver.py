@@ -40,32 +40,39 @@ class Linearization:
         self.shape = (3 * n, plan.n_cam_params + 3 * plan.info.n_points)
 
 
-_PLAN_CACHE = {}
+_PLAN_CACHE = []        # (key, structure tensors, plan), most recent last
+_PLAN_CACHE_MAX = 8
 
 
-def _fingerprint(t):
-    """Shape + two weighted sums of an integer/bool tensor (one small reduction)."""
-    v = t.reshape(-1).long()
-    w = torch.arange(1, v.numel() + 1, device=v.device, dtype=torch.int64) % 1000003
-    return (tuple(t.shape),) + tuple(torch.stack([v.sum(), (v * w).sum()]).tolist())
+def _structure(rigs, pids, modes):
+    """The tensors that define a plan's structure (device copies are kept for comparison)."""
+    return [rigs, pids] + [m for m in modes if isinstance(m, torch.Tensor)]
 
 
-def _structure_key(rigs, pids, n_cams, n_nodes, n_tracks, C, modes):
-    return (_fingerprint(rigs), _fingerprint(pids), n_cams, n_nodes, n_tracks, C,
-            tuple(m if isinstance(m, bool) else ('mask',) + _fingerprint(m) for m in modes))
+def _same(a, b):
+    return a.shape == b.shape and a.dtype == b.dtype and a.device == b.device and torch.equal(a, b)
 
 
 def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=True, optim_Z=True,
              optim_X=True, device=None):
-    """Plan for this structure, reused while the structure tensors are unchanged."""
-    key = _structure_key(rigs, pids, n_cams, n_nodes, n_tracks, C, (optim_K, optim_P, optim_Z, optim_X))
-    plan = _PLAN_CACHE.get(key)
-    if plan is None:
-        if len(_PLAN_CACHE) > 8:
-            _PLAN_CACHE.clear()
-        plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
-                      optim_Z=optim_Z, optim_X=optim_X, device=device)
-        _PLAN_CACHE[key] = plan
+    """Plan for this structure, reused while the structure tensors hold the same values.
+
+    A cached plan is returned only when ``rigs``, ``pids`` and every bool mask are equal,
+    element by element, to the copies taken when it was built (one device comparison per
+    call), so a reordering or an in-place edit of the structure always gets a new plan."""
+    modes = (optim_K, optim_P, optim_Z, optim_X)
+    key = (tuple(rigs.shape), tuple(pids.shape), n_cams, n_nodes, n_tracks, C,
+           tuple(m if isinstance(m, bool) else ('mask', tuple(m.shape)) for m in modes))
+    cur = _structure(rigs, pids, modes)
+    for j, (k, saved, plan) in enumerate(_PLAN_CACHE):
+        if k == key and len(saved) == len(cur) and all(_same(a, b) for a, b in zip(cur, saved)):
+            _PLAN_CACHE.append(_PLAN_CACHE.pop(j))
+            return plan
+    plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
+                  optim_Z=optim_Z, optim_X=optim_X, device=device)
+    if len(_PLAN_CACHE) >= _PLAN_CACHE_MAX:
+        _PLAN_CACHE.pop(0)
+    _PLAN_CACHE.append((key, [t.detach().clone() for t in cur], plan))
     return plan
 
 
@@ -114,6 +121,10 @@ class GaussNewtonSolver:
         opts = BAPlan.lin_opts(is_depth_log=f['is_depth_log'], clamp_w=clamp_w, dampen=self.dampen,
                                adaptive_dampen=self.adaptive_dampen, no_grad_f_from_rz=self.no_grad_f_from_rz,
                                optim_Z0=f['optim_Z0'], optim_Z_1st_cam=f['optim_Z_1st_cam'], **kw)
+        # the plan's track-sorted copy of the observation arrays is refreshed for every
+        # linearization: the caller may have edited them in place, or new arrays may sit at
+        # the addresses of old ones
+        J.plan.stage_obs(t['pix2d'], t['pix2d_std'], t['pix2d_dep'])
         if t['pix2d'] is not None:
             p = J.plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
                               t['pix2d_dep'], pix2d=t['pix2d'])

@@ -12,9 +12,11 @@
 //     rank's observation-pair lists bucketed by segment, cut into pair tasks;
 //   * the block-sparse pattern of S (upper block triangle) and every destination offset.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <new>
+#include <thread>
 #include "b3r_plan.h"
 #include "b3r_status.h"
 
@@ -51,6 +53,27 @@ int make_type(int mode, const uint8_t* mask, int n, const char* name, TypeMap& t
 }
 
 inline int round4(int x) { return (x + 3) & ~3; }
+
+// Host threads of the planner: $B3R_PLAN_THREADS, else the hardware's, at most 32.
+int plan_threads() {
+  if (const char* e = std::getenv("B3R_PLAN_THREADS")) {
+    const int v = std::atoi(e);
+    if (v >= 1) return std::min(v, 256);
+  }
+  const unsigned h = std::thread::hardware_concurrency();
+  return (int)std::max(1u, std::min(h ? h : 1u, 32u));
+}
+
+// fn(t, begin, end) over nt contiguous ranges of [0, n), one thread each (the first on the
+// calling thread).
+template <typename F>
+void parallel_ranges(int64_t n, int nt, F&& fn) {
+  nt = (int)std::max<int64_t>(1, std::min<int64_t>(nt, n));
+  std::vector<std::thread> th;
+  for (int t = 1; t < nt; ++t) th.emplace_back([&, t] { fn(t, n * t / nt, n * (t + 1) / nt); });
+  fn(0, 0, n / nt);
+  for (auto& x : th) x.join();
+}
 
 }  // namespace
 
@@ -97,6 +120,7 @@ static int build_maps(PlanBuild& B) {
   B3R_REQUIRE(d.infos != nullptr && (d.n_obs == 0 || d.pids != nullptr), "NULL infos/pids");
   B3R_REQUIRE(d.track_begin >= 0 && d.track_begin <= d.track_end && d.track_end <= d.n_tracks,
               "bad track range [%d, %d)", d.track_begin, d.track_end);
+  B3R_REQUIRE(d.obs_local == 0 || d.obs_local == 1, "obs_local must be 0 or 1");
   const int32_t* cum = d.infos;
   const int32_t* node = d.infos + I;
   const int32_t* cam = d.infos + 2 * I;
@@ -173,9 +197,14 @@ static int build_tracks(PlanBuild& B) {
   // local tracks: eliminated, owned, non-empty; ordered by (first image, id)
   for (int t = d.track_begin; t < d.track_end; ++t)
     if (B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) B.loc_tracks.push_back(t);
-  std::stable_sort(B.loc_tracks.begin(), B.loc_tracks.end(), [&](int a, int b) {
-    return B.img_of[B.all_obs[B.all_ptr[a]]] < B.img_of[B.all_obs[B.all_ptr[b]]];
-  });
+  {
+    // stable counting sort by first image (tracks arrive in id order)
+    std::vector<int> cnt(d.n_imgs + 1, 0), sorted(B.loc_tracks.size());
+    for (int t : B.loc_tracks) cnt[B.img_of[B.all_obs[B.all_ptr[t]]] + 1]++;
+    for (int i = 0; i < d.n_imgs; ++i) cnt[i + 1] += cnt[i];
+    for (int t : B.loc_tracks) sorted[cnt[B.img_of[B.all_obs[B.all_ptr[t]]]]++] = t;
+    B.loc_tracks.swap(sorted);
+  }
   const int nT = (int)B.loc_tracks.size();
   B.trk_col.resize(nT);
   for (int tl = 0; tl < nT; ++tl) B.trk_col[tl] = B.X.col[B.loc_tracks[tl]];
@@ -255,26 +284,40 @@ namespace b3r {
 static int build_segments(PlanBuild& B) {
   const b3r_plan_desc& d = *B.d;
   const int I = d.n_imgs;
-  B.seg_row_ptr.assign(I + 1, 0);
-  std::vector<int> stamp(I, -1), partners;
   const int32_t* cum = d.infos;
-  for (int i = 0; i < I; ++i) {
-    partners.clear();
-    const int64_t o0 = i ? cum[i - 1] : 0, o1 = cum[i];
-    for (int64_t o = o0; o < o1; ++o) {
-      const int t = d.pids[o];
-      if (!B.elim[t] || !B.obs_live[o]) continue;
-      for (int j = B.all_ptr[t]; j < B.all_ptr[t + 1]; ++j) {
-        const int o2 = B.all_obs[j];
-        if (o2 <= o || !B.obs_live[o2]) continue;   // o2 > o  =>  img(o2) >= i
-        const int i2 = B.img_of[o2];
-        if (stamp[i2] != i) { stamp[i2] = i; partners.push_back(i2); }
+  // each thread takes a contiguous range of row images; per image its partners, sorted
+  const int nt = plan_threads();
+  std::vector<std::vector<int>> part_col(nt), part_cnt(nt);
+  parallel_ranges(I, nt, [&](int t, int64_t i0, int64_t i1) {
+    std::vector<int> stamp(I, -1), partners;
+    std::vector<int>& col = part_col[t];
+    std::vector<int>& cnt = part_cnt[t];
+    for (int i = (int)i0; i < (int)i1; ++i) {
+      partners.clear();
+      const int64_t o0 = i ? cum[i - 1] : 0, o1 = cum[i];
+      for (int64_t o = o0; o < o1; ++o) {
+        const int tk = d.pids[o];
+        if (!B.elim[tk] || !B.obs_live[o]) continue;
+        for (int j = B.all_ptr[tk]; j < B.all_ptr[tk + 1]; ++j) {
+          const int o2 = B.all_obs[j];
+          if (o2 <= o || !B.obs_live[o2]) continue;   // o2 > o  =>  img(o2) >= i
+          const int i2 = B.img_of[o2];
+          if (stamp[i2] != i) { stamp[i2] = i; partners.push_back(i2); }
+        }
       }
+      std::sort(partners.begin(), partners.end());
+      col.insert(col.end(), partners.begin(), partners.end());
+      cnt.push_back((int)partners.size());
     }
-    std::sort(partners.begin(), partners.end());
-    B.seg_col.insert(B.seg_col.end(), partners.begin(), partners.end());
-    B.seg_row_ptr[i + 1] = (int)B.seg_col.size();
+  });
+  B.seg_row_ptr.assign(I + 1, 0);
+  B.seg_col.clear();
+  int i = 0;
+  for (int t = 0; t < nt; ++t) {
+    B.seg_col.insert(B.seg_col.end(), part_col[t].begin(), part_col[t].end());
+    for (int c : part_cnt[t]) { B.seg_row_ptr[i + 1] = B.seg_row_ptr[i] + c; ++i; }
   }
+  B3R_REQUIRE(i == I, "internal: segment rows %d of %d", i, I);
   return B3R_OK;
 }
 
@@ -289,12 +332,14 @@ static inline int64_t seg_lookup(const PlanBuild& B, int i, int i2) {
 // the pair tasks.
 static int build_pairs(PlanBuild& B) {
   const int64_t S = (int64_t)B.seg_col.size();
-  B.seg_cnt.assign(S + 1, 0);
-  auto for_pairs = [&](auto&& fn) {
-    int64_t k0 = 0;
-    for (size_t tl = 0; tl < B.loc_tracks.size(); ++tl) {
-      const int t = B.loc_tracks[tl];
-      const int L = B.all_ptr[t + 1] - B.all_ptr[t];
+  const int64_t nT = (int64_t)B.loc_tracks.size();
+  // Pairs (a < b) of every local track in local order, visited by track ranges: a two-pass
+  // counting sort (count per thread and segment, then fill at per-thread offsets) keeps the
+  // pairs of a segment in local track order, the same as one sequential pass.
+  auto for_pairs = [&](int64_t tl0, int64_t tl1, auto&& fn) {
+    for (int64_t tl = tl0; tl < tl1; ++tl) {
+      const int64_t k0 = B.trk_ptr[tl];
+      const int L = B.trk_ptr[tl + 1] - B.trk_ptr[tl];
       for (int a = 0; a < L; ++a) {
         const int ka = (int)(k0 + a);
         const int oa = B.perm_t[ka];
@@ -306,13 +351,35 @@ static int build_pairs(PlanBuild& B) {
           fn(seg_lookup(B, B.img_of[oa], B.img_of[ob]), ka, kb);
         }
       }
-      k0 += L;
     }
   };
-  int bad = 0;
-  for_pairs([&](int64_t s, int, int) { if (s < 0) ++bad; else B.seg_cnt[s + 1]++; });
-  B3R_REQUIRE(bad == 0, "internal: %d pairs without a segment", bad);
-  for (int64_t s = 0; s < S; ++s) B.seg_cnt[s + 1] += B.seg_cnt[s];
+  const int nt = (int)std::max<int64_t>(1, std::min<int64_t>(plan_threads(), nT));
+  std::vector<int64_t> cnt;
+  try {
+    cnt.assign((size_t)nt * (size_t)S, 0);
+  } catch (const std::bad_alloc&) {
+    return fail(B3R_E_NOMEM, "cannot allocate the planner's per-thread segment counts");
+  }
+  std::vector<int64_t> bad(nt, 0);
+  parallel_ranges(nT, nt, [&](int t, int64_t a, int64_t b) {
+    int64_t* c = cnt.data() + (size_t)t * S;
+    for_pairs(a, b, [&](int64_t sg, int, int) { if (sg < 0) ++bad[t]; else c[sg]++; });
+  });
+  for (int t = 0; t < nt; ++t) B3R_REQUIRE(bad[t] == 0, "internal: %lld pairs without a segment", (long long)bad[t]);
+  B.seg_cnt.assign(S + 1, 0);
+  for (int64_t sg = 0; sg < S; ++sg) {
+    int64_t run = 0;
+    for (int t = 0; t < nt; ++t) run += cnt[(size_t)t * S + sg];
+    B.seg_cnt[sg + 1] = B.seg_cnt[sg] + run;
+  }
+  for (int64_t sg = 0; sg < S; ++sg) {       // per-thread fill offsets
+    int64_t run = B.seg_cnt[sg];
+    for (int t = 0; t < nt; ++t) {
+      const int64_t c = cnt[(size_t)t * S + sg];
+      cnt[(size_t)t * S + sg] = run;
+      run += c;
+    }
+  }
   const int64_t P = B.seg_cnt[S];
   try {
     B.pairs.resize(P);
@@ -323,12 +390,17 @@ static int build_pairs(PlanBuild& B) {
   std::vector<int> e_of_k(B.perm_t.size(), -1);
   for (size_t e = 0; e < B.c1_k.size(); ++e)
     if (B.c1_k[e] >= 0) e_of_k[B.c1_k[e]] = (int)e;
-  {
-    std::vector<int64_t> fill(B.seg_cnt.begin(), B.seg_cnt.end() - 1);
-    for_pairs([&](int64_t s, int ka, int kb) { B.pairs[fill[s]++] = make_int2(e_of_k[ka], e_of_k[kb]); });
-  }
-  for (const int2& pr : B.pairs)
-    B3R_REQUIRE(pr.x >= 0 && pr.y >= 0, "internal: pair observation without an image-major slot");
+  std::vector<int64_t> missing(nt, 0);
+  parallel_ranges(nT, nt, [&](int t, int64_t a, int64_t b) {
+    int64_t* fill = cnt.data() + (size_t)t * S;
+    for_pairs(a, b, [&](int64_t sg, int ka, int kb) {
+      const int2 pr = make_int2(e_of_k[ka], e_of_k[kb]);
+      if (pr.x < 0 || pr.y < 0) ++missing[t];
+      B.pairs[fill[sg]++] = pr;
+    });
+  });
+  for (int t = 0; t < nt; ++t)
+    B3R_REQUIRE(missing[t] == 0, "internal: pair observation without an image-major slot");
   // Tasks: segments cut into <= kPairTask pairs, in segment order (row image major) so that
   // the records of a row image and of its window of partner images stay in L2 while its
   // tasks run; within one row image the longest tasks go first so the short ones fill in
@@ -570,7 +642,15 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   std::memset(&d, 0, sizeof(d));
   d.n_imgs = desc->n_imgs; d.n_cams = desc->n_cams; d.n_nodes = desc->n_nodes;
   d.n_tracks = desc->n_tracks; d.C = desc->C; d.n_obs = desc->n_obs;
-  d.R = round4(27 + desc->C);
+  {
+    bool any_kp = false, any_z = false;
+    for (int i = 0; i < desc->n_imgs; ++i) {
+      any_kp = any_kp || B.img_bk[3 * i] >= 0 || B.img_bk[3 * i + 1] >= 0;
+      any_z = any_z || B.img_bk[3 * i + 2] >= 0;
+    }
+    d.zonly = (!any_kp && any_z && desc->C <= 8) ? 1 : 0;
+  }
+  d.R = d.zonly ? round4(3 + desc->C) : round4(27 + desc->C);
   d.nbK = B.K.n_cols; d.nbP = B.P.n_cols; d.nbZ = B.Z.n_cols; d.nb = B.nb;
   d.off_P = 2 * d.nbK; d.off_Z = d.off_P + 6 * d.nbP;
   d.n_cam_params = d.off_Z + desc->C * d.nbZ;
@@ -586,10 +666,34 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   d.nnzb = (int64_t)B.col_idx.size();
   d.nnz = B.nnz;
 
+  // Input rows: the global observation index, or with obs_local the rank of the observation
+  // among this rank's own (image-sorted) observations.  The kernels index the caller's
+  // per-observation arrays by it; the planner's own structures keep global indices.
+  std::vector<int> perm_dev;
+  d.first_in = desc->n_obs > 0 ? 0 : -1;
+  d.n_in = desc->n_obs;
+  if (desc->obs_local) {
+    std::vector<int> own(desc->n_obs, -1);
+    for (int64_t o = 0; o < desc->n_obs; ++o) {
+      const int t = desc->pids[o];
+      if (t >= desc->track_begin && t < desc->track_end) {
+        own[o] = (int)P->in_obs.size();
+        P->in_obs.push_back((int)o);
+      }
+    }
+    perm_dev.resize(B.perm_t.size());
+    for (size_t k = 0; k < B.perm_t.size(); ++k) {
+      perm_dev[k] = own[B.perm_t[k]];
+      B.t_idx[k].w = own[B.t_idx[k].w];
+    }
+    for (auto& x : B.c1_idx) x.x = own[x.x];
+    d.first_in = desc->n_obs > 0 ? own[0] : -1;
+    d.n_in = (int64_t)P->in_obs.size();
+  }
   Arena A;
   A.add(B.img_bk, &d.img_bk); A.add(B.img_sc, &d.img_sc); A.add(B.img_dst, &d.img_dst);
   A.add(B.img_node, &d.img_node); A.add(B.img_cam, &d.img_cam);
-  A.add(B.perm_t, &d.perm_t); A.add(B.trk_t, &d.trk_t); A.add(B.img_t, &d.img_t);
+  A.add(desc->obs_local ? perm_dev : B.perm_t, &d.perm_t); A.add(B.trk_t, &d.trk_t); A.add(B.img_t, &d.img_t);
   A.add(B.loc_tracks, &d.trk_gid); A.add(B.trk_col, &d.trk_col); A.add(B.pt_task, &d.pt_task);
   A.add_mut<float2>(d.n_loc, &d.t_pix); A.add_mut<float2>(d.n_loc, &d.t_std);
   A.add_mut<float>((size_t)d.n_loc * desc->C, &d.t_dep);
@@ -635,6 +739,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   I.workspace_bytes = (int64_t)ws_total;
   I.nb_K = d.nbK; I.nb_P = d.nbP; I.nb_Z = d.nbZ; I.off_P = d.off_P; I.off_Z = d.off_Z;
   I.record_floats = d.R;
+  I.n_obs_input = d.n_in;
+  I.depth_stitch = d.zonly;
   *out = P;
   return B3R_OK;
 }
@@ -656,6 +762,16 @@ extern "C" int b3r_plan_destroy(b3r_plan* plan) {
 extern "C" int b3r_plan_get_info(const b3r_plan* plan, b3r_plan_info* info) {
   B3R_REQUIRE(plan && info, "NULL argument");
   *info = plan->info;
+  return B3R_OK;
+}
+
+extern "C" int b3r_plan_get_input_obs(const b3r_plan* plan, int32_t* obs) {
+  B3R_REQUIRE(plan && obs, "NULL argument");
+  if (plan->in_obs.empty()) {
+    for (int64_t o = 0; o < plan->d.n_in; ++o) obs[o] = (int32_t)o;
+  } else {
+    std::copy(plan->in_obs.begin(), plan->in_obs.end(), obs);
+  }
   return B3R_OK;
 }
 

@@ -32,6 +32,10 @@ struct DevPlan {
   int64_t n_obs;
   int nbK, nbP, nbZ, nb, n_cam_params, off_P, off_Z;
   int zeroK, zeroP, zeroZ, zeroX;
+  int64_t first_in;       // input row of global observation 0 (-1: not in this plan's input)
+  int64_t n_in;           // rows of the per-observation input arrays
+  int zonly;              // only zcf blocks are active (focal and pose types off, C <= 8): the
+                          // depth-stitch passes with 3 + C float records run instead
 
   const int* img_bk;      // [n_imgs*3] active block of (foc, tau, zcf) per image, -1 if none
   const int* img_sc;      // [n_imgs*3] scalar offset of those blocks, -1 if none
@@ -42,7 +46,7 @@ struct DevPlan {
   // track-major side (eliminated tracks of this rank)
   int64_t n_loc;
   int nT_loc;
-  const int* perm_t;      // [n_loc] o of local observation k
+  const int* perm_t;      // [n_loc] input row of local observation k
   const int* trk_t;       // [n_loc] tl of local observation k
   const int* img_t;       // [n_loc] image of local observation k
   const int* trk_gid;     // [nT_loc] global track id
@@ -81,8 +85,8 @@ struct DevPlan {
   const int* sdiag_pos;   // [n_cam_params] position of each diagonal scalar in S_vals
   const int* blk_row;     // [nnzb] block row of each stored block
   const int* trk_ptr;     // [nT_loc+1] first k of each local track
-  const int4* t_idx;      // [n_loc] (image, global track id, tl, o) of local observation k
-  const int4* c1_idx;     // [n_c1] (o, k or -1, track id, tl or -1) of image-major entry e
+  const int4* t_idx;      // [n_loc] (image, global track id, tl, input row) of local observation k
+  const int4* c1_idx;     // [n_c1] (input row, k or -1, track id, tl or -1) of image-major entry e
   // the full (symmetric) block rows of S for an atomic-free matvec: entries of block row p
   // are sym_ent[sym_ptr[p] .. sym_ptr[p+1]), each 2 * stored block + 1 if it is the
   // transpose of a stored block (q, p) with q < p
@@ -128,6 +132,7 @@ struct b3r_plan {
   // per image-major slot e) | staged r/w | misc scalars
   size_t ws_img = 0, ws_trec = 0, ws_rec = 0, ws_rw = 0, ws_misc = 0;
   int64_t n_pairs_total = 0;
+  std::vector<int> in_obs;   // global observation of each input row (empty: the identity)
   bool staged = false;
   const void* staged_src[3] = {nullptr, nullptr, nullptr};
 };

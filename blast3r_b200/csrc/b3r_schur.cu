@@ -154,7 +154,8 @@ __device__ __forceinline__ void make_view(const Ctx& c, const ObsLin& L, float r
   }
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) V.dep[ch] = dep_raw[ch];
-  if (!c.optim_Z0 || (o == 0 && !c.optim_Z_1st_cam)) V.dep[0] = 0.f;
+  // the reference zeroes channel 0 of observation 0's depth Jacobian (ba_solver.py:38)
+  if (!c.optim_Z0 || (o == c.d.first_in && !c.optim_Z_1st_cam)) V.dep[0] = 0.f;
 }
 
 // Load + linearize local (track-sorted) observation k.
@@ -948,6 +949,192 @@ __global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* _
 }
 
 // ------------------------------------------------------------------------------------
+// depth-stitch plans: only the depth-coefficient (zcf) blocks take part in S
+// ------------------------------------------------------------------------------------
+// With the focal and pose types switched off (the reference's second BA phase, optim_K =
+// optim_P = False, whose blocks become decoupled ZerosMat diagonals, ba_solver.py:508-517),
+// the camera side of an observation is its image's zcf block, whose Jacobian is zs * dep in
+// the depth row only (sfm_jacobian_rigs.cu:494-501).  So Hpc = h dep^T with the 3-vector
+// h = zw * Jpw[2][:] (zw = sqrt(W_z) zs), the elimination record is y = L^-1 h plus the
+// observation's depth channels, and every Schur term is a scalar times an outer product of
+// depth vectors:
+//   image block      (zw^2 - y.y) dep dep^T
+//   gradient         (zw sqrt(W_z) r_z - y.z) dep          (z = L^-1 g_p)
+//   diag(A)          zw^2 dep_c^2
+//   pair product     (y_o . y_o') dep_o dep_o'^T
+// These are the general passes' values with the focal and pose columns left out (the same
+// per-observation arithmetic, in the same order).  Record: [0, 3) y, [3, 3+C) the depth
+// channels, padded to a multiple of four floats (32 bytes for C = 5).
+constexpr int kZonlyMaxC = 8;        // C*C accumulators per lane in the pair pass
+template <int CT> __host__ __device__ constexpr int zrec_floats() { return (3 + CT + 3) & ~3; }
+
+// Sum of v[0 .. 32 NG) over the warp, scattered: afterwards lane l holds in v[g] the total
+// of value 32 g + l (a recursive-halving butterfly: 31 shuffles per group of 32 values).
+template <int NG>
+__device__ __forceinline__ void warp_reduce_scatter(float (&v)[32 * NG], int lane) {
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float* w = v + 32 * g;
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) {
+      const bool up = lane & d;
+#pragma unroll
+      for (int i = 0; i < d; ++i) {
+        const float send = up ? w[i] : w[i + d];
+        const float keep = up ? w[i + d] : w[i];
+        w[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+      }
+    }
+    v[g] = w[0];
+  }
+}
+
+constexpr int kDiagZThreads = 128;
+
+// Image-major pass of a depth-stitch plan: one CTA per <= 1024-observation chunk of one
+// image, thread per observation (the next batch's inputs loaded ahead); the image's zcf
+// block, gradient and diag(A) summed per thread, then over the CTA, one atomic per value.
+template <int CT>
+__global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restrict__ S, float* __restrict__ b,
+                                                         float* __restrict__ diagA) {
+  constexpr int NZZ = CT * (CT + 1) / 2, NV = NZZ + 2 * CT, R = zrec_floats<CT>();
+  constexpr int NW = kDiagZThreads / 32;
+  __shared__ float red[NW][NV];
+  const int chunk = blockIdx.x;
+  const int img = c.d.c1_img[chunk];
+  const int eb = c.d.c1_chunk[chunk], ee = c.d.c1_chunk[chunk + 1];
+  const Cam cam = load_cam(c.img_rec + (int64_t)img * kImgRec);
+  float zc[CT];
+#pragma unroll
+  for (int ch = 0; ch < CT; ++ch) zc[ch] = __ldg(c.z_coefs + (int64_t)img * CT + ch);
+  float acc[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+  ObsIn<CT> nxt;
+  load_obs_in<CT>(c, eb + threadIdx.x, ee, nxt);
+  for (int base = eb; base < ee; base += kDiagZThreads) {
+    const int e = base + threadIdx.x;
+    const ObsIn<CT> cur = nxt;
+    if (base + kDiagZThreads < ee) load_obs_in<CT>(c, e + kDiagZThreads, ee, nxt);   // CTA-uniform
+    if (e >= ee) continue;
+    ObsView<CT> V;
+    view_in<CT>(c, cur, img, cam, zc, V);
+    const float zw = V.Jcw[26];
+    const float d = zw * zw;
+    float a = d, g = zw * V.sWr[2];
+    if (cur.ix.y >= 0) {                          // eliminated track: record y, subtract y.y, y.z
+      const float h0 = V.Jpw[6] * zw, h1 = V.Jpw[7] * zw, h2 = V.Jpw[8] * zw;
+      const float y0 = h0 * cur.tf0.x;
+      const float y1 = (h1 - cur.tf0.y * y0) * cur.tf0.w;
+      const float y2 = (h2 - cur.tf0.z * y0 - cur.tf1.x * y1) * cur.tf1.y;
+      a = fmaf(-y2, y2, fmaf(-y1, y1, fmaf(-y0, y0, a)));
+      g = fmaf(-y2, cur.tf2, fmaf(-y1, cur.tf1.w, fmaf(-y0, cur.tf1.z, g)));
+      float rv[R];
+      rv[0] = y0; rv[1] = y1; rv[2] = y2;
+#pragma unroll
+      for (int ch = 0; ch < CT; ++ch) rv[3 + ch] = V.dep[ch];
+#pragma unroll
+      for (int q = 3 + CT; q < R; ++q) rv[q] = 0.f;
+      float4* dst = reinterpret_cast<float4*>(c.rec + (int64_t)e * R);
+#pragma unroll
+      for (int q = 0; q < R / 4; ++q) dst[q] = make_float4(rv[4 * q], rv[4 * q + 1], rv[4 * q + 2], rv[4 * q + 3]);
+    }
+#pragma unroll
+    for (int i = 0; i < CT; ++i) {
+      const float ai = a * V.dep[i];
+#pragma unroll
+      for (int j = i; j < CT; ++j) acc[sym_idx(i, j, CT)] += ai * V.dep[j];
+      acc[NZZ + i] += g * V.dep[i];
+      acc[NZZ + CT + i] += d * V.dep[i] * V.dep[i];
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const float t = warp_sum(acc[v]);
+    if (lane == 0) red[warp][v] = t;
+  }
+  __syncthreads();
+  const int dzz = c.d.img_dst[6 * img + 5], sz = c.d.img_sc[3 * img + 2];
+  for (int e = threadIdx.x; e < CT * CT + 2 * CT; e += kDiagZThreads) {
+    int v;
+    float* addr;
+    if (e < CT * CT) {                            // the image's (z,z) block, stored in full
+      const int r = e / CT, q = e % CT;
+      v = sym_idx(min(r, q), max(r, q), CT);
+      addr = dzz >= 0 ? S + dzz + e : nullptr;
+    } else if (e < CT * CT + CT) {
+      v = NZZ + (e - CT * CT);
+      addr = sz >= 0 ? b + sz + (e - CT * CT) : nullptr;
+    } else {
+      v = NZZ + CT + (e - CT * CT - CT);
+      addr = sz >= 0 ? diagA + sz + (e - CT * CT - CT) : nullptr;
+    }
+    if (addr) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) t += red[w][v];
+      atomicAdd(addr, t);
+    }
+  }
+}
+
+constexpr int kPairZThreads = 128;   // four pair tasks per CTA, one warp each
+
+// Pair pass of a depth-stitch plan: warp per pair task, lane per observation pair, the
+// C x C block of the segment's (z,z) sub-block summed per lane, reduce-scattered over the
+// warp, one atomic per value per task.
+template <int CT>
+__global__ void __launch_bounds__(kPairZThreads) k_pairs_z(Ctx c, float* __restrict__ S) {
+  constexpr int R = zrec_floats<CT>(), Q = R / 4, NG = (CT * CT + 31) / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t task = (int64_t)blockIdx.x * (kPairZThreads / 32) + (threadIdx.x >> 5);
+  if (task >= c.d.n_tasks) return;                  // warp-uniform; no CTA barrier below
+  const int s = c.d.task_seg[task];
+  const int mode = (c.d.seg_mode[s] >> 16) & 3;     // sub-block (z,z) = 3 * 2 + 2
+  if (mode == kModeNone) return;
+  const int64_t pb = c.d.task_pb[task], pe = c.d.task_pe[task];
+  const int2* __restrict__ pairs = c.d.pairs;
+  const float4* __restrict__ rec4 = reinterpret_cast<const float4*>(c.rec);
+  float acc[32 * NG];
+#pragma unroll
+  for (int v = 0; v < 32 * NG; ++v) acc[v] = 0.f;
+  for (int64_t p = pb + lane; p < pe; p += 32) {
+    const int2 kk = __ldg(pairs + p);
+    float rv[R], cv[R];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const float4 u = __ldg(rec4 + (int64_t)kk.x * Q + q), w = __ldg(rec4 + (int64_t)kk.y * Q + q);
+      rv[4 * q] = u.x; rv[4 * q + 1] = u.y; rv[4 * q + 2] = u.z; rv[4 * q + 3] = u.w;
+      cv[4 * q] = w.x; cv[4 * q + 1] = w.y; cv[4 * q + 2] = w.z; cv[4 * q + 3] = w.w;
+    }
+    const float sy = fmaf(rv[2], cv[2], fmaf(rv[1], cv[1], rv[0] * cv[0]));
+#pragma unroll
+    for (int i = 0; i < CT; ++i) {
+      const float t = sy * rv[3 + i];
+#pragma unroll
+      for (int j = 0; j < CT; ++j) acc[CT * i + j] = fmaf(t, cv[3 + j], acc[CT * i + j]);
+    }
+  }
+  warp_reduce_scatter<NG>(acc, lane);
+  float* base = S + c.d.seg_dst[9 * (int64_t)s + 8];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int v = 32 * g + lane;
+    if (v >= CT * CT) continue;
+    const int i = v / CT, j = v % CT;
+    if (mode == kModeDirect) {
+      atomicAdd(base + i * CT + j, -acc[g]);
+    } else if (mode == kModeTrans) {
+      atomicAdd(base + j * CT + i, -acc[g]);
+    } else {
+      atomicAdd(base + i * CT + j, -acc[g]);
+      atomicAdd(base + j * CT + i, -acc[g]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // finalize: per-type adaptive damping and the Jacobi preconditioner
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ int scalar_type(const DevPlan& d, int j) { return j < d.off_P ? 0 : (j < d.off_Z ? 1 : 2); }
@@ -1215,6 +1402,27 @@ int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
   return check_launch("pairs pass");
 }
 
+template <int CT>
+int diag_z_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
+  if constexpr (CT <= kZonlyMaxC) {
+    k_diag_z<CT><<<c.d.n_c1_chunks, kDiagZThreads, 0, s>>>(c, S, b, diagA);
+    return check_launch("diag pass (depth-stitch)");
+  } else {
+    return fail(B3R_E_INVALID, "internal: depth-stitch kernels for C=%d", CT);
+  }
+}
+
+template <int CT>
+int pairs_z_launch(const Ctx& c, float* S, cudaStream_t s) {
+  if constexpr (CT <= kZonlyMaxC) {
+    const int64_t per = kPairZThreads / 32;
+    k_pairs_z<CT><<<(unsigned)((c.d.n_tasks + per - 1) / per), kPairZThreads, 0, s>>>(c, S);
+    return check_launch("pairs pass (depth-stitch)");
+  } else {
+    return fail(B3R_E_INVALID, "internal: depth-stitch kernels for C=%d", CT);
+  }
+}
+
 int launch_factor(const Ctx& c, cudaStream_t s) {
   k_factor<<<grid_for(std::max(c.d.nT_loc, 1), 256), 256, 0, s>>>(c);   // also records the damping
   return check_launch("factor pass");
@@ -1229,10 +1437,10 @@ int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaSt
       return launch_factor(c, s);
     case B3R_PASS_DIAG:
       if (c.d.n_c1_chunks == 0) return B3R_OK;
-      return diag_launch<CT>(c, S, b, diagA, s);
+      return c.d.zonly ? diag_z_launch<CT>(c, S, b, diagA, s) : diag_launch<CT>(c, S, b, diagA, s);
     case B3R_PASS_PAIRS:
       if (c.d.n_tasks == 0) return B3R_OK;
-      return pairs_launch<CT>(c, S, s);
+      return c.d.zonly ? pairs_z_launch<CT>(c, S, s) : pairs_launch<CT>(c, S, s);
   }
   return fail(B3R_E_INVALID, "bad pass %d", pass);
 }
@@ -1240,6 +1448,11 @@ int launch_pass(const Ctx& c, int pass, float* S, float* b, float* diagA, cudaSt
 template <int CT>
 int launch_assemble(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
   B3R_TRY(launch_factor(c, s));
+  if (c.d.zonly) {
+    if (c.d.n_c1_chunks > 0) B3R_TRY(diag_z_launch<CT>(c, S, b, diagA, s));
+    if (c.d.n_tasks > 0) B3R_TRY(pairs_z_launch<CT>(c, S, s));
+    return B3R_OK;
+  }
   if (c.d.n_c1_chunks > 0) B3R_TRY(diag_launch<CT>(c, S, b, diagA, s));
   if (c.d.n_tasks > 0) B3R_TRY(pairs_launch<CT>(c, S, s));
   return B3R_OK;

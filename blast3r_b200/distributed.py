@@ -87,6 +87,7 @@ def sharded_lm_step(sharded, rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2c
     lo = BAPlan.lin_opts(is_depth_log=is_log, weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err,
                          huber_delta=huber_delta, dampen=dampen)
     p = plan.params(K, P_rig2cam, P_w2rig, z_coefs, pts3d, pix2d_std, pix2d_dep, pix2d=pix2d)
+    plan.stage_obs(pix2d, pix2d_std, pix2d_dep)          # the observation arrays may have changed
     sharded.linearize(p, lo)
     dt = torch.float64 if dtype == torch.float64 else torch.float32
     if sharded.rank == sharded.root:

@@ -1,7 +1,8 @@
-"""Levenberg-Marquardt driver on the B200 solver: the reference's ``lm_step`` and
-``bundle_adjustment`` (inference/engine.py:206-334, 405-503) with the same arguments,
-update rules, line search and return values, running ``blast3r_b200.ba_solver`` and the
-library's residual op.
+"""Levenberg-Marquardt step on the B200 solver: the reference's ``lm_step``
+(inference/engine.py:206-334) with the same arguments, update rules, line search and return
+values, running ``blast3r_b200.ba_solver`` and the library's residual op.  The reference's
+phase loop ``bundle_adjustment`` (engine.py:405-503) calls ``lm_step`` and is not mirrored
+here.
 
 Differences: the dense tangent prior (``weight_tan > 0``, ``tangent_reg > 0``) is not
 supported (it is off by default in the reference); with ``recompute_residuals`` (default)
@@ -78,8 +79,12 @@ def line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P, 
         new_loss, new_residuals, _ = objective(**update)
         # the reference's NaN fallback, loss margin and comparison, on the device, read back
         # with the score in one synchronisation
+        # On a NaN loss the reference binds new_loss to the init_loss tensor itself, so its
+        # in-place margin raises init_loss too and every later trial is compared with the
+        # raised value (engine.py:316-318); the same here, in place on init_loss.
         isnan = new_loss.isnan()
-        new_loss = torch.where(isnan, init_loss, new_loss) + min_loss_delta
+        init_loss.add_(torch.where(isnan, min_loss_delta, 0.0).to(init_loss.dtype))
+        new_loss = torch.where(isnan, init_loss, new_loss + min_loss_delta)
         was_nan, lower, new_reproj = torch.stack([isnan.float(), (new_loss < init_loss).float(),
                                                   reproj_score(new_residuals)]).tolist()
         if was_nan and verbose:

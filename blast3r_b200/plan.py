@@ -48,7 +48,7 @@ class SchurSystem:
 
 class BAPlan:
     def __init__(self, infos, pids, n_cams, n_nodes, n_tracks, n_zcf, optim_K=True, optim_P=True,
-                 optim_Z=True, optim_X=True, track_range=None, device=None):
+                 optim_Z=True, optim_X=True, track_range=None, device=None, obs_local=False):
         infos_h = np.ascontiguousarray(torch.as_tensor(infos).detach().cpu().numpy().astype(np.int32))
         pids_h = np.ascontiguousarray(torch.as_tensor(pids).detach().cpu().numpy().astype(np.int32))
         n_imgs = infos_h.shape[1]
@@ -72,7 +72,7 @@ class BAPlan:
                           mask_Z=modes[2][1].ctypes.data_as(u8) if modes[2][1] is not None else None,
                           mask_X=modes[3][1].ctypes.data_as(u8) if modes[3][1] is not None else None,
                           track_begin=t0, track_end=t1,
-                          device=device.index if device.type == 'cuda' else -1)
+                          device=device.index if device.type == 'cuda' else -1, obs_local=int(bool(obs_local)))
         self._h = C.c_void_p()
         L.call('b3r_plan_create', C.byref(self._h), C.byref(desc))
         self.info = L.PlanInfo()
@@ -88,6 +88,13 @@ class BAPlan:
         self.row_ptr, self.col_idx, self.val_off, self.block_size, self.block_off = rp, ci, vo, bs, bo
         self.n_cam_params = i.n_cam_params
         self._ws = None
+
+    def input_obs(self):
+        """Global image-sorted index of every row of the per-observation arrays this plan's
+        linearization reads (all observations, or with ``obs_local`` only this rank's)."""
+        out = np.empty(int(self.info.n_obs_input), np.int32)
+        L.call('b3r_plan_get_input_obs', self._h, out.ctypes.data)
+        return out
 
     def __del__(self):
         h = getattr(self, '_h', None)

@@ -126,8 +126,14 @@ def _track_lengths(spec, n_tracks, max_len, rng):
     return np.clip(L, 2, np.minimum(30, max_len)).astype(np.int64)
 
 
-def _sample_windows(n_imgs, window, loops, L, rng, chunk=1 << 20):
-    """Per track: the L distinct camera ids it is observed in (ragged, flattened)."""
+def _sample_windows(n_imgs, window, loops, L, rng, chunk=1 << 21):
+    """Per track: the L distinct camera ids it is observed in (ragged, flattened).
+
+    A track's candidates are a window of ``window`` consecutive trajectory neighbours, or for
+    a loop-closure track the union of the windows around the two images of a loop pair; its
+    L cameras are the first L candidates in a random order.  The random orders come from a
+    table of 4096 random permutations (one table lookup per track instead of a sort), so
+    every subset of each length stays reachable."""
     T = len(L)
     is_loop = np.zeros(T, bool)
     pairs = None
@@ -136,35 +142,35 @@ def _sample_windows(n_imgs, window, loops, L, rng, chunk=1 << 20):
         v = (u + n_imgs // 2 + rng.integers(-n_imgs // 8, n_imgs // 8 + 1, size=loops)) % n_imgs
         pairs = np.stack([u, v], 1)
         is_loop = rng.random(T) < loops / n_imgs
-    cams = np.empty(int(L.sum()), np.int64)
+    W2 = 2 * window
+    perm1 = rng.permuted(np.tile(np.arange(window, dtype=np.int16), (4096, 1)), axis=1)
+    perm2 = rng.permuted(np.tile(np.arange(W2, dtype=np.int16), (4096, 1)), axis=1)
+    L = np.minimum(L, np.where(is_loop, W2, window))
     ptr = np.concatenate([[0], np.cumsum(L)])
+    cams = np.empty(int(ptr[-1]), np.int64)
     for s in range(0, T, chunk):
         e = min(T, s + chunk)
         n = e - s
-        Lc = L[s:e]
-        Wmax = 2 * window
-        # candidate camera ids per track: its window (or the union of two windows)
         start = rng.integers(0, n_imgs, size=n)
-        cand = (start[:, None] + np.arange(window)[None]) % n_imgs
-        cand = np.concatenate([cand, np.full((n, window), -1)], 1)
-        lp = np.nonzero(is_loop[s:e])[0]
-        if len(lp):
-            k = rng.integers(0, loops, size=len(lp))
-            cu = (pairs[k, 0, None] - window // 2 + np.arange(window)[None]) % n_imgs
-            cv = (pairs[k, 1, None] - window // 2 + np.arange(window)[None]) % n_imgs
-            cand[lp] = np.concatenate([cu, cv], 1)
-        nvalid = np.where(is_loop[s:e], Wmax, window)
-        Lc = np.minimum(Lc, nvalid)
-        L[s:e] = Lc
-        keys = rng.random((n, Wmax))
-        keys[cand < 0] = 2.0                      # never pick padding
-        order = np.argsort(keys, axis=1)
-        picked = np.take_along_axis(cand, order, 1)
-        m = np.arange(Wmax)[None] < Lc[:, None]
-        cams_c = picked[m]
-        cams[ptr[s]:ptr[s] + len(cams_c)] = cams_c
-    ptr = np.concatenate([[0], np.cumsum(L)])
-    return cams[:ptr[-1]], ptr, is_loop
+        lp = is_loop[s:e]
+        order = np.empty((n, W2), np.int16)
+        order[:, :window] = perm1[rng.integers(0, 4096, size=n)]
+        nl = int(lp.sum())
+        if nl:
+            order[lp] = perm2[rng.integers(0, 4096, size=nl)]
+        offs = order.astype(np.int64)
+        cand = (start[:, None] + offs[:, :window]) % n_imgs if not nl else None
+        if nl:
+            cand = np.empty((n, W2), np.int64)
+            cand[~lp, :window] = (start[~lp, None] + offs[~lp, :window]) % n_imgs
+            k = rng.integers(0, loops, size=nl)
+            o = offs[lp]
+            side = o >= window                     # candidate from the second window
+            base = np.where(side, pairs[k, 1, None], pairs[k, 0, None]) - window // 2
+            cand[lp] = (base + np.where(side, o - window, o)) % n_imgs
+        m = np.arange(cand.shape[1])[None] < L[s:e, None]
+        cams[ptr[s]:ptr[e]] = cand[m]
+    return cams, ptr, is_loop
 
 
 def make_scene(cfg, seed=None, n_tracks=None, n_imgs=None, dtype_check=True):

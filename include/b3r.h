@@ -129,6 +129,14 @@ typedef struct {
     int32_t track_begin, track_end;   /* tracks owned by this rank (all: 0, n_tracks)      */
     int32_t device;                   /* CUDA device ordinal the plan lives on; < 0 builds
                                          a host-only plan (info and pattern queries only) */
+    int32_t obs_local;                /* 0: the per-observation arrays handed to the
+                                         linearization (pix2d, pix2d_std, pix2d_dep, and
+                                         residuals / w_pts) are the global image-sorted ones
+                                         (n_obs rows); 1: they hold only the observations of
+                                         this rank's tracks [track_begin, track_end), in
+                                         image-sorted order (n_obs_input rows, the order
+                                         b3r_plan_get_input_obs lists), so a sharded caller
+                                         keeps and copies only its own shard */
 } b3r_plan_desc;
 
 typedef struct {
@@ -143,6 +151,10 @@ typedef struct {
     int32_t nb_K, nb_P, nb_Z;         /* blocks per type                                   */
     int32_t off_P, off_Z;             /* scalar offsets of the tau and zcf ranges          */
     int32_t record_floats;            /* floats per per-observation elimination record     */
+    int64_t n_obs_input;              /* rows of the per-observation input arrays          */
+    int32_t depth_stitch;             /* 1: only depth-coefficient blocks are active (focal
+                                         and pose types off, C <= 8) and the linearization
+                                         runs its depth-stitch passes                       */
 } b3r_plan_info;
 
 /* Build the plan: image -> block maps, the track-sorted observation order, per-warp
@@ -162,6 +174,11 @@ int b3r_plan_get_info(const b3r_plan* plan, b3r_plan_info* info);
  * camera/depth vector).  Any pointer may be NULL. */
 int b3r_plan_get_pattern(const b3r_plan* plan, int32_t* row_ptr, int32_t* col_idx,
                          int64_t* val_off, int32_t* block_size, int32_t* block_off);
+
+/* Global image-sorted index of every row of the per-observation input arrays
+ * (b3r_plan_info.n_obs_input entries): 0, 1, ... n_obs-1 for a plan with obs_local = 0,
+ * else the observations of this rank's tracks in image order.  Host pointer. */
+int b3r_plan_get_input_obs(const b3r_plan* plan, int32_t* obs);
 
 /* Gather the static observation data (device pointers, image-sorted reference layout:
  * pix2d [n_obs,2], pix2d_std [n_obs,2], pix2d_dep [n_obs,C]) into the plan's

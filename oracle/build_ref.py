@@ -23,6 +23,18 @@ REL_SRC = os.path.join('src', 'blast3r', 'extensions', 'cujac', 'sfm_jacobian_ri
 NAME = 'ba_with_rigs_cuda_kernels'
 
 
+def default_reference():
+    """The reference checkout: $B3R_REFERENCE, else a ``reference`` directory beside this
+    repository's own directory; None when neither exists (the GPU box has no checkout and
+    uses the prebuilt extension)."""
+    cands = [os.environ.get('B3R_REFERENCE'),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), 'reference')]
+    for c in cands:
+        if c and os.path.isfile(os.path.join(c, REL_SRC)):
+            return c
+    return None
+
+
 def built_path():
     """Path of the compiled reference extension, or None if it was never built."""
     if not os.path.isdir(OUT_DIR):
@@ -60,9 +72,11 @@ def load_built():
 
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default=os.environ.get('B3R_REFERENCE', '/root/reference'))
+    ap.add_argument('--reference', default=default_reference())
     ap.add_argument('-v', '--verbose', action='store_true')
     a = ap.parse_args()
+    if a.reference is None:
+        sys.exit('no reference checkout found: pass --reference or set B3R_REFERENCE')
     p = build(a.reference, verbose=a.verbose)
     print(p)
     sys.exit(0 if p else 1)

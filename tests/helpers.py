@@ -9,7 +9,8 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden')
 
 # Parity tolerances (fp32 CUDA path vs the fp64 oracle / reference):
 TOL_OBS = 1e-5      # per-observation quantities (residuals, J): max|a-b| / max|b| per component
-TOL_ACC = 1e-4      # accumulated quantities (S, b, diag A): max|a-b| / max|b|
+TOL_ACC = 1e-4      # accumulated blocks (S, diag A): max|a-b| / max|b|
+TOL_B = 1e-5        # the reduced gradient b (north-star tolerance for b): max|a-b| / max|b|
 
 
 def golden_files():

@@ -1,11 +1,11 @@
 """The native PCG (b3r_pcg / b3r_pcg_f64, one cooperative kernel) against the step-by-step
-PCG of ``blast3r_b200.pcg`` (the reference's iteration and stopping rule,
+PCG of ``tests/pcg_stepwise.py`` (the reference's iteration and stopping rule,
 inference/ba_solver.py:1197-1238) on the same assembled S, b and preconditioner."""
 import numpy as np
 import pytest
 import torch
 
-from blast3r_b200.pcg import pcg as pcg_steps
+from tests.pcg_stepwise import pcg as pcg_steps
 from blast3r_b200.synthetic import make_scene
 from tests.helpers import golden_files, load_golden, rel_err, scene_inputs
 from tests.test_gpu_schur import run_plan

@@ -78,3 +78,25 @@ def test_plan_rejects_bad_inputs():
     h = C.c_void_p()
     with pytest.raises(L.B3RError, match='must equal n_obs'):
         L.call('b3r_plan_create', C.byref(h), C.byref(d))
+
+
+def test_local_observation_input_rows():
+    """With obs_local the input rows are this rank's observations in image order."""
+    sc = make_scene(1, n_imgs=40, n_tracks=3000)
+    t0, t1 = 1000, 2200
+    infos = np.ascontiguousarray(sc.infos, np.int32)
+    pids = np.ascontiguousarray(sc.pids, np.int32)
+    for local in (0, 1):
+        d = L.PlanDesc(n_imgs=sc.n_imgs, n_cams=sc.n_cams, n_nodes=sc.n_nodes, n_tracks=sc.n_tracks,
+                       n_obs=sc.n_obs, C=sc.n_zcf, infos=infos.ctypes.data_as(C.POINTER(C.c_int32)),
+                       pids=pids.ctypes.data_as(C.POINTER(C.c_int32)), track_begin=t0, track_end=t1,
+                       device=-1, obs_local=local)
+        h = C.c_void_p()
+        L.call('b3r_plan_create', C.byref(h), C.byref(d))
+        info = L.PlanInfo()
+        L.call('b3r_plan_get_info', h, C.byref(info))
+        rows = np.empty(info.n_obs_input, np.int32)
+        L.call('b3r_plan_get_input_obs', h, rows.ctypes.data)
+        L.lib().b3r_plan_destroy(h)
+        want = np.nonzero((sc.pids >= t0) & (sc.pids < t1))[0] if local else np.arange(sc.n_obs)
+        assert np.array_equal(rows, want)

@@ -47,3 +47,25 @@ def test_masks_and_unpack_delta():
     dK, dP, dZ, dX = s.unpack_delta_inplace(delta)
     assert dK.shape == (8, 2) and dP.shape == (8, 6) and dZ.shape == (8, 5) and dX.shape == (sc.n_tracks, 3)
     assert (dP[0] == 0).all() and (dP[3] == 0).all() and dP[1, 0] == 16
+
+
+def test_plan_cache_sees_a_reordering_of_pids():
+    """Swapping two observations' track ids (positions 1,000,003 apart, which a weighted-sum
+    fingerprint modulo 1,000,003 would not see) must give a new plan."""
+    sc = make_scene(2, n_imgs=100, n_tracks=180000)
+    assert sc.n_obs > 1000010
+    t = _t(sc)
+    BS._PLAN_CACHE.clear()
+    s = BS.GaussNewtonSolver(sc.n_cams, sc.n_nodes, sc.n_imgs, sc.n_tracks, 'cpu')
+    args = (t['rigs'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'])
+    J = s.compute_jacobians(*args, t['pids'], t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    pids = t['pids'].clone()
+    i = int(np.nonzero(sc.pids[:-1000003] != sc.pids[1000003:])[0][0])
+    pids[i], pids[i + 1000003] = t['pids'][i + 1000003], t['pids'][i]
+    J2 = s.compute_jacobians(*args, pids, t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    assert J2.plan is not J.plan
+    J3 = s.compute_jacobians(*args, t['pids'].clone(), t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    assert J3.plan is J.plan
+    t['pids'][i] = t['pids'][i + 1000003]      # an in-place edit of the tensor the plan was built from
+    J4 = s.compute_jacobians(*args, t['pids'], t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
+    assert J4.plan is not J.plan
