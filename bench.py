@@ -228,25 +228,28 @@ class Workload:
 
     def __init__(self, cfg, n_tracks, world, rank, dev, obs_local):
         import torch
-        from blast3r_b200.distributed import ShardedSchur, shard_tracks
+        from blast3r_b200.distributed import ShardedSchur, shard_tracks_by_image
         from blast3r_b200.plan import BAPlan
         self.cfg, self.world, self.rank, self.dev = cfg, world, rank, dev
         tg = time.perf_counter()
         sc = self.sc = cached_scene(cfg, n_tracks=n_tracks)
         self.scene_s = time.perf_counter() - tg
-        self.t0, self.t1, self.n_local = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+        # tracks sharded by first image (each rank's tracks share a range of images)
+        owner, per_rank = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
+        self.n_local = int(per_rank[rank])
+        self.tracks_local = int((owner == rank).sum())
         o = sc.options
         tp = time.perf_counter()
         plan = self.plan = BAPlan(sc.infos, sc.pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf,
                                   optim_K=o['optim_K'], optim_P=o['optim_P'], optim_Z=o['optim_Z'],
-                                  optim_X=o['optim_X'], track_range=(self.t0, self.t1), device=dev,
+                                  optim_X=o['optim_X'], track_owner=owner, rank=rank, device=dev,
                                   obs_local=obs_local)
         torch.cuda.synchronize(dev)
         self.plan_s = time.perf_counter() - tp
         rows = plan.input_obs()
         self.obs_local = obs_local
         # host arrays this rank reads: its observations (all of them on one GPU) and the
-        # parameters (the points of its own tracks only are read)
+        # parameters
         self.host_obs = {k: np.ascontiguousarray(getattr(sc, k)[rows] if obs_local else getattr(sc, k))
                          for k in ('pix2d', 'pix2d_std', 'pix2d_dep')}
         self.host_par = {k: np.ascontiguousarray(getattr(sc, k)) for k in ('K', 'P_rig2cam', 'P_w2rig', 'z_coefs',
@@ -267,7 +270,7 @@ class Workload:
     def release(self):
         import torch
         for k in list(self.__dict__):
-            if k not in ('cfg', 'world', 'rank', 'dev', 'scene_s', 'plan_s', 't0', 't1', 'n_local'):
+            if k not in ('cfg', 'world', 'rank', 'dev', 'scene_s', 'plan_s', 'n_local', 'tracks_local'):
                 delattr(self, k)
         torch.cuda.empty_cache()
 
@@ -332,7 +335,7 @@ def pass_times(wl, reps=5):
 
 def e2e_measure(wl, steps):
     """The same step through the public API from HOST buffers: every step copies this rank's
-    inputs (its observation arrays, the camera parameters and its tracks' points) from
+    inputs (its observation arrays, the camera parameters and the points) from
     pinned memory, re-stages the observations, linearizes (with the NCCL reduce on N GPUs),
     and rank 0 reads S and b back; all inside the timed region.  Two device input sets:
     step k+1's copies run on a copy stream while step k computes.  Returns (ms, h2d bytes,
@@ -341,11 +344,10 @@ def e2e_measure(wl, steps):
     import torch.distributed as dist
     dev, world, rank = wl.dev, wl.world, wl.rank
     pin = {k: torch.from_numpy(v).pin_memory() for k, v in {**wl.host_obs, **wl.host_par}.items()}
-    pts_lo, pts_hi = 3 * wl.t0, 3 * wl.t1          # the points this rank's tracks read
     S, b = wl.sharded.S, wl.sharded.b
     S_h = torch.empty(S.numel(), dtype=torch.float32).pin_memory()
     b_h = torch.empty(b.numel(), dtype=torch.float32).pin_memory()
-    h2d = sum(v.numel() * v.element_size() for k, v in pin.items() if k != 'pts3d') + 4 * (pts_hi - pts_lo)
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
     d2h = (S_h.numel() + b_h.numel()) * 4 if rank == 0 else 0
     sets = [wl.t, {k: torch.empty_like(v) for k, v in wl.t.items()}]
     psets = [wl.params(s_) for s_ in sets]
@@ -358,11 +360,7 @@ def e2e_measure(wl, steps):
             if k >= 2:
                 cs.wait_event(freed[k % 2])          # step k-2 is done with this set
             for key, src in pin.items():
-                dst = sets[k % 2][key]
-                if key == 'pts3d':
-                    dst.view(-1)[pts_lo:pts_hi].copy_(src.view(-1)[pts_lo:pts_hi], non_blocking=True)
-                else:
-                    dst.copy_(src, non_blocking=True)
+                sets[k % 2][key].copy_(src, non_blocking=True)
             copied[k % 2].record(cs)
 
     def compute(k):
@@ -447,7 +445,7 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
     passes = pass_times(wl)
     dom = max((k for k in passes if k not in ('prep', 'finalize')), key=lambda k: passes[k]['ms'])
     # SURVEY 8(d) bytes of what this rank processes: its observations and tracks, and S, b
-    B, nnz_upper = algorithmic_bytes(wl.n_local, wl.t1 - wl.t0, plan.info, plan.block_size)
+    B, nnz_upper = algorithmic_bytes(wl.n_local, wl.tracks_local, plan.info, plan.block_size)
     dom_ms = passes[dom]['ms']
     R = int(plan.info.record_floats)
     inter = {'elimination_records': 2 * 4 * R * int(plan.info.n_obs_local),
@@ -476,7 +474,8 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
                       'n_imgs': sc.n_imgs, 'mean_track_length': sc.meta['mean_track_length'],
                       'n_obs_pairs_rank0': int(plan.info.n_pairs), 'nnz_S': int(plan.info.nnz),
                       'depth_stitch_passes': bool(plan.info.depth_stitch),
-                      'parallelism': f'track-sharded x{wl.world}' + (' + NCCL reduce of S, b' if wl.world > 1 else ''),
+                      'parallelism': f'track-sharded x{wl.world} (tracks by first image)' +
+                                     (' + NCCL reduce of S, b' if wl.world > 1 else ''),
                       'l2': 'inputs larger than L2, no flush'},
            'setup_s': {'scene': round(wl.scene_s, 2), 'plan_rank0': round(wl.plan_s, 2)}}
     if clocks is not None:
@@ -867,14 +866,14 @@ def sharded_lm_iteration(args, dev, world, rank):
     every rank; 3 timed after 3 untimed, max over ranks."""
     import torch
     import torch.distributed as dist
-    from blast3r_b200.distributed import ShardedSchur, shard_tracks, sharded_lm_step
+    from blast3r_b200.distributed import ShardedSchur, shard_tracks_by_image, sharded_lm_step
     from blast3r_b200.plan import BAPlan
     sc = cached_scene(args.config, n_tracks=args.tracks)
     o = sc.options
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
-    t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+    owner, _ = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
     plan = BAPlan(sc.infos, sc.pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
-                  optim_P=o['optim_P'], track_range=(t0, t1), device=dev)
+                  optim_P=o['optim_P'], track_owner=owner, rank=rank, device=dev)
     sh = ShardedSchur(plan)
     last = {}
 

@@ -25,7 +25,8 @@ class PlanDesc(C.Structure):
                 ('n_obs', _i64), ('C', _i32), ('infos', _pi32), ('pids', _pi32),
                 ('mode_K', _i32), ('mode_P', _i32), ('mode_Z', _i32), ('mode_X', _i32),
                 ('mask_K', _pu8), ('mask_P', _pu8), ('mask_Z', _pu8), ('mask_X', _pu8),
-                ('track_begin', _i32), ('track_end', _i32), ('device', _i32), ('obs_local', _i32)]
+                ('track_begin', _i32), ('track_end', _i32), ('device', _i32), ('obs_local', _i32),
+                ('track_owner', _pi32), ('rank', _i32)]
 
 
 class PlanInfo(C.Structure):

@@ -88,6 +88,7 @@ struct PlanBuild {
   // all eliminated tracks (global), grouped
   std::vector<int> all_ptr, all_obs;       // CSR over track id
   std::vector<char> elim;                  // [n_tracks]
+  std::vector<char> owned;                 // [n_tracks] track belongs to this rank
   std::vector<char> obs_live;              // [n_obs] observation touches an active block
   // local side
   std::vector<int> loc_tracks, trk_col, perm_t, trk_t, img_t, pt_task, kof;
@@ -121,6 +122,9 @@ static int build_maps(PlanBuild& B) {
   B3R_REQUIRE(d.track_begin >= 0 && d.track_begin <= d.track_end && d.track_end <= d.n_tracks,
               "bad track range [%d, %d)", d.track_begin, d.track_end);
   B3R_REQUIRE(d.obs_local == 0 || d.obs_local == 1, "obs_local must be 0 or 1");
+  B.owned.assign(d.n_tracks, 0);
+  for (int t = 0; t < d.n_tracks; ++t)
+    B.owned[t] = d.track_owner ? (d.track_owner[t] == d.rank) : (t >= d.track_begin && t < d.track_end);
   const int32_t* cum = d.infos;
   const int32_t* node = d.infos + I;
   const int32_t* cam = d.infos + 2 * I;
@@ -195,8 +199,8 @@ static int build_tracks(PlanBuild& B) {
       if (B.elim[d.pids[o]]) B.all_obs[fill[d.pids[o]]++] = (int)o;
   }
   // local tracks: eliminated, owned, non-empty; ordered by (first image, id)
-  for (int t = d.track_begin; t < d.track_end; ++t)
-    if (B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) B.loc_tracks.push_back(t);
+  for (int t = 0; t < T; ++t)
+    if (B.owned[t] && B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) B.loc_tracks.push_back(t);
   {
     // stable counting sort by first image (tracks arrive in id order)
     std::vector<int> cnt(d.n_imgs + 1, 0), sorted(B.loc_tracks.size());
@@ -248,7 +252,7 @@ static int build_tracks(PlanBuild& B) {
   int last_img = -1, in_chunk = 0;
   for (int64_t o = 0; o < d.n_obs; ++o) {
     const int t = d.pids[o];
-    if (t < d.track_begin || t >= d.track_end || !B.obs_live[o]) continue;
+    if (!B.owned[t] || !B.obs_live[o]) continue;
     const int i = B.img_of[o];
     if (i != last_img || in_chunk == kDiagChunk) {
       B.c1_chunk.push_back((int)B.c1_obs.size());
@@ -676,7 +680,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
     std::vector<int> own(desc->n_obs, -1);
     for (int64_t o = 0; o < desc->n_obs; ++o) {
       const int t = desc->pids[o];
-      if (t >= desc->track_begin && t < desc->track_end) {
+      if (B.owned[t]) {
         own[o] = (int)P->in_obs.size();
         P->in_obs.push_back((int)o);
       }

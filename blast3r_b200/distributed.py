@@ -30,6 +30,32 @@ def shard_tracks(pids, n_tracks, world, rank):
     return bounds[rank], bounds[rank + 1], int(cum[bounds[rank + 1]] - cum[bounds[rank]])
 
 
+def shard_tracks_by_image(infos, pids, n_tracks, world):
+    """Owner rank of every track: tracks ordered by their first image (then id) and cut into
+    ``world`` contiguous runs of about equal observation counts, so that each rank's tracks
+    share a range of images.  A rank then meets about 1/world of the image pairs (segments)
+    instead of a thin slice of all of them: its pair tasks stay long and its partial S
+    touches few block rows.  Returns (owner int32 [n_tracks], observations per rank)."""
+    infos = np.asarray(infos)
+    pids = np.asarray(pids).astype(np.int64)
+    cum = np.asarray(infos[0], np.int64)
+    img = np.repeat(np.arange(len(cum)), np.diff(np.concatenate([[0], cum])))
+    first = np.full(n_tracks, len(cum), np.int64)
+    np.minimum.at(first, pids, img)                   # first image of every track
+    cnt = np.bincount(pids, minlength=n_tracks)
+    order = np.lexsort((np.arange(n_tracks), first))
+    cum_obs = np.cumsum(cnt[order])
+    total = int(cum_obs[-1]) if n_tracks else 0
+    cuts = np.searchsorted(cum_obs, [total * r / world for r in range(1, world)], side='left')
+    rank_of_pos = np.zeros(n_tracks, np.int32)
+    for c in cuts:
+        rank_of_pos[c + 1:] += 1
+    owner = np.empty(n_tracks, np.int32)
+    owner[order] = rank_of_pos
+    per_rank = np.bincount(owner, weights=cnt, minlength=world).astype(np.int64)
+    return owner, per_rank
+
+
 class ShardedSchur:
     """Runs the sharded linearization for one rank's ``BAPlan`` (built with its
     ``track_range``).  The reduced S, b, diag(A) and preconditioner are valid on ``root``."""

@@ -48,7 +48,8 @@ class SchurSystem:
 
 class BAPlan:
     def __init__(self, infos, pids, n_cams, n_nodes, n_tracks, n_zcf, optim_K=True, optim_P=True,
-                 optim_Z=True, optim_X=True, track_range=None, device=None, obs_local=False):
+                 optim_Z=True, optim_X=True, track_range=None, device=None, obs_local=False, track_owner=None,
+                 rank=0):
         infos_h = np.ascontiguousarray(torch.as_tensor(infos).detach().cpu().numpy().astype(np.int32))
         pids_h = np.ascontiguousarray(torch.as_tensor(pids).detach().cpu().numpy().astype(np.int32))
         n_imgs = infos_h.shape[1]
@@ -63,6 +64,12 @@ class BAPlan:
         self._keep = [infos_h, pids_h] + [m for _, m in modes if m is not None]
         u8 = C.POINTER(C.c_uint8)
         t0, t1 = track_range if track_range is not None else (0, n_tracks)
+        owner = None
+        if track_owner is not None:                 # tracks t with track_owner[t] == rank
+            owner = np.ascontiguousarray(np.asarray(track_owner, np.int32))
+            if owner.shape != (n_tracks,):
+                raise ValueError(f'track_owner must have shape ({n_tracks},)')
+            self._keep.append(owner)
         desc = L.PlanDesc(n_imgs=n_imgs, n_cams=n_cams, n_nodes=n_nodes, n_tracks=n_tracks, n_obs=self.n_obs,
                           C=n_zcf, infos=infos_h.ctypes.data_as(C.POINTER(C.c_int32)),
                           pids=pids_h.ctypes.data_as(C.POINTER(C.c_int32)),
@@ -72,7 +79,9 @@ class BAPlan:
                           mask_Z=modes[2][1].ctypes.data_as(u8) if modes[2][1] is not None else None,
                           mask_X=modes[3][1].ctypes.data_as(u8) if modes[3][1] is not None else None,
                           track_begin=t0, track_end=t1,
-                          device=device.index if device.type == 'cuda' else -1, obs_local=int(bool(obs_local)))
+                          device=device.index if device.type == 'cuda' else -1, obs_local=int(bool(obs_local)),
+                          track_owner=owner.ctypes.data_as(C.POINTER(C.c_int32)) if owner is not None else None,
+                          rank=int(rank))
         self._h = C.c_void_p()
         L.call('b3r_plan_create', C.byref(self._h), C.byref(desc))
         self.info = L.PlanInfo()

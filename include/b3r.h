@@ -126,17 +126,23 @@ typedef struct {
     const int32_t* pids;              /* host, int32 [n_obs]                               */
     int32_t mode_K, mode_P, mode_Z, mode_X;          /* B3R_ENABLE_*                       */
     const uint8_t *mask_K, *mask_P, *mask_Z, *mask_X; /* host bool masks for MODE_MASK    */
-    int32_t track_begin, track_end;   /* tracks owned by this rank (all: 0, n_tracks)      */
+    int32_t track_begin, track_end;   /* tracks owned by this rank (all: 0, n_tracks), used
+                                         when track_owner is NULL                          */
     int32_t device;                   /* CUDA device ordinal the plan lives on; < 0 builds
                                          a host-only plan (info and pattern queries only) */
     int32_t obs_local;                /* 0: the per-observation arrays handed to the
                                          linearization (pix2d, pix2d_std, pix2d_dep, and
                                          residuals / w_pts) are the global image-sorted ones
                                          (n_obs rows); 1: they hold only the observations of
-                                         this rank's tracks [track_begin, track_end), in
+                                         this rank's tracks, in
                                          image-sorted order (n_obs_input rows, the order
                                          b3r_plan_get_input_obs lists), so a sharded caller
                                          keeps and copies only its own shard */
+    const int32_t* track_owner;       /* host, int32 [n_tracks] or NULL: when given, this
+                                         rank owns the tracks t with track_owner[t] == rank
+                                         (any partition, e.g. by first image, so that a
+                                         rank's tracks share images) instead of the range */
+    int32_t rank;
 } b3r_plan_desc;
 
 typedef struct {

@@ -23,8 +23,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, cfg, result_path):
-    from blast3r_b200.distributed import ShardedSchur, shard_tracks
+def _rank_main(rank, world, port, cfg, result_path, by_image=False):
+    from blast3r_b200.distributed import ShardedSchur, shard_tracks, shard_tracks_by_image
     from blast3r_b200.plan import BAPlan
     from blast3r_b200.synthetic import make_scene
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
@@ -33,21 +33,27 @@ def _rank_main(rank, world, port, cfg, result_path):
     dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     try:
-        sc = make_scene(cfg, n_imgs=60 if cfg == 1 else None, n_tracks=6000 if cfg == 1 else None)
+        sc = make_scene(cfg, n_imgs=60 if cfg in (1, 4) else None, n_tracks=6000 if cfg in (1, 4) else None)
         o = sc.options
         t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
         lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
                              huber_delta=o['huber_delta'])
 
-        def run(track_range):
+        def run(track_range, **kw):
             plan = BAPlan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
-                          optim_P=o['optim_P'], track_range=track_range, device=dev)
-            p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
-                            t['pix2d_dep'], pix2d=t['pix2d'])
+                          optim_P=o['optim_P'], track_range=track_range, device=dev, **kw)
+            rows = torch.from_numpy(plan.input_obs().astype(np.int64)).to(dev)
+            ob = {k: t[k][rows].contiguous() for k in ('pix2d', 'pix2d_std', 'pix2d_dep')}
+            p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], ob['pix2d_std'],
+                            ob['pix2d_dep'], pix2d=ob['pix2d'])
             return plan, p
 
-        t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
-        plan, p = run((t0, t1))
+        if by_image:       # tracks by first image, each rank fed only its own observations
+            owner, _ = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
+            plan, p = run(None, track_owner=owner, rank=rank, obs_local=True)
+        else:
+            t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+            plan, p = run((t0, t1))
         sh = ShardedSchur(plan).linearize(p, lo)
         torch.cuda.synchronize()
         if rank == 0:
@@ -65,12 +71,12 @@ def _rank_main(rank, world, port, cfg, result_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
-@pytest.mark.parametrize('cfg', [0, 1])
-def test_two_gpu_sharded_schur_equals_single_gpu(cfg, tmp_path):
+@pytest.mark.parametrize('cfg,by_image', [(0, False), (1, False), (1, True), (4, True)])
+def test_two_gpu_sharded_schur_equals_single_gpu(cfg, by_image, tmp_path):
     out = str(tmp_path / 'errs.npy')
-    mp.spawn(_rank_main, args=(2, _free_port(), cfg, out), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(2, _free_port(), cfg, out, by_image), nprocs=2, join=True)
     errs = np.load(out)
-    assert (errs < 1e-4).all(), errs
+    assert (errs[:1] < 1e-4).all() and errs[1] < 1e-5 and errs[2] < 1e-4, errs
 
 
 def _lm_rank_main(rank, world, port, result_path):

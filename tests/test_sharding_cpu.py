@@ -18,18 +18,20 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from blast3r_b200 import _lib as L
-from blast3r_b200.distributed import shard_tracks
+from blast3r_b200.distributed import shard_tracks, shard_tracks_by_image
 from blast3r_b200.synthetic import make_scene
 from oracle import ba_oracle as O
 from tests.helpers import rel_err, scene_inputs
 
 
-def _host_plan(sc, t0, t1):
+def _host_plan(sc, t0, t1, owner=None, rank=0):
     infos = np.ascontiguousarray(sc.infos, np.int32)
     pids = np.ascontiguousarray(sc.pids, np.int32)
+    own = np.ascontiguousarray(owner, np.int32) if owner is not None else None
     d = L.PlanDesc(n_imgs=sc.n_imgs, n_cams=sc.n_cams, n_nodes=sc.n_nodes, n_tracks=sc.n_tracks, n_obs=sc.n_obs,
                    C=sc.n_zcf, infos=infos.ctypes.data_as(C.POINTER(C.c_int32)),
-                   pids=pids.ctypes.data_as(C.POINTER(C.c_int32)), track_begin=t0, track_end=t1, device=-1)
+                   pids=pids.ctypes.data_as(C.POINTER(C.c_int32)), track_begin=t0, track_end=t1, device=-1,
+                   track_owner=own.ctypes.data_as(C.POINTER(C.c_int32)) if own is not None else None, rank=rank)
     h = C.c_void_p()
     L.call('b3r_plan_create', C.byref(h), C.byref(d))
     info = L.PlanInfo()
@@ -65,20 +67,48 @@ def test_shard_plans_share_pattern_and_partition_work(world):
     assert max(per) < 1.05 * sc.n_obs / world + 30
 
 
+@pytest.mark.parametrize('world', [2, 4, 8])
+def test_image_sharding_partitions_work_on_fewer_segments(world):
+    """Tracks sharded by first image: the ranks partition tracks, observations and pairs,
+    share one S layout, stay balanced by observations, and each meets far fewer image-pair
+    segments (longer pair tasks) than with id-range sharding."""
+    sc = make_scene(2, n_imgs=200, n_tracks=40000)
+    full, pat = _host_plan(sc, 0, sc.n_tracks)
+    owner, per_rank = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
+    assert owner.shape == (sc.n_tracks,) and set(np.unique(owner)) == set(range(world))
+    assert per_rank.sum() == sc.n_obs and per_rank.max() < 1.05 * sc.n_obs / world + 40
+    pairs = tracks = obs = tasks_img = tasks_id = 0
+    for r in range(world):
+        info, p = _host_plan(sc, 0, 0, owner=owner, rank=r)
+        assert all(np.array_equal(a, b) for a, b in zip(p, pat))
+        pairs += info.n_pairs
+        tracks += info.n_tracks_local
+        obs += info.n_obs_local
+        tasks_img += info.n_pair_tasks
+        t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, r)
+        tasks_id += _host_plan(sc, t0, t1)[0].n_pair_tasks
+    assert (pairs, tracks, obs) == (full.n_pairs, full.n_tracks_local, full.n_obs_local)
+    assert tasks_img < (0.8 if world == 2 else 0.5) * tasks_id, (tasks_img, tasks_id)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(('127.0.0.1', 0))
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, result_path):
+def _rank_main(rank, world, port, result_path, by_image):
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
     dist.init_process_group('gloo', rank=rank, world_size=world)
     try:
         sc = make_scene(0, n_imgs=10, n_tracks=300, seed=9)
         inp, opts = scene_inputs(sc), dict(sc.options)
-        t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
-        mask = (sc.pids >= t0) & (sc.pids < t1)
+        if by_image:
+            owner, _ = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
+            mask = owner[sc.pids] == rank
+        else:
+            t0, t1, _ = shard_tracks(sc.pids, sc.n_tracks, world, rank)
+            mask = (sc.pids >= t0) & (sc.pids < t1)
         part = O.linearize(inp, opts, obs_mask=mask)
         lam = part['lam']
         S_part = torch.from_numpy(part['S'] - np.diag(lam))         # undamped partial S
@@ -102,8 +132,9 @@ def _rank_main(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
-def test_gloo_two_ranks_partial_systems_sum_to_full(tmp_path):
+@pytest.mark.parametrize('by_image', [False, True], ids=['id-ranges', 'by-image'])
+def test_gloo_two_ranks_partial_systems_sum_to_full(tmp_path, by_image):
     out = str(tmp_path / 'errs.npy')
-    mp.spawn(_rank_main, args=(2, _free_port(), out), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(2, _free_port(), out, by_image), nprocs=2, join=True)
     errs = np.load(out)
     assert (errs < 1e-9).all(), errs
