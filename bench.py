@@ -587,8 +587,10 @@ def internal_ref_gpu(args):
     """Child process: the reference's GaussNewtonSolver on this B200 with its own compiled
     CUDA ops, float64 (its production dtype) and float32; the linearization up to the PCG, and
     the full solve_delta (PCG and back-substitution)."""
+    import faulthandler
     import torch
     from oracle import ref_runner as RR
+    faulthandler.enable()
     ba_solver, engine = RR.import_reference(cpu_ops=False)
     sc = cached_scene(args.config, n_tracks=args.tracks)
     t = RR.tensors(sc.lm_inputs(), 'cuda')
@@ -640,8 +642,8 @@ def run_child(mode, extra):
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, cwd=ROOT)
     lines = [ln for ln in r.stdout.strip().splitlines() if ln.startswith('{')]
     if r.returncode != 0 or not lines:
-        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ['no output']
-        return {'unavailable': f'{mode} exited {r.returncode}: {tail[0][:300]}'}
+        tail = (r.stderr or r.stdout).strip().splitlines()[-12:] or ['no output']
+        return {'unavailable': f'{mode} exited {r.returncode}', 'stderr_tail': [t[:300] for t in tail]}
     return json.loads(lines[-1])
 
 

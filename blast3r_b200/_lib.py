@@ -14,6 +14,7 @@ B3R_F32, B3R_F64 = 0, 1
 ENABLE_ALL, ENABLE_ZERO, ENABLE_MASK = 0, 1, 2
 PASS_PREP, PASS_POINTS, PASS_FACTOR, PASS_DIAG, PASS_PAIRS = 0, 1, 2, 3, 4
 PASS_ELIMINATE = PASS_FACTOR   # former name
+PCG_TEST_UNREACHABLE_BARRIER = 1
 
 _i32, _i64, _f32, _f64, _vp = C.c_int32, C.c_int64, C.c_float, C.c_double, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)
@@ -94,6 +95,10 @@ _SIGS = {
     'b3r_reproj_score': (C.c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     'b3r_pcg': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
     'b3r_pcg_f64': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _f64, C.c_int, _vp, _vp, _vp]),
+    'b3r_tangent_prior': (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _i32, _f64, _f64, _i32, _i32, _vp,
+                                    _vp, _vp, _vp]),
+    'b3r_lin_add_zprior': (C.c_int, [_vp, _vp, _vp, _vp, C.POINTER(Outputs), _vp]),
+    'b3r_pcg_ex': (C.c_int, [_vp, _vp, _vp, _vp, _vp, C.c_int, _f64, C.c_int, _i64, C.c_int, _vp, _vp, _vp]),
 }
 
 _lib = None

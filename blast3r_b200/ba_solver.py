@@ -114,7 +114,7 @@ class GaussNewtonSolver:
                        pix2d_std=pix2d_std, pix2d_dep=pix2d_dep, pix2d=pix2d)
         return Linearization(plan, tensors, flags)
 
-    def linearize(self, J, residuals=None, w_pts=None, clamp_w=(1e-6, 1e6), lin_kw=None):
+    def linearize(self, J, residuals=None, w_pts=None, clamp_w=(1e-6, 1e6), lin_kw=None, z_prior=None):
         """Run the fused linearization; returns the SchurSystem (S, b, diag A, preconditioner)."""
         t, f = J.tensors, J.flags
         kw = dict(lin_kw or {})
@@ -131,7 +131,7 @@ class GaussNewtonSolver:
         else:
             p = J.plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
                               t['pix2d_dep'], residuals=residuals, w_pts=w_pts)
-        J.system = J.plan.linearize(p, opts)
+        J.system = J.plan.linearize(p, opts, z_prior=z_prior)
         return J.system
 
     def solve_delta(self, J, residuals, w_pts, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
@@ -139,9 +139,19 @@ class GaussNewtonSolver:
         Schur complement (ba_solver.py:110-182); float32 like the reference."""
         assert residuals.shape == (self.n_kpts, 3)
         assert w_pts.shape in ((self.n_kpts, 1), (self.n_kpts, 3))
-        if z_prior is not None and z_prior[0] is not None:
-            raise NotImplementedError('dense tangent prior (z_prior) is not supported by the fused path yet')
-        s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw)
+        zp = None
+        if z_prior is not None:
+            H_z, g_z = z_prior
+            if H_z is not None and g_z is not None:
+                # the reference's checks (ba_solver.py:149-157): one C x C block per enabled image
+                assert g_z.shape == (self.imgs.n, self.n_zcf), \
+                    f"bad g_z shape {g_z.shape}, expected {(self.imgs.n, self.n_zcf)}"
+                assert H_z.shape == (self.imgs.n, self.n_zcf, self.n_zcf), \
+                    f"bad H_z shape {H_z.shape}, expected {(self.imgs.n, self.n_zcf, self.n_zcf)}"
+                if self.imgs.true_idxs is not None and self.imgs.n != self.imgs.true_n:
+                    raise TypeError('z_prior with a partial depth-coefficient mask is not supported')
+                zp = (H_z, g_z)
+        s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw, z_prior=zp)
         dt = torch.float64 if self.dtype == torch.float64 else torch.float32
         # the reference's PCG (ba_solver.py:202, 1197-1238) as one device kernel on the explicit S
         delta_c, niter, conv = s.plan.pcg(s.S_vals, s.precond, s.b.to(dt), tol=1e-6, maxiter=300)

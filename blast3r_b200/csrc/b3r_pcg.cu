@@ -5,16 +5,24 @@
 // 300): x0 = 0, Jacobi preconditioner, stop at the first iterate with ||r|| <= tol ||b||
 // (returned), break on a non-finite r.z, else return the best-so-far iterate.  Each of its
 // iterations is a dozen small launches with a host synchronisation.  Here the whole loop is
-// ONE cooperative kernel: a grid-wide barrier (bounded spin, co-residency guaranteed by the
-// cooperative launch) separates
-//   phase A  the decisions on the previous iterate (best-so-far copy, convergence,
-//            non-finite break, beta), p = z + beta p computed on the fly inside the matvec
-//            Ap = S p (row panels of the symmetric S, built once per solve, cut into
-//            <= 256-column warp tasks; a row of several tasks adds its parts atomically)
-//            and the partial sums of p.Ap
-//   phase B  x += alpha p, r -= alpha Ap, z = r / M and the partial sums of r.r and r.z
-// so an iteration costs two barriers.  Vectors are float or double (the solver's dtype);
-// reductions accumulate in double.
+// ONE cooperative kernel running the pipelined form of the same iteration (Ghysels and
+// Vanroose, "Hiding global synchronization latency in the preconditioned conjugate gradient
+// algorithm", Parallel Computing 40, 2014, algorithm 4): with u = M^-1 r, w = S u,
+// m = M^-1 w, n = S m and the recurrences z = n + beta z, q = m + beta q, s = w + beta s,
+// p = u + beta p, x += alpha p, r -= alpha s, u -= alpha q, w -= alpha z, the iterate, its
+// residual and the reference's r.z are those of the standard iteration, while the dot
+// products (r.u, w.u, r.r) and the matvec n = S m of one iteration depend only on the
+// previous iteration's vectors.  So one grid barrier per iteration suffices:
+//   after the barrier every block sums the previous iteration's partial dot products in the
+//   same fixed order, takes the reference's decisions (best-so-far copy, convergence,
+//   non-finite break), forms alpha and beta, computes n = S m for its row group (row panels
+//   of the symmetric S, built once per solve, cut into <= 256-column warp tasks whose partial
+//   row sums go to fixed shared-memory slots, summed in task order: deterministic), updates
+//   its rows of the eight vectors and publishes its partial dot products.
+// Each block row belongs to one block's row group, so the update of a row never waits for
+// another block; only m, which every block's matvec reads, is kept in two buffers by
+// iteration parity.  Vectors are float or double (the solver's dtype); reductions
+// accumulate in double.
 #include <algorithm>
 #include <cstring>
 #include "b3r_common.cuh"
@@ -25,10 +33,13 @@ namespace b3r {
 namespace {
 
 constexpr int kPcgThreads = 256;
-constexpr int kBarrierSpins = 1 << 24;   // polls before a grid barrier gives up
+// Polls (each followed by a 32 ns sleep) before a grid barrier gives up: about half a
+// second, far beyond any barrier of a running solve; b3r_pcg_ex takes another limit.
+constexpr long long kBarrierSpins = 1 << 24;
+constexpr int kPcgVectors = 11;      // double vectors in the work buffer
 
 // Work buffer layout: barrier words | per-block arrival flags | per-block partial sums |
-// the seven vectors.  Same-address atomics from every block serialise at one L2 slice, so
+// the vectors.  Same-address atomics from every block serialise at one L2 slice, so
 // neither the barrier nor the reductions use them: each block writes its own flag and its
 // own partial sums, and every block sums all partials in the same fixed order.
 constexpr int kPcgMaxBlocks = 1024;
@@ -36,16 +47,21 @@ constexpr size_t kPcgFlagsOff = 256, kPcgPartOff = kPcgFlagsOff + 4 * kPcgMaxBlo
 constexpr size_t kPcgVecOff = kPcgPartOff + 4 * 8 * kPcgMaxBlocks;
 static_assert(kPcgMaxBlocks % kPcgThreads == 0, "barrier flags per polling thread");
 
-inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the seven vectors
-  return (kPcgVecOff + 7 * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
+inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the vectors
+  return (kPcgVecOff + kPcgVectors * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
 }
 
 struct PcgWords {
   unsigned int bar_gen, unused;
 };
-// per-block partial sums: [0] p.Ap, [1] r.r, [2] r.z (prologue: b.b and r0.z0)
+// per-block partial sums of the next iteration's r.u, w.u and r.r (prologue: r0.u0, w0.u0, b.b)
 struct PcgPart {
   double v[4];
+};
+
+struct BarrierCfg {
+  long long spins;     // polls before a wait gives up
+  bool unreachable;    // test mode: block 0 waits for an arrival no block ever makes
 };
 
 constexpr unsigned int kGenAbort = 0x80000000u;   // in bar_gen: the barrier was abandoned
@@ -65,12 +81,15 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
 // acquire-poll the flags, then thread 0 of block 0 release-stores bar_gen = target, which
 // thread 0 of every other block acquire-polls before a block-wide __syncthreads (the
 // release/acquire pair and the CTA barriers order every thread's writes before the barrier
-// with every thread's reads after it).  Every poll is bounded (kBarrierSpins).  A block
+// with every thread's reads after it).  Every poll is bounded (cfg.spins).  A block
 // that gives up waiting for bar_gen leaves with false and sets its flag to kFlagAbort; block
 // 0, seeing such a flag or giving up on one, publishes bar_gen with kGenAbort, and every
 // block that reads it leaves with false, so all of them leave the loop at this barrier or
 // the next one.
-__device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, unsigned int target) {
+// With cfg.unreachable (a test of the failure path) block 0 waits for flag values one
+// generation beyond what any block publishes, so its wait always runs out.
+__device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, unsigned int target,
+                                             const BarrierCfg& cfg) {
   __shared__ int ok_s;
   __syncthreads();                                       // the block's writes precede its arrival
   if (threadIdx.x == 0) {
@@ -91,13 +110,14 @@ __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, u
         f[j] = b < (int)gridDim.x ? ld_acquire(flags + b) : target;
       }
       bool all = true;
+      const unsigned int want = cfg.unreachable ? target + 1 : target;
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         if (f[j] == kFlagAbort) bad = true;
-        if (f[j] < target) all = false;
+        if (f[j] < want) all = false;
       }
       if (all) break;
-      if (spins >= kBarrierSpins) { bad = true; break; }
+      if (spins >= cfg.spins) { bad = true; break; }
       __nanosleep(32);
     }
     if (bad) ok_s = 0;
@@ -107,7 +127,7 @@ __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, u
     int spins = 0;
     unsigned int g;
     while (((g = ld_acquire(&w->bar_gen)) & ~kGenAbort) < target) {
-      if (++spins > kBarrierSpins) break;
+      if (++spins > cfg.spins) break;
       __nanosleep(32);
     }
     if ((g & ~kGenAbort) < target || (g & kGenAbort)) {
@@ -117,62 +137,6 @@ __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, u
   }
   __syncthreads();
   return ok_s != 0;
-}
-
-// Sum of v over the block (valid on thread 0).
-__device__ __forceinline__ double block_sum(double v, double* red) {
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  double t = 0.0;
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kPcgThreads / 32; ++i) t += red[i];
-  return t;
-}
-
-// Sum over blocks of partial field f, the same fixed order in every block; broadcast to
-// every thread of the block.
-__device__ __forceinline__ double grid_sum(const PcgPart* part, int f, double* red, double* bcast) {
-  double v = 0.0;
-  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) v += __ldcg(&part[b].v[f]);
-  const double t = block_sum(v, red);
-  if (threadIdx.x == 0) *bcast = t;
-  __syncthreads();
-  return *bcast;
-}
-
-// Sums of (u, v) over the block (valid on thread 0).
-__device__ __forceinline__ double2 block_sum2(double u, double v, double2* red2) {
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) {
-    u += __shfl_xor_sync(0xffffffffu, u, d);
-    v += __shfl_xor_sync(0xffffffffu, v, d);
-  }
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red2[w] = make_double2(u, v);
-  __syncthreads();
-  double2 t = make_double2(0.0, 0.0);
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kPcgThreads / 32; ++i) { t.x += red2[i].x; t.y += red2[i].y; }
-  return t;
-}
-
-// Sums over blocks of partial fields f and f + 1 in one pass, the same fixed order in every
-// block; broadcast to every thread of the block.
-__device__ __forceinline__ double2 grid_sum2(const PcgPart* part, int f, double2* red2, double2* bcast) {
-  double u = 0.0, v = 0.0;
-  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
-    u += __ldcg(&part[b].v[f]);
-    v += __ldcg(&part[b].v[f + 1]);
-  }
-  const double2 t = block_sum2(u, v, red2);
-  if (threadIdx.x == 0) *bcast = t;
-  __syncthreads();
-  return *bcast;
 }
 
 // Row panels of the symmetric S (once per solve, before the PCG kernel): warp per
@@ -192,167 +156,281 @@ __global__ void __launch_bounds__(256) k_build_panels(DevPlan d, const float* __
   }
 }
 
-// The lanes of a warp compute the part of y_p = sum_c panel_p[r][c] x[col_c] over panel
-// columns [c0, c1) of block row p (panel P of width W, column list cols) (at most kMvCols = 256, so at most eight per lane), with
-// x = z + beta * pold formed on the fly.  The panel rows are read coalesced (consecutive
-// lanes, consecutive columns) and so mostly are the x values (a block's columns are
-// consecutive scalars).  Every lane returns the partial y_p[r] (r < bp) in yo.
-template <typename T, int MAXB>
+// The lanes of a warp compute the part of y_p = sum_c panel_p[r][c] v[col_c] over panel
+// columns [c0, c1) of block row p (panel P of width W, column list cols; at most kMvCols =
+// 256, so at most eight per lane), in double, with v = src[col] (or src[col] / M[col] when
+// DIV).  The panel rows are read coalesced (consecutive lanes, consecutive columns) and so
+// mostly are the v values (a block's columns are consecutive scalars).  Every lane returns
+// the partial y_p[r] (r < bp) in yo.
+template <typename TS, int MAXB, bool DIV>
 __device__ __forceinline__ void panel_matvec(const float* __restrict__ P, const int* __restrict__ cols, int W, int bp,
-                                             int c0, int c1, const T* __restrict__ z, const T* __restrict__ pold,
-                                             T beta, int lane, T yo[MAXB]) {
+                                             int c0, int c1, const TS* __restrict__ src, const float* __restrict__ M,
+                                             int lane, double yo[MAXB]) {
   constexpr int CPL = kMvCols / 32;                      // columns per lane
-  T xc[CPL];
+  double xc[CPL];
   bool has[CPL];
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
     const int c = c0 + lane + 32 * j;
     has[j] = c < c1;
     const int col = has[j] ? __ldg(cols + c) : 0;
-    xc[j] = has[j] ? __ldcg(z + col) + beta * __ldcg(pold + col) : T(0);   // other blocks wrote them
+    if (DIV) xc[j] = has[j] ? (double)src[col] / (double)__ldg(M + col) : 0.0;
+    else     xc[j] = has[j] ? (double)__ldcg(src + col) : 0.0;   // other blocks wrote it
   }
-  T y[MAXB];
+  double y[MAXB];
 #pragma unroll
-  for (int r = 0; r < MAXB; ++r) y[r] = T(0);
+  for (int r = 0; r < MAXB; ++r) y[r] = 0.0;
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
     if (!has[j]) continue;
     const int c = c0 + lane + 32 * j;
 #pragma unroll
     for (int r = 0; r < MAXB; ++r)
-      if (r < bp) y[r] += (T)__ldg(P + (int64_t)r * W + c) * xc[j];
+      if (r < bp) y[r] += (double)__ldg(P + (int64_t)r * W + c) * xc[j];
   }
 #pragma unroll
   for (int r = 0; r < MAXB; ++r) {
-    T v = y[r];
+    double v = y[r];
 #pragma unroll
     for (int dd = 16; dd > 0; dd >>= 1) v += __shfl_xor_sync(0xffffffffu, v, dd);
     yo[r] = v;
   }
 }
 
-// Three blocks per SM (<= 85 registers): more resident warps than matvec tasks leaves fewer
-// warps with two tasks, and the slowest warp sets each iteration's pace (8.0 vs 9.8 ms for
-// the cfg2 solve with two blocks per SM).
-template <typename T, int MAXB>
-__global__ void __launch_bounds__(kPcgThreads, 3) k_pcg(DevPlan d, const float* __restrict__ S,
-                                                     const float* __restrict__ M, const T* __restrict__ b,
-                                                     T* __restrict__ xo, double tol, int maxiter, char* work,
-                                                     const float* __restrict__ pan, int* result) {
-  __shared__ double red[kPcgThreads / 32];
-  __shared__ double bc;
-  __shared__ double2 red2[kPcgThreads / 32];
-  __shared__ double2 bc2;
-  PcgWords* w = reinterpret_cast<PcgWords*>(work);
+// The matvec of row group g: every task's partial row sums into its shared-memory slots.
+template <typename TS, int MAXB, bool DIV>
+__device__ __forceinline__ void group_matvec(const DevPlan& d, const float* __restrict__ pan, int4 g,
+                                             const TS* __restrict__ src, const float* __restrict__ M, double* slots) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int task = g.x + warp; task < g.y; task += kPcgThreads / 32) {
+    const int4 tk = __ldg(d.mv_task + task);             // block row, panel columns [c0, c1), flags
+    const int4 rw = __ldg(d.mv_row + task);              // boff, W, panel offset / 4, column-list offset
+    const int bp = tk.w >> 8, slot = __ldg(d.mv_slot + task);
+    double yo[MAXB];
+    panel_matvec<TS, MAXB, DIV>(pan + 4 * (int64_t)rw.z, d.pan_col + rw.w, rw.y, bp, tk.y, tk.z, src, M, lane, yo);
+#pragma unroll
+    for (int rr = 0; rr < MAXB; ++rr)
+      if (lane == rr && rr < bp) slots[slot + rr] = yo[rr];
+  }
+}
+
+// (S v)_j of scalar j of the current row group: its row's task slots summed in task order.
+__device__ __forceinline__ double slot_sum(const DevPlan& d, int j, const double* slots) {
+  const int2 sc = __ldg(d.pcg_scl + j);
+  const int nt = sc.y & 0xffff, stride = sc.y >> 16;
+  double v = 0.0;
+  for (int t = 0; t < nt; ++t) v += slots[sc.x + t * stride];
+  return v;
+}
+
+// Sums of (u, v, w) over the block (valid on thread 0).
+__device__ __forceinline__ double3 block_sum3(double u, double v, double w, double3* red3) {
+#pragma unroll
+  for (int dd = 16; dd > 0; dd >>= 1) {
+    u += __shfl_xor_sync(0xffffffffu, u, dd);
+    v += __shfl_xor_sync(0xffffffffu, v, dd);
+    w += __shfl_xor_sync(0xffffffffu, w, dd);
+  }
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red3[wp] = make_double3(u, v, w);
+  __syncthreads();
+  double3 t = make_double3(0.0, 0.0, 0.0);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPcgThreads / 32; ++i) { t.x += red3[i].x; t.y += red3[i].y; t.z += red3[i].z; }
+  return t;
+}
+
+// Sums over blocks of partial fields 0..2, the same fixed order in every block; broadcast to
+// every thread of the block.
+__device__ __forceinline__ double3 grid_sum3(const PcgPart* part, double3* red3, double3* bcast) {
+  double u = 0.0, v = 0.0, w = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    u += __ldcg(&part[b].v[0]);
+    v += __ldcg(&part[b].v[1]);
+    w += __ldcg(&part[b].v[2]);
+  }
+  const double3 t = block_sum3(u, v, w, red3);
+  if (threadIdx.x == 0) *bcast = t;
+  __syncthreads();
+  return *bcast;
+}
+
+// Three blocks per SM (<= 85 registers); the planner sizes the row groups for that many.
+// TI is the type of b and x (the solver's dtype); the iteration runs in double either way.
+template <typename TI, int MAXB>
+__global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
+    DevPlan d, const float* __restrict__ M, const TI* __restrict__ b, TI* __restrict__ xo, double tol, int maxiter,
+    char* work, const float* __restrict__ pan, int* result, long long spin_limit, int test_flags) {
+  __shared__ double slots[kPcgSlots];
+  __shared__ double3 red3[kPcgThreads / 32];
+  __shared__ double3 bc3;
+  PcgWords* wd = reinterpret_cast<PcgWords*>(work);
   unsigned int* flags = reinterpret_cast<unsigned int*>(work + kPcgFlagsOff);
   PcgPart* part = reinterpret_cast<PcgPart*>(work + kPcgPartOff);
-  T* vec = reinterpret_cast<T*>(work + kPcgVecOff);
-  const int n = d.n_cam_params;
-  T* x = vec;                          // iterate (each element owned by one thread)
-  T* r = vec + n;                      // residual (owned)
-  T* z = vec + 2 * (int64_t)n;         // preconditioned residual (owned; read by the matvec)
-  T* Ap = vec + 3 * (int64_t)n;        // S p (written by the matvec warps)
-  T* pbuf0 = vec + 4 * (int64_t)n;     // search direction, double-buffered by iteration parity
-  T* pbuf1 = vec + 5 * (int64_t)n;
-  T* bx = vec + 6 * (int64_t)n;        // best-so-far iterate (owned)
-  const int tid = blockIdx.x * blockDim.x + threadIdx.x, nth = gridDim.x * blockDim.x;
-  const int lane = threadIdx.x & 31;
-  const int gw = tid >> 5, nwarps = nth >> 5;
+  double* vec = reinterpret_cast<double*>(work + kPcgVecOff);
+  const int64_t n = d.n_cam_params;
+  double* x = vec;                     // every vector element is owned by the block of its row group
+  double* r = vec + n;
+  double* u = vec + 2 * n;
+  double* w = vec + 3 * n;
+  double* z = vec + 4 * n;
+  double* q = vec + 5 * n;
+  double* s = vec + 6 * n;
+  double* p = vec + 7 * n;
+  double* bx = vec + 8 * n;            // best-so-far iterate
+  double* mb[2] = {vec + 9 * n, vec + 10 * n};   // m = M^-1 w by iteration parity (read by every block)
+  BarrierCfg bcfg{spin_limit, (test_flags & 1) != 0};
   unsigned int target = 0;
+  auto publish = [&](double a, double b2, double c) {
+    const double3 t = block_sum3(a, b2, c, red3);
+    if (threadIdx.x == 0) { part[blockIdx.x].v[0] = t.x; part[blockIdx.x].v[1] = t.y; part[blockIdx.x].v[2] = t.z; }
+  };
 
-  // prologue: x0 = 0, r0 = b - S x0 = b, z0 = M^-1 r0, p = z0 (formed on the fly from p_old = 0)
-  double s_rz = 0.0, s_bb = 0.0;
-  for (int i = tid; i < n; i += nth) {
-    const T bi = b[i], zi = bi / (T)M[i];
-    x[i] = T(0); r[i] = bi; z[i] = zi; pbuf0[i] = T(0); pbuf1[i] = T(0); bx[i] = T(0); Ap[i] = T(0);
-    s_rz += (double)bi * (double)zi;
-    s_bb += (double)bi * (double)bi;
+  // prologue: x0 = 0, r0 = b, u0 = M^-1 b, w0 = S u0, m0 = M^-1 w0, and the partial sums of
+  // r0.u0, w0.u0, b.b
+  double s_g = 0.0, s_d = 0.0, s_bb = 0.0;
+  for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+    const int4 g = __ldg(d.pcg_grp + gi);
+    group_matvec<TI, MAXB, true>(d, pan, g, b, M, slots);
+    __syncthreads();
+    for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+      const double bj = (double)b[j], Mj = (double)M[j];
+      const double uj = bj / Mj, wj = slot_sum(d, j, slots);
+      x[j] = 0.0; r[j] = bj; u[j] = uj; w[j] = wj; mb[0][j] = wj / Mj;
+      z[j] = 0.0; q[j] = 0.0; s[j] = 0.0; p[j] = 0.0; bx[j] = 0.0;
+      s_g += bj * uj;
+      s_d += wj * uj;
+      s_bb += bj * bj;
+    }
+    __syncthreads();
   }
-  double2 t2 = block_sum2(s_bb, s_rz, red2);
-  if (threadIdx.x == 0) { part[blockIdx.x].v[1] = t2.x; part[blockIdx.x].v[2] = t2.y; }
-  bool ok = grid_barrier(w, flags, ++target);
-  t2 = grid_sum2(part, 1, red2, &bc2);
-  const double bnorm = fmax(sqrt(t2.x), 1e-12);
-  double rz_old = t2.y;
-  double rn = 0.0, rz_new = 0.0;
+  publish(s_g, s_d, s_bb);
+  bool ok = grid_barrier(wd, flags, ++target, bcfg);
+  double3 t3 = grid_sum3(part, red3, &bc3);
+  double gamma = t3.x, delta = t3.y;
+  const double bnorm = fmax(sqrt(t3.z), 1e-12);
+  double rn = sqrt(t3.z), gamma_old = 0.0, alpha_old = 1.0;
 
   double best = __longlong_as_double(0x7ff0000000000000LL);   // +inf
   int best_k = 0, k_stop = 0;
   bool converged = false;
   for (int k = 1; ok && k <= maxiter + 1; ++k) {
-    // ---- phase A: decisions on iterate k-1 (identical in every thread) ----
-    double beta = 0.0;
+    // ---- decisions on iterate k-1 (x_{k-1}, r_{k-1}; identical in every thread) ----
     if (k > 1) {
+      if (rn <= tol * bnorm) {
+        // The recurrences' residual may drift from b - S x: confirm with the true residual
+        // before stopping.  If it is not below the tolerance, the iteration continues from
+        // true values (residual replacement): r = b - S x, u = M^-1 r, w = S u, s = S p,
+        // z = S q, m = M^-1 w.
+        double s_rr = 0.0;
+        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+          const int4 g = __ldg(d.pcg_grp + gi);
+          group_matvec<double, MAXB, false>(d, pan, g, x, M, slots);
+          __syncthreads();
+          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+            const double rj = (double)b[j] - slot_sum(d, j, slots);
+            r[j] = rj;
+            u[j] = rj / (double)M[j];
+            s_rr += rj * rj;
+          }
+          __syncthreads();
+        }
+        publish(0.0, 0.0, s_rr);
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+        t3 = grid_sum3(part, red3, &bc3);
+        rn = sqrt(t3.z);
+        if (rn <= tol * bnorm) { converged = true; k_stop = k - 1; break; }
+        s_g = 0.0; s_d = 0.0;
+        double* mc = mb[(k - 1) & 1];
+        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+          const int4 g = __ldg(d.pcg_grp + gi);
+          group_matvec<double, MAXB, false>(d, pan, g, u, M, slots);
+          __syncthreads();
+          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+            const double wj = slot_sum(d, j, slots);
+            w[j] = wj;
+            mc[j] = wj / (double)M[j];
+            s_g += r[j] * u[j];
+            s_d += wj * u[j];
+          }
+          __syncthreads();
+          group_matvec<double, MAXB, false>(d, pan, g, p, M, slots);
+          __syncthreads();
+          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) s[j] = slot_sum(d, j, slots);
+          __syncthreads();
+          group_matvec<double, MAXB, false>(d, pan, g, q, M, slots);
+          __syncthreads();
+          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) z[j] = slot_sum(d, j, slots);
+          __syncthreads();
+        }
+        publish(s_g, s_d, 0.0);
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+        t3 = grid_sum3(part, red3, &bc3);
+        gamma = t3.x;
+        delta = t3.y;
+      }
       if (rn < best) {                                   // best-so-far iterate
         best = rn;
         best_k = k - 1;
-        for (int i = tid; i < n; i += nth) bx[i] = x[i];
-      }
-      if (rn <= tol * bnorm) { converged = true; k_stop = k - 1; break; }
-      if (!isfinite(rz_new)) break;
-      beta = rz_new / fmax(rz_old, 1e-32);
-      rz_old = rz_new;
-    }
-    if (k > maxiter) break;
-    const T* pold = (k & 1) ? pbuf0 : pbuf1;
-    T* pnew = (k & 1) ? pbuf1 : pbuf0;
-    const T tb = (T)beta;
-    double s_pap = 0.0;
-    for (int task = gw; task < d.n_mv_tasks; task += nwarps) {   // warp per matvec task
-      const int4 tk = __ldg(d.mv_task + task);           // block row, panel columns [c0, c1), flags
-      const int4 rw = __ldg(d.mv_row + task);            // boff, W, panel offset / 4, column-list offset
-      const int bp = tk.w >> 8, op = rw.x;
-      const bool single = tk.w & 1, first = tk.w & 2;
-      // this lane's scalar of the row (lane < bp): its new search direction, loaded early
-      const T pn = lane < bp ? __ldcg(z + op + lane) + tb * __ldcg(pold + op + lane) : T(0);
-      T yo[MAXB];
-      panel_matvec<T, MAXB>(pan + 4 * (int64_t)rw.z, d.pan_col + rw.w, rw.y, bp, tk.y, tk.z, z, pold, tb, lane, yo);
-#pragma unroll
-      for (int rr = 0; rr < MAXB; ++rr) {
-        if (lane == rr && rr < bp) {
-          if (single) Ap[op + rr] = yo[rr];              // the row is one task
-          else atomicAdd(Ap + op + rr, yo[rr]);          // zeroed by the previous phase B
-          if (first) pnew[op + rr] = pn;
-          s_pap += (double)pn * (double)yo[rr];          // p.Ap is linear in the row's tasks
+        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+          const int4 g = __ldg(d.pcg_grp + gi);
+          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) bx[j] = x[j];
         }
       }
+      if (!isfinite(gamma)) break;                       // the reference's r.z
     }
-    const double t = block_sum(s_pap, red);
-    if (threadIdx.x == 0) part[blockIdx.x].v[0] = t;
-    if (!(ok = grid_barrier(w, flags, ++target))) break;
-    // ---- phase B: x, r, z and the partial sums of r.r and r.z ----
-    const double alpha = rz_old / fmax(grid_sum(part, 0, red, &bc), 1e-32);
-    const T ta = (T)alpha;
+    if (k > maxiter) break;
+    // ---- iteration k-1 of the pipelined recurrences ----
+    const double beta = k > 1 ? gamma / fmax(gamma_old, 1e-32) : 0.0;
+    const double den = k > 1 ? delta - beta * gamma / alpha_old : delta;   // = p.S p
+    const double alpha = gamma / fmax(den, 1e-32);
+    const double* mc = mb[(k - 1) & 1];
+    double* mn = mb[k & 1];
     double s_rr = 0.0;
-    s_rz = 0.0;
-    for (int i = tid; i < n; i += nth) {
-      const T xi = x[i] + ta * __ldcg(pnew + i);
-      const T ri = r[i] - ta * __ldcg(Ap + i);
-      Ap[i] = T(0);                                      // for the next matvec's atomics
-      const T zi = ri / (T)M[i];
-      x[i] = xi; r[i] = ri; z[i] = zi;
-      s_rr += (double)ri * (double)ri;
-      s_rz += (double)ri * (double)zi;
+    s_g = 0.0; s_d = 0.0;
+    for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+      const int4 g = __ldg(d.pcg_grp + gi);
+      group_matvec<double, MAXB, false>(d, pan, g, mc, M, slots);
+      __syncthreads();
+      for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+        const double nj = slot_sum(d, j, slots), mj = mc[j], wj = w[j], uj = u[j];
+        const double zj = nj + beta * z[j], qj = mj + beta * q[j], sj = wj + beta * s[j], pj = uj + beta * p[j];
+        const double xj = x[j] + alpha * pj, rj = r[j] - alpha * sj, un = uj - alpha * qj, wn = wj - alpha * zj;
+        z[j] = zj; q[j] = qj; s[j] = sj; p[j] = pj;
+        x[j] = xj; r[j] = rj; u[j] = un; w[j] = wn;
+        mn[j] = wn / (double)M[j];
+        s_g += rj * un;
+        s_d += wn * un;
+        s_rr += rj * rj;
+      }
+      __syncthreads();
     }
-    t2 = block_sum2(s_rr, s_rz, red2);
-    if (threadIdx.x == 0) { part[blockIdx.x].v[1] = t2.x; part[blockIdx.x].v[2] = t2.y; }
-    if (!(ok = grid_barrier(w, flags, ++target))) break;
-    t2 = grid_sum2(part, 1, red2, &bc2);
-    rn = sqrt(t2.x);
-    rz_new = t2.y;
+    publish(s_g, s_d, s_rr);
+    if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+    t3 = grid_sum3(part, red3, &bc3);
+    gamma_old = gamma;
+    alpha_old = alpha;
+    gamma = t3.x;
+    delta = t3.y;
+    rn = sqrt(t3.z);
   }
-  // the converging iterate, else the best-so-far one (zeros if none improved)
-  for (int i = tid; i < n; i += nth) xo[i] = ok ? (converged ? x[i] : bx[i]) : T(0);
-  if (tid == 0) {
+  // the converging iterate, else the best-so-far one (zeros if none improved or a barrier
+  // gave up)
+  for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+    const int4 g = __ldg(d.pcg_grp + gi);
+    for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) xo[j] = ok ? (TI)(converged ? x[j] : bx[j]) : TI(0);
+  }
+  if (!ok && threadIdx.x == 0) atomicOr(result + 2, 1);   // any block that gave up flags the solve
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
     result[0] = converged ? k_stop : best_k;
     result[1] = converged ? 1 : 0;
-    result[2] = ok ? 0 : 1;     // 1: a grid barrier gave up
   }
 }
 
 template <typename T, int MAXB>
 int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b, T* xo, double tol, int maxiter,
-               void* work, int* result, cudaStream_t s) {
+               long long spin_limit, int test_flags, void* work, int* result, cudaStream_t s) {
   const DevPlan& d = plan->d;
   static int per_sm = 0, n_sm = 0;         // one occupancy query per instantiation
   if (per_sm == 0) {
@@ -363,15 +441,14 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
                        "pcg occupancy"));
     B3R_REQUIRE(per_sm >= 1, "the PCG kernel does not fit on an SM");
   }
-  const int want = (d.n_mv_tasks * 32 + kPcgThreads - 1) / kPcgThreads;   // one warp per matvec task
-#ifndef B3R_PCG_BLOCKS_PER_SM
-#define B3R_PCG_BLOCKS_PER_SM 0   // 0: as many as fit (more blocks make each grid barrier dearer)
-#endif
-  const int cap = B3R_PCG_BLOCKS_PER_SM > 0 ? std::min(per_sm, B3R_PCG_BLOCKS_PER_SM) : per_sm;
-  const int grid = std::max(1, std::min(want, cap * n_sm));        // all co-resident
+  // one block per row group where they all fit at once (cooperative: all co-resident); the
+  // blocks take the groups with a stride otherwise
+  const int grid = std::max(1, std::min(d.n_pcg_groups, per_sm * n_sm));
   B3R_REQUIRE(grid <= kPcgMaxBlocks, "internal: PCG grid %d > %d", grid, kPcgMaxBlocks);
-  // barrier words and arrival flags start at zero (targets count up from 1 in every launch)
+  // barrier words and arrival flags start at zero (targets count up from 1 in every launch);
+  // result[2] is set by any block whose barrier wait runs out
   B3R_TRY(check_cuda(cudaMemsetAsync(work, 0, kPcgPartOff, s), "clear PCG barrier words"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(result, 0, 3 * sizeof(int), s), "clear PCG result"));
   DevPlan dv = d;
   char* wk = reinterpret_cast<char*>(work);
   float* pan = reinterpret_cast<float*>(wk + pcg_panel_off(d));
@@ -379,7 +456,7 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
   k_build_panels<<<grid_for((int64_t)n_ent * 32, 256), 256, 0, s>>>(dv, S, pan);
   B3R_TRY(check_launch("pcg panels"));
   const float* panc = pan;
-  void* args[] = {&dv, &S, &M, &b, &xo, &tol, &maxiter, &wk, &panc, &result};
+  void* args[] = {&dv, &M, &b, &xo, &tol, &maxiter, &wk, &panc, &result, &spin_limit, &test_flags};
   B3R_TRY(check_cuda(cudaLaunchCooperativeKernel((const void*)k_pcg<T, MAXB>, dim3(grid), dim3(kPcgThreads), args,
                                                  0, s),
                      "pcg cooperative launch"));
@@ -388,10 +465,12 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
 
 template <typename T>
 int pcg_impl(const b3r_plan* plan, const float* S, const float* M, const T* b, T* xo, double tol, int maxiter,
-             void* work, int* result, void* stream) {
+             long long spin_limit, int flags, void* work, int* result, void* stream) {
   B3R_REQUIRE(plan && S && M && b && xo && work && result, "NULL argument");
   B3R_REQUIRE(((uintptr_t)work & 255) == 0, "PCG work buffer must be 256-byte aligned");
   B3R_REQUIRE(maxiter >= 0, "maxiter must be >= 0");
+  B3R_REQUIRE(spin_limit >= 1, "the barrier spin limit must be >= 1");
+  B3R_REQUIRE((flags & ~B3R_PCG_TEST_UNREACHABLE_BARRIER) == 0, "unknown PCG flags %d", flags);
   int dev = -1;
   B3R_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   B3R_REQUIRE(dev == plan->device, "current device %d differs from the plan's device %d", dev, plan->device);
@@ -399,9 +478,9 @@ int pcg_impl(const b3r_plan* plan, const float* S, const float* M, const T* b, T
   int maxb = 0;
   for (int v : plan->pat.bsize) maxb = std::max(maxb, v);
   cudaStream_t s = as_stream(stream);
-  if (maxb <= 8) return pcg_launch<T, 8>(plan, S, M, b, xo, tol, maxiter, work, result, s);
+  if (maxb <= 8) return pcg_launch<T, 8>(plan, S, M, b, xo, tol, maxiter, spin_limit, flags, work, result, s);
   B3R_REQUIRE(maxb <= 32, "block size %d > 32", maxb);
-  return pcg_launch<T, 32>(plan, S, M, b, xo, tol, maxiter, work, result, s);
+  return pcg_launch<T, 32>(plan, S, M, b, xo, tol, maxiter, spin_limit, flags, work, result, s);
 }
 
 }  // namespace
@@ -416,10 +495,22 @@ extern "C" int64_t b3r_pcg_work_bytes(const b3r_plan* plan) {
 
 extern "C" int b3r_pcg(const b3r_plan* plan, const float* S_vals, const float* precond, const float* b, float* x,
                        double tol, int maxiter, void* work, int* result, void* stream) {
-  return pcg_impl<float>(plan, S_vals, precond, b, x, tol, maxiter, work, result, stream);
+  return pcg_impl<float>(plan, S_vals, precond, b, x, tol, maxiter, kBarrierSpins, 0, work, result, stream);
 }
 
 extern "C" int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond, const double* b,
                            double* x, double tol, int maxiter, void* work, int* result, void* stream) {
-  return pcg_impl<double>(plan, S_vals, precond, b, x, tol, maxiter, work, result, stream);
+  return pcg_impl<double>(plan, S_vals, precond, b, x, tol, maxiter, kBarrierSpins, 0, work, result, stream);
+}
+
+extern "C" int b3r_pcg_ex(const b3r_plan* plan, const float* S_vals, const float* precond, const void* b, void* x,
+                          int dtype, double tol, int maxiter, int64_t barrier_spin_limit, int flags, void* work,
+                          int* result, void* stream) {
+  const long long spins = barrier_spin_limit > 0 ? (long long)barrier_spin_limit : kBarrierSpins;
+  if (dtype == B3R_F64)
+    return pcg_impl<double>(plan, S_vals, precond, (const double*)b, (double*)x, tol, maxiter, spins, flags, work,
+                            result, stream);
+  B3R_REQUIRE(dtype == B3R_F32, "dtype must be B3R_F32 or B3R_F64");
+  return pcg_impl<float>(plan, S_vals, precond, (const float*)b, (float*)x, tol, maxiter, spins, flags, work, result,
+                         stream);
 }

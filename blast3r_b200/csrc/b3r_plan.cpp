@@ -101,10 +101,14 @@ struct PlanBuild {
   std::vector<int> task_seg;
   // pattern
   std::vector<int> row_ptr, col_idx, val_off;
-  std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr;
+  std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr, img_zdiag, img_zsc;
   std::vector<int4> t_idx, c1_idx;
   std::vector<int> sym_ptr, sym_ent;
   std::vector<int4> mv_task, mv_row, mv_ent;
+  std::vector<int4> pcg_grp;
+  std::vector<int> mv_slot;
+  std::vector<int2> pcg_scl;
+  int pcg_target_groups = 444;
   std::vector<int64_t> pan_off;
   std::vector<int> pan_w, col_off, pan_col, ent_col, ent_row;
   int64_t pan_floats = 0;
@@ -570,6 +574,47 @@ static int build_pattern(PlanBuild& B) {
       }
     }
     B.pan_floats = poff;
+    // PCG row groups: cut the block rows into contiguous groups of about total / target
+    // panel work (a heavier row is a group of its own), at most kPcgSlots task-row sums each
+    int64_t total = 0;
+    for (int pr = 0; pr < nb; ++pr) total += (int64_t)B.bsize[pr] * B.pan_w[pr];
+    const int64_t target = std::max<int64_t>(1, total / std::max(1, B.pcg_target_groups));
+    B.mv_slot.assign(B.mv_task.size(), 0);
+    const int ncp_all = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
+    B.pcg_scl.assign(ncp_all, make_int2(0, 0));
+    int task0 = 0;
+    for (int pr = 0; pr < nb;) {
+      int slots = 0, t_begin = task0;
+      int64_t work = 0;
+      const int sc_begin = B.boff[pr];
+      int q = pr;
+      for (; q < nb; ++q) {
+        const int nt = (B.pan_w[q] + kMvCols - 1) / kMvCols;
+        const int64_t wq = (int64_t)B.bsize[q] * B.pan_w[q];
+        if (q > pr && (work + wq > target || slots + nt * B.bsize[q] > kPcgSlots)) break;
+        for (int t = 0; t < nt; ++t) B.mv_slot[task0 + t] = slots + t * B.bsize[q];
+        for (int r = 0; r < B.bsize[q]; ++r) B.pcg_scl[B.boff[q] + r] = make_int2(slots + r, nt | (B.bsize[q] << 16));
+        slots += nt * B.bsize[q];
+        work += wq;
+        task0 += nt;
+      }
+      B3R_REQUIRE(slots <= kPcgSlots, "internal: PCG row group needs %d slots", slots);
+      B.pcg_grp.push_back(make_int4(t_begin, task0, sc_begin, B.boff[q - 1] + B.bsize[q - 1]));
+      pr = q;
+    }
+    B3R_REQUIRE(task0 == (int)B.mv_task.size(), "internal: PCG groups cover %d of %zu tasks", task0,
+                B.mv_task.size());
+  }
+  // every image's zcf diagonal block, also when the type is switched off (a dense prior can
+  // still be added there)
+  B.img_zdiag.assign(I, -1);
+  B.img_zsc.assign(I, -1);
+  for (int i = 0; i < I; ++i) {
+    const int col = B.Z.col[i];
+    if (col < 0) continue;
+    const int p = B.K.n_cols + B.P.n_cols + col;
+    B.img_zdiag[i] = pat_lookup(B, p, p);
+    B.img_zsc[i] = B.boff[p];
   }
   // diagonal scalar positions
   const int ncp = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
@@ -624,6 +669,11 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   *out = nullptr;
   PlanBuild B;
   B.d = desc;
+  if (desc->device >= 0) {
+    int n_sm = 0;
+    if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, desc->device) == cudaSuccess && n_sm > 0)
+      B.pcg_target_groups = kPcgBlocksPerSm * n_sm;
+  }
   try {
     B3R_TRY(build_maps(B));
     B3R_TRY(build_tracks(B));
@@ -696,6 +746,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   }
   Arena A;
   A.add(B.img_bk, &d.img_bk); A.add(B.img_sc, &d.img_sc); A.add(B.img_dst, &d.img_dst);
+  A.add(B.img_zdiag, &d.img_zdiag); A.add(B.img_zsc, &d.img_zsc);
   A.add(B.img_node, &d.img_node); A.add(B.img_cam, &d.img_cam);
   A.add(desc->obs_local ? perm_dev : B.perm_t, &d.perm_t); A.add(B.trk_t, &d.trk_t); A.add(B.img_t, &d.img_t);
   A.add(B.loc_tracks, &d.trk_gid); A.add(B.trk_col, &d.trk_col); A.add(B.pt_task, &d.pt_task);
@@ -713,6 +764,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
   A.add(B.mv_task, &d.mv_task); A.add(B.mv_row, &d.mv_row); A.add(B.mv_ent, &d.mv_ent);
   d.n_mv_tasks = (int)B.mv_task.size();
+  A.add(B.pcg_grp, &d.pcg_grp); A.add(B.mv_slot, &d.mv_slot); A.add(B.pcg_scl, &d.pcg_scl);
+  d.n_pcg_groups = (int)B.pcg_grp.size();
   A.add(B.pan_off, &d.pan_off); A.add(B.pan_w, &d.pan_w); A.add(B.col_off, &d.col_off);
   A.add(B.pan_col, &d.pan_col); A.add(B.ent_col, &d.ent_col); A.add(B.ent_row, &d.ent_row);
   d.pan_floats = B.pan_floats;

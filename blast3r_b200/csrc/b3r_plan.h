@@ -23,6 +23,8 @@ constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal ch
 constexpr int kPointTask = 32;     // max observations per point task (one warp)
 constexpr int kImgRecFloats = 32;  // floats per per-image camera record
 constexpr int kMvCols = 256;       // max panel columns per matvec task (8 per lane)
+constexpr int kPcgSlots = 1024;    // per-task partial row sums one PCG row group keeps in shared memory
+constexpr int kPcgBlocksPerSm = 3; // resident PCG blocks per SM the row groups are sized for
 
 // sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
 constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
@@ -40,6 +42,9 @@ struct DevPlan {
   const int* img_bk;      // [n_imgs*3] active block of (foc, tau, zcf) per image, -1 if none
   const int* img_sc;      // [n_imgs*3] scalar offset of those blocks, -1 if none
   const int* img_dst;     // [n_imgs*6] value offset of the image's own (f,f),(f,t),(f,z),(t,t),(t,z),(z,z)
+  const int* img_zdiag;   // [n_imgs] value offset of the image's zcf diagonal block (any mode but
+                          //  a masked-out image: -1)
+  const int* img_zsc;     // [n_imgs] scalar offset of that block
   const int* img_node;    // [n_imgs]
   const int* img_cam;     // [n_imgs]
 
@@ -112,6 +117,14 @@ struct DevPlan {
   const int* pan_col;     // [sum W_p]
   const int* ent_col;     // [2*nnzb - nb] first panel column of each symmetric entry
   const int* ent_row;     // [2*nnzb - nb] block row of each symmetric entry
+  // PCG row groups: contiguous block rows whose matvec tasks and vector updates one CTA does
+  // (so the update of a row never waits for another CTA's matvec); about one group per
+  // resident CTA, balanced by panel work
+  int n_pcg_groups;
+  const int4* pcg_grp;    // [n_pcg_groups] (first task, end task, first scalar, end scalar)
+  const int* mv_slot;     // [n_mv_tasks] first shared-memory slot of the task's row sums
+  const int2* pcg_scl;    // [n_cam_params] (slot of the scalar's first task, the row's task
+                          //  count | block size << 16): the scalar sums its tasks' slots in order
 };
 
 struct HostPattern {

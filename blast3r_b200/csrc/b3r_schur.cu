@@ -7,10 +7,10 @@
 //   points    track-major, one warp per <=32-observation task: per-track Hpp and g_p by a
 //             segmented warp scan, and the max |diag(Hpp)| for adaptive damping
 //   factor    per track: damped guarded 3x3 Cholesky Hpp = L L^T (sfm_jacobian_rigs.cu
-//             :578-617), stored in reciprocal form, and z = L^-1 g_p
+//             :578-617), stored in reciprocal form, and the point step Hpp^-1 g_p (double)
 //   diag      image-major: per observation the elimination record Y = L^-1 Hpc in reduced
 //             form (3 x [f0 f1 tau0..5 zscale]) + its depth channels, written to its
-//             image-major slot; Hcc - Y^T Y and g_c - Y^T z expanded to the typed blocks of
+//             image-major slot; Hcc - Y^T Y and g_c - Hcp Hpp^-1 g_p expanded to the typed blocks of
 //             its image, reduced per image chunk, one atomic per value per chunk; also
 //             diag(Hcc) for the damping and preconditioner
 //   pairs     segment-major: for every image pair (i, i') the sum over shared tracks of
@@ -245,7 +245,7 @@ struct ObsIn {
   float px, py, sx, sy;
   float dep[CT];
   float4 tf0, tf1;  // track factor (reciprocal form) and z, track-record floats 12..19
-  float tf2;        // track-record float 20
+  float4 tf2;       // track-record floats 20..23: z[2], delta = Hpp^-1 g_p
 };
 
 template <int CT>
@@ -267,8 +267,7 @@ __device__ __forceinline__ void load_obs_in(const Ctx& c, int e, int ee, ObsIn<C
   if (in.ix.y >= 0) {
     // trec is 256-byte aligned with 96-byte records: floats 12..19 are two aligned float4
     const float4* t4 = reinterpret_cast<const float4*>(c.trec + (int64_t)in.ix.w * 24 + 12);
-    in.tf0 = t4[0]; in.tf1 = t4[1];
-    in.tf2 = c.trec[(int64_t)in.ix.w * 24 + 20];
+    in.tf0 = t4[0]; in.tf1 = t4[1]; in.tf2 = t4[2];
   }
 }
 
@@ -428,10 +427,10 @@ __global__ void __launch_bounds__(128) k_points(Ctx c) {
 }
 
 // Pass "factor": damped Cholesky factor of every local track (BlockDiagMat.dampen_ then
-// chol3x3_solve's guarded factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599)
-// and z = L^-1 g_p.  The factor is stored in reciprocal form (1/l00, l10, l20, 1/l11,
-// l21, 1/l22) at track-record floats 12..17, z at 18..20, so the per-observation
-// elimination Y = L^-1 Hpc needs no division.
+// chol3x3_solve's guarded factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599),
+// z = L^-1 g_p and the point step delta = Hpp^-1 g_p.  The factor is stored in reciprocal
+// form (1/l00, l10, l20, 1/l11, l21, 1/l22) at track-record floats 12..17, z at 18..20,
+// delta at 21..23, so the per-observation elimination Y = L^-1 Hpc needs no division.
 __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   const int tl = blockIdx.x * blockDim.x + threadIdx.x;
   const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
@@ -446,9 +445,17 @@ __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   chol3<float>(h00, h01, h02, h01, h11, h12, h02, h12, h22, 1e-12f, l);
   const float g[3] = {b.z, b.w, g8};
   chol3_fwd<float>(l, g, z);
+  // the point step delta = Hpp^-1 g_p, solved in double (the gradient's elimination term
+  // Hcp delta is formed with it, as the reference's rhs g_c - B D^-1 g_p, ba_solver.py:188)
+  double ld[6], zd[3], dd[3];
+  const double gd[3] = {(double)b.z, (double)b.w, (double)g8};
+  chol3<double>((double)h00, (double)h01, (double)h02, (double)h01, (double)h11, (double)h12, (double)h02,
+                (double)h12, (double)h22, 1e-12, ld);
+  chol3_fwd<double>(ld, gd, zd);
+  chol3_bwd<double>(ld, zd, dd);
   t4[3] = make_float4(1.f / l[0], l[1], l[2], 1.f / l[3]);    // floats 12..15
   t4[4] = make_float4(l[4], 1.f / l[5], z[0], z[1]);          // floats 16..19
-  t4[5] = make_float4(z[2], 0.f, 0.f, 0.f);                   // floats 20..23 (21..23 unused)
+  t4[5] = make_float4(z[2], (float)dd[0], (float)dd[1], (float)dd[2]);   // floats 20..23
 }
 
 // ------------------------------------------------------------------------------------
@@ -474,7 +481,7 @@ __host__ __device__ constexpr int sym_idx(int a, int b, int n) { return a * n - 
 
 template <int CT>
 __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, bool elim, int64_t e, float4 tf0,
-                                           float4 tf1, float tf2, float* __restrict__ out) {
+                                           float4 tf1, float4 tf2, float* __restrict__ out) {
   // value v of this observation goes to out[v] (its lane's row of the warp's transpose
   // buffer), as soon as it is computed
   using Lay = DiagLayout<CT>;
@@ -505,17 +512,23 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
   for (int t = 0; t < 6; ++t) out[Lay::DA + 2 + t] = H[2 + t][2 + t];
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) out[Lay::DA + 8 + ch] = H[8][8] * V.dep[ch] * V.dep[ch];
-  if (elim) {                                     // eliminated track: record Y, subtract Y^T Y, Y^T z
+  if (elim) {              // eliminated track: record Y, subtract Y^T Y and Hcp delta (delta = Hpp^-1 g_p)
     const float li[6] = {tf0.x, tf0.y, tf0.z, tf0.w, tf1.x, tf1.y};
     float Y[9][3];
     elim_record<CT>(c, e, V, li, Y);
-    const float z0 = tf1.z, z1 = tf1.w, z2 = tf2;
+    float jd[3];                                  // Jpw delta, so that Hcp delta = Jcw^T (Jpw delta)
+#pragma unroll
+    for (int i = 0; i < 3; ++i) jd[i] = fmaf(V.Jpw[3 * i + 2], tf2.w, fmaf(V.Jpw[3 * i + 1], tf2.z, V.Jpw[3 * i] * tf2.y));
 #pragma unroll
     for (int a = 0; a < 9; ++a) {
 #pragma unroll
       for (int b = a; b < 9; ++b)
         H[a][b] = fmaf(-Y[a][2], Y[b][2], fmaf(-Y[a][1], Y[b][1], fmaf(-Y[a][0], Y[b][0], H[a][b])));
-      g[a] = fmaf(-Y[a][2], z2, fmaf(-Y[a][1], z1, fmaf(-Y[a][0], z0, g[a])));
+      float hd = V.Jcw[18 + a] * jd[2];
+#pragma unroll
+      for (int i = 1; i >= 0; --i)
+        if (jc_nz(i, a)) hd = fmaf(V.Jcw[9 * i + a], jd[i], hd);
+      g[a] -= hd;
     }
   }
   out[Lay::FF + 0] = H[0][0];
@@ -959,7 +972,7 @@ __global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* _
 // observation's depth channels, and every Schur term is a scalar times an outer product of
 // depth vectors:
 //   image block      (zw^2 - y.y) dep dep^T
-//   gradient         (zw sqrt(W_z) r_z - y.z) dep          (z = L^-1 g_p)
+//   gradient         (zw sqrt(W_z) r_z - zw Jpw[2].delta) dep   (delta = Hpp^-1 g_p)
 //   diag(A)          zw^2 dep_c^2
 //   pair product     (y_o . y_o') dep_o dep_o'^T
 // These are the general passes' values with the focal and pose columns left out (the same
@@ -1022,13 +1035,14 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
     const float zw = V.Jcw[26];
     const float d = zw * zw;
     float a = d, g = zw * V.sWr[2];
-    if (cur.ix.y >= 0) {                          // eliminated track: record y, subtract y.y, y.z
+    if (cur.ix.y >= 0) {                          // eliminated track: record y, subtract y.y and Hcp delta
       const float h0 = V.Jpw[6] * zw, h1 = V.Jpw[7] * zw, h2 = V.Jpw[8] * zw;
       const float y0 = h0 * cur.tf0.x;
       const float y1 = (h1 - cur.tf0.y * y0) * cur.tf0.w;
       const float y2 = (h2 - cur.tf0.z * y0 - cur.tf1.x * y1) * cur.tf1.y;
       a = fmaf(-y2, y2, fmaf(-y1, y1, fmaf(-y0, y0, a)));
-      g = fmaf(-y2, cur.tf2, fmaf(-y1, cur.tf1.w, fmaf(-y0, cur.tf1.z, g)));
+      // Hcp delta = zw (Jpw[2] . delta), delta = Hpp^-1 g_p
+      g -= zw * fmaf(V.Jpw[8], cur.tf2.w, fmaf(V.Jpw[7], cur.tf2.z, V.Jpw[6] * cur.tf2.y));
       float rv[R];
       rv[0] = y0; rv[1] = y1; rv[2] = y2;
 #pragma unroll
@@ -1154,7 +1168,8 @@ __global__ void k_fin_apply(Ctx c, const float* __restrict__ diagA, float* __res
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= c.d.n_cam_params) return;
   const int t = scalar_type(c.d, j);
-  const int zero = t == 0 ? c.d.zeroK : (t == 1 ? c.d.zeroP : c.d.zeroZ);
+  // a switched-off zcf type that received a dense prior is damped like a block diagonal
+  const int zero = t == 0 ? c.d.zeroK : (t == 1 ? c.d.zeroP : (c.d.zeroZ && c.misc[8] == 0.f));
   // BlockDiagMat.dampen_ scales by max |diag| of the type; ZerosMat.dampen_ uses 1e-12*I
   const float lam = zero ? c.dampen : c.dampen * (c.adaptive ? c.misc[4 + t] : 1.f);
   S[c.d.sdiag_pos[j]] += lam;
@@ -1526,6 +1541,7 @@ extern "C" int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const 
   B3R_TRY(check_cuda(cudaMemsetAsync(out->S_vals, 0, sizeof(float) * (size_t)c.d.nnz, s), "memset S"));
   B3R_TRY(check_cuda(cudaMemsetAsync(out->b, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset b"));
   B3R_TRY(check_cuda(cudaMemsetAsync(out->diagA, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset diagA"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(c.misc + 8, 0, sizeof(float), s), "memset prior flag"));
   switch (c.d.C) {
 #define X(CC) case CC: return launch_assemble<CC>(c, out->S_vals, out->b, out->diagA, s);
     B3R_FOR_EACH_C(X)

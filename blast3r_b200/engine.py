@@ -4,10 +4,10 @@ values, running ``blast3r_b200.ba_solver`` and the library's residual op.  The r
 phase loop ``bundle_adjustment`` (engine.py:405-503) calls ``lm_step`` and is not mirrored
 here.
 
-Differences: the dense tangent prior (``weight_tan > 0``, ``tangent_reg > 0``) is not
-supported (it is off by default in the reference); with ``recompute_residuals`` (default)
-the linearization recomputes residuals and weights in-kernel instead of reading the
-objective's tensors (same device function, same values).
+The dense tangent prior (``weight_tan > 0``, engine.py:15-158, 253-299) runs on the
+library's ``b3r_tangent_prior`` kernel (``blast3r_b200.prior``).  With
+``recompute_residuals`` (default) the linearization recomputes residuals and weights
+in-kernel instead of reading the objective's tensors (same device function, same values).
 """
 from collections import namedtuple
 
@@ -16,6 +16,7 @@ import torch
 from . import _lib as L
 from .ba_solver import GaussNewtonSolver
 from .cujac import exp_se3, residuals_with_rigs as residual_func
+from .prior import dense_tangent_prior_terms
 
 BA_Status = namedtuple('BA_Status', 'init_loss, init_residuals, new_loss, new_residuals')
 
@@ -111,9 +112,10 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
     solve, back-substitution, then the line search over step scales 1, 1/2, 1/4, 1/8,
     1/64, 1/512, 1/4096, 0 with the degenerate-geometry reject."""
     assert depth_mode in ('lin', 'log')
-    if weight_tan > 0:
-        raise NotImplementedError('the dense tangent prior is not supported by the B200 solver')
     is_depth_log = depth_mode == 'log'
+    if weight_tan > 0:
+        # implemented for log-depth combination only (engine.py:237-239)
+        assert is_depth_log, 'tangent prior currently only implemented for depth_mode="log"'
     n_imgs = rigs.shape[1]
     fin = []                 # the inputs' all-finite flags, checked together below
     assert shape_of(rigs, finite=fin) == (3, n_imgs)
@@ -136,20 +138,37 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
     assert n_obs >= n_tracks, 'there must be more 2d kpts than tracks'
     assert huber_delta >= 0.1
 
+    # the prior treats the intrinsics as constant within a step (engine.py:258-260)
+    K_tan = K.detach()
+
     def objective(K, P_w2rig, pts3d, z_coefs):
         residuals_, err_pts_, w_pts_ = residual_func(
             rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep, is_depth_log,
             weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
-        return err_pts_.mean(), residuals_, w_pts_
+        loss = err_pts_.mean()
+        if weight_tan > 0:
+            tan_loss, _, _ = dense_tangent_prior_terms(
+                rigs, K_tan, z_coefs, log_depth_maps, conf, pts3d_ref, weight_tan=float(weight_tan),
+                tan_stride=int(tan_stride), optim_Z0=optim_Z0, dtype=loss.dtype, compute_gn=False,
+                normalize_tangents=bool(normalize_tangents))
+            loss = loss + tan_loss
+        return loss, residuals_, w_pts_
 
     init_loss, init_residuals, w_pts = objective(K, P_w2rig, pts3d, z_coefs)
     jac = GaussNewtonSolver(n_cams, n_nodes, n_imgs, n_tracks, pts3d.device, dampen=dampen, **ba_options)
+    z_prior = None
+    if weight_tan > 0:                 # adds only to the depth-coefficient normal equations
+        _, g_z, H_z = dense_tangent_prior_terms(
+            rigs, K_tan, z_coefs, log_depth_maps, conf, pts3d_ref, weight_tan=float(weight_tan),
+            tan_stride=int(tan_stride), optim_Z0=optim_Z0, dtype=jac.dtype, compute_gn=True,
+            normalize_tangents=bool(normalize_tangents))
+        z_prior = (H_z, g_z)
     J = jac.compute_jacobians(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d_std, pix2d_dep,
                               optim_K=optim_K, optim_Z=optim_Z, optim_Z0=optim_Z0, optim_P=optim_P,
                               optim_X=optim_X, is_depth_log=is_depth_log,
                               pix2d=pix2d if recompute_residuals else None)
     lin_kw = dict(weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err, huber_delta=huber_delta)
-    delta = jac.solve_delta(J, init_residuals, w_pts, lin_kw=lin_kw)
+    delta = jac.solve_delta(J, init_residuals, w_pts, z_prior=z_prior, lin_kw=lin_kw)
     delta_K, delta_P, delta_zcf, delta_pts = jac.unpack_delta_inplace(delta)
 
     update, new_loss, new_residuals = line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P,

@@ -171,14 +171,25 @@ class BAPlan:
         self._live = live
         return p
 
-    def linearize(self, params, opts, outputs=None, stream=None):
-        """Full single-GPU linearization; returns a SchurSystem."""
+    def linearize(self, params, opts, outputs=None, stream=None, z_prior=None):
+        """Full single-GPU linearization; returns a SchurSystem.  ``z_prior`` = (H_z, g_z), the
+        dense tangent prior's terms ([n_imgs, C, C], [n_imgs, C]), is added to the system before
+        its damping (solve_delta's z_prior, ba_solver.py:141-173)."""
         S, b, dA, pc, hm = outputs if outputs is not None else self.new_outputs()
         out = L.Outputs(S_vals=S.data_ptr(), b=b.data_ptr(), diagA=dA.data_ptr(), precond=pc.data_ptr(),
                         hpp_max=hm.data_ptr())
         ws = self.workspace()
         s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
-        L.call('b3r_linearize_schur', self._h, C.byref(params), C.byref(opts), ws, C.byref(out), s)
+        if z_prior is None:
+            L.call('b3r_linearize_schur', self._h, C.byref(params), C.byref(opts), ws, C.byref(out), s)
+        else:
+            Hz, gz = (t.to(device=self.device, dtype=torch.float64).contiguous() for t in z_prior)
+            assert Hz.shape == (self.n_imgs, self.C, self.C) and gz.shape == (self.n_imgs, self.C)
+            L.call('b3r_lin_points', self._h, C.byref(params), C.byref(opts), ws, C.byref(out), s)
+            L.call('b3r_lin_assemble', self._h, C.byref(params), C.byref(opts), ws, C.byref(out), s)
+            L.call('b3r_lin_add_zprior', self._h, Hz.data_ptr(), gz.data_ptr(), ws, C.byref(out), s)
+            L.call('b3r_lin_finalize', self._h, C.byref(opts), ws, C.byref(out), s)
+            self._live_prior = (Hz, gz)
         return SchurSystem(self, S, b, dA, pc, hm, ws, params, opts)
 
     def capture(self, params, opts, outputs=None):
@@ -216,18 +227,23 @@ class BAPlan:
         L.call(name, self._h, S_vals.data_ptr(), x.contiguous().data_ptr(), y.data_ptr(), s)
         return y
 
-    def pcg(self, S_vals, precond, b, tol=1e-6, maxiter=300):
-        """Solve S x = b on the device (b3r_pcg[_f64]): the reference's PCG iteration and
-        stopping rule, one cooperative kernel.  Returns (x, iterations, converged)."""
+    def pcg(self, S_vals, precond, b, tol=1e-6, maxiter=300, barrier_spin_limit=0, flags=0, raw=False):
+        """Solve S x = b on the device (b3r_pcg_ex): the reference's PCG iteration and
+        stopping rule, one cooperative kernel.  Returns (x, iterations, converged); raises if a
+        grid-barrier wait ran out (with ``raw``, returns (x, iterations, converged, error)
+        instead).  ``barrier_spin_limit`` bounds every barrier wait (0: the library's default)."""
         assert b.dtype in (torch.float32, torch.float64)
         b = b.contiguous()
         x = torch.empty_like(b)
         work = torch.empty(int(L.lib().b3r_pcg_work_bytes(self._h)) // 8 + 32, dtype=torch.float64, device=b.device)
         res = torch.zeros(4, dtype=torch.int32, device=b.device)
-        name = 'b3r_pcg_f64' if b.dtype == torch.float64 else 'b3r_pcg'
-        L.call(name, self._h, S_vals.data_ptr(), precond.contiguous().data_ptr(), b.data_ptr(), x.data_ptr(),
-               float(tol), int(maxiter), work.data_ptr(), res.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        dt = L.B3R_F64 if b.dtype == torch.float64 else L.B3R_F32
+        L.call('b3r_pcg_ex', self._h, S_vals.data_ptr(), precond.contiguous().data_ptr(), b.data_ptr(), x.data_ptr(),
+               dt, float(tol), int(maxiter), int(barrier_spin_limit), int(flags), work.data_ptr(), res.data_ptr(),
+               torch.cuda.current_stream().cuda_stream)
         it, conv, err = res[:3].tolist()
+        if raw:
+            return x, int(it), bool(conv), int(err)
         if err:
             raise L.B3RError('b3r_pcg: a grid barrier of the PCG kernel gave up')
         return x, int(it), bool(conv)

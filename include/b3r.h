@@ -277,7 +277,8 @@ int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
  * x0 = 0 with the Jacobi preconditioner precond (out->precond of the linearization),
  * stopping at the first iterate with ||r|| <= tol ||b|| (converged, returned), breaking on a
  * non-finite r.z, else returning the best-so-far iterate after maxiter iterations.  One
- * cooperative kernel runs the whole loop on `stream`.  `work` is a 256-byte aligned device
+ * cooperative kernel runs the whole loop on `stream`, in the pipelined form of the
+ * iteration (one grid-wide barrier per iteration; every barrier wait is bounded).  `work` is a 256-byte aligned device
  * buffer of b3r_pcg_work_bytes(plan) bytes; `result` is a device int[3] receiving
  * (iterations, converged, device error) -- read it after synchronising the stream.
  * b3r_pcg uses float vectors, b3r_pcg_f64 double vectors; S stays float either way.
@@ -287,6 +288,18 @@ int b3r_pcg(const b3r_plan* plan, const float* S_vals, const float* precond, con
             double tol, int maxiter, void* work, int* result, void* stream);
 int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond, const double* b, double* x,
                 double tol, int maxiter, void* work, int* result, void* stream);
+
+/* The same solve with the vector type given by dtype (B3R_F32 or B3R_F64; b and x of that
+ * type), and the limit of every grid-barrier wait inside the kernel: `barrier_spin_limit`
+ * polls of about 32 ns each (<= 0: the default of b3r_pcg, about half a second).  A wait
+ * that runs out makes every block leave the kernel at that barrier or the next, x is zeroed
+ * and result[2] = 1; the context stays usable.  flags: 0, or
+ * B3R_PCG_TEST_UNREACHABLE_BARRIER, a test of that failure path in which the first barrier
+ * waits for an arrival that no block makes. */
+#define B3R_PCG_TEST_UNREACHABLE_BARRIER 1
+int b3r_pcg_ex(const b3r_plan* plan, const float* S_vals, const float* precond, const void* b, void* x, int dtype,
+               double tol, int maxiter, int64_t barrier_spin_limit, int flags, void* work, int* result,
+               void* stream);
 
 /* The line search's reprojection score (the reference's reproj_score, inference/engine.py
  * :357-361, used by its step reject at :308-333): the mean of the floor(0.8 n) smallest
@@ -299,6 +312,46 @@ int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond,
 int64_t b3r_reproj_score_work_bytes(int64_t n_obs);
 int b3r_reproj_score(const float* residuals, int64_t n_obs, int64_t stride_obs, int64_t stride_comp, void* work,
                      float* score, void* stream);
+
+/* ===================================================================================
+ * Part 4 -- dense tangent prior on the depth coefficients
+ * =================================================================================== */
+
+/* One image's dense maps (device pointers): the log-depth channels (H, W, channels with
+ * `channel_stride` floats between pixels; the first C are used) and the reference pointmap
+ * in camera coordinates (H, W, 3), both row-major. */
+typedef struct {
+    const float* log_depth;
+    const float* pts3d_ref;
+    int32_t H, W, channel_stride, reserved;
+} b3r_dense_map;
+
+/* The reference's _dense_tangent_prior_terms (inference/engine.py:15-158) with
+ * confident_in_planar_regions (:161-179), for all images in one launch: per image, the
+ * tangents of the points of the combined log-depth exp(min(sum_c z_coefs[i,c] L_c, 80)) on the
+ * grid subsampled by `stride` (first sample at stride / 2) against those of the reference
+ * pointmap, weighted by the planarity confidence of the reference depth.  maps: DEVICE
+ * array [n_imgs]; cam_ids: device int32 [n_imgs] (infos[2]); K [n_cams,3,3]; z_coefs
+ * [n_imgs, C] (device).  x0_scale: device [n_imgs] factor applied to each reference
+ * pointmap (the median depth ratio the reference uses when normalize == 0), or NULL (1).
+ * cells_hint: about the largest subsampled grid (H' W'), a launch-size hint only.
+ * Outputs (device, double, overwritten): loss [1] = the prior's term of the objective;
+ * unless g_z == H_z == NULL, g_z [n_imgs, C] and H_z [n_imgs, C, C], with channel 0 zeroed
+ * when optim_Z0 == 0.  weight_tan <= 0 gives zeros, like the reference. */
+int b3r_tangent_prior(const b3r_dense_map* maps, int32_t n_imgs, int32_t cells_hint, const float* K,
+                      const int32_t* cam_ids, const float* z_coefs, int32_t C, const double* x0_scale,
+                      int32_t stride, double weight_tan, double eps, int32_t optim_Z0, int32_t normalize,
+                      double* loss, double* g_z, double* H_z, void* stream);
+
+/* Adds the prior's Gauss-Newton terms to an assembled system between b3r_lin_assemble and
+ * b3r_lin_finalize, as solve_delta adds z_prior (inference/ba_solver.py:141-173): H_z [n_imgs,
+ * C, C] to each image's depth-coefficient diagonal block of S and its diagonal to diag(A),
+ * g_z [n_imgs, C] to b (device, double).  An image whose depth coefficients are switched off
+ * (optim_Z = False) then carries the prior alone, adaptively damped like the reference's
+ * BlockDiagMat(H_z).  On a sharded problem call it on the solving rank only, after the
+ * reduce. */
+int b3r_lin_add_zprior(b3r_plan* plan, const double* H_z, const double* g_z, void* workspace,
+                       const b3r_outputs* out, void* stream);
 
 /* One pass of b3r_lin_points/b3r_lin_assemble on its own (profiling and custom
  * pipelines): B3R_PASS_PREP (per-image records), _POINTS (per-track Hpp, g_p), _FACTOR

@@ -37,6 +37,13 @@ def import_reference(cpu_ops):
     if cpu_ops:
         from oracle import ref_ops
         sys.modules['blast3r.extensions.cujac.ba_with_rigs_cuda_kernels'] = ref_ops.make_module()
+    else:
+        # the reference's CUDA ops as compiled from its source by oracle/build_ref.py (the
+        # build the GPU tests already load); the installed package's own build otherwise
+        from oracle import build_ref
+        mod = build_ref.load_built()
+        if mod is not None:
+            sys.modules['blast3r.extensions.cujac.ba_with_rigs_cuda_kernels'] = mod
     import blast3r.extensions.cujac  # noqa: F401
     import blast3r.inference.ba_solver as ba_solver
     import blast3r.inference.engine as engine

@@ -22,11 +22,12 @@ def _both(s, dtype, maxiter=300):
 
 
 def _check_close(s, xn, xs, itn, its, cn, cs, dist):
-    """Same stopping decision and iteration (within the run-dependent summation order), the
-    native iterate's true residual within the stopping tolerance (or, unconverged, close to
-    the stepwise one), and iterates within `dist`: two PCG runs that differ only in rounding
-    drift apart by up to cond(S) times their residuals."""
-    assert cn == cs and abs(itn - its) <= max(2, 0.05 * its), (itn, its, cn, cs)
+    """Same stopping decision and about the same iteration (the native kernel runs the
+    pipelined form of the iteration, whose rounding differs), the native iterate's true
+    residual within the stopping tolerance (or, unconverged, close to the stepwise one), and
+    iterates within `dist`: two PCG runs that differ only in rounding drift apart by up to
+    cond(S) times their residuals."""
+    assert cn == cs and abs(itn - its) <= max(2, 0.1 * its), (itn, its, cn, cs)
     b = s.b.double()
     rn = float((s.matvec(torch.from_numpy(xn).cuda()) - b).norm() / b.norm())
     rs = float((s.matvec(torch.from_numpy(xs).cuda()) - b).norm() / b.norm())
@@ -50,7 +51,9 @@ def test_native_pcg_equals_stepwise_f32(path):
     inp, opts, _ = load_golden(path)
     _, s = run_plan(inp, opts)
     (xn, itn, cn), (xs, its, cs) = _both(s, torch.float32)
-    assert cn == cs
+    # the native kernel iterates in double for float32 vectors too: it converges whenever the
+    # float32 step-by-step iteration does (and may where float32 stalls)
+    assert cn or not cs
     # float32 iterates drift with the rounding order: compare true (float64) residuals, and
     # the distance to the float64 solution loosely
     b = s.b.double()
@@ -77,3 +80,21 @@ def test_native_pcg_best_so_far_when_not_converged():
     (xn, itn, cn), (xs, its, cs) = _both(s, torch.float64, maxiter=3)
     assert not cn and not cs and itn == its
     assert rel_err(xn, xs) < 1e-9
+
+
+def test_pcg_barrier_wait_that_runs_out_returns_an_error():
+    """The failure path of the kernel's grid barrier, without a fault: with a short wait limit
+    and the test flag that makes the first barrier wait for an arrival no block makes, every
+    block leaves, x is zeroed and result[2] reports it; the context stays usable and the next
+    solve is normal."""
+    from blast3r_b200 import _lib as L
+    inp, opts, _ = load_golden(golden_files()[0])
+    _, s = run_plan(inp, opts)
+    b = s.b.double()
+    x, it, conv, err = s.plan.pcg(s.S_vals, s.precond, b, barrier_spin_limit=2000,
+                                  flags=L.PCG_TEST_UNREACHABLE_BARRIER, raw=True)
+    torch.cuda.synchronize()
+    assert err == 1 and not conv and float(x.abs().max()) == 0.0
+    x2, it2, conv2 = s.plan.pcg(s.S_vals, s.precond, b)
+    x3, it3, conv3 = s.plan.pcg(s.S_vals, s.precond, b, barrier_spin_limit=1 << 20)
+    assert conv2 and conv3 and it2 == it3 and torch.equal(x2, x3)   # deterministic reductions

@@ -233,5 +233,8 @@ def test_local_inputs_equal_global_inputs(cfg):
         dp = plan.backsub(p, lo, plan.workspace(), torch.full((plan.n_cam_params,), 1e-3, device='cuda'))
         torch.cuda.synchronize()
         res.append([x.clone() for x in outs[:3]] + [outs[4].clone(), dp])
-    for a, b in zip(*res):
-        assert torch.equal(a, b)
+    # the same arithmetic per observation; only the order of the float atomics differs
+    (S0, b0, d0, h0, p0), (S1, b1, d1, h1, p1) = res
+    assert torch.equal(h0, h1)
+    for a, b in ((S0, S1), (b0, b1), (d0, d1), (p0, p1)):
+        assert rel_err(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
