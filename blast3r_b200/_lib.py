@@ -56,7 +56,8 @@ class LinOpts(C.Structure):
 
 
 class Outputs(C.Structure):
-    _fields_ = [('S_vals', _vp), ('b', _vp), ('diagA', _vp), ('precond', _vp), ('hpp_max', _vp)]
+    _fields_ = [('S_vals', _vp), ('b', _vp), ('diagA', _vp), ('precond', _vp), ('hpp_max', _vp),
+                ('residuals', _vp), ('loss', _vp)]
 
 
 # name -> (restype, argtypes)
@@ -66,6 +67,9 @@ _SIGS = {
     'b3r_residuals_with_rigs': (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _i64, _vp, C.c_int, _vp,
                                           C.c_int, _vp, C.c_int, _vp, _i64, _vp, _vp, _vp, C.c_int,
                                           _f32, _f32, _f32, _f32, _f32, _vp, _vp]),
+    'b3r_residual_loss': (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _i64, _vp, C.c_int, _vp, C.c_int, _vp,
+                                    C.c_int, _vp, _i64, _vp, _vp, _vp, C.c_int, _f32, _f32, _f32, _f32, _vp, _vp,
+                                    _vp]),
     'b3r_jacobians_with_rigs': (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _i64, _vp, C.c_int, _vp,
                                           C.c_int, _vp, C.c_int, _vp, _i64, _vp, _vp, C.c_int,
                                           C.c_int, _vp, _vp, _vp, _vp]),

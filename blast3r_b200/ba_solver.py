@@ -114,7 +114,8 @@ class GaussNewtonSolver:
                        pix2d_std=pix2d_std, pix2d_dep=pix2d_dep, pix2d=pix2d)
         return Linearization(plan, tensors, flags)
 
-    def linearize(self, J, residuals=None, w_pts=None, clamp_w=(1e-6, 1e6), lin_kw=None, z_prior=None):
+    def linearize(self, J, residuals=None, w_pts=None, clamp_w=(1e-6, 1e6), lin_kw=None, z_prior=None,
+                  objective=False):
         """Run the fused linearization; returns the SchurSystem (S, b, diag A, preconditioner)."""
         t, f = J.tensors, J.flags
         kw = dict(lin_kw or {})
@@ -131,14 +132,16 @@ class GaussNewtonSolver:
         else:
             p = J.plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
                               t['pix2d_dep'], residuals=residuals, w_pts=w_pts)
-        J.system = J.plan.linearize(p, opts, z_prior=z_prior)
+        J.system = J.plan.linearize(p, opts, z_prior=z_prior, objective=objective)
         return J.system
 
     def solve_delta(self, J, residuals, w_pts, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
         """delta = [delta_c, delta_p] solving (J^T W J + damping) delta = J^T W r through the
         Schur complement (ba_solver.py:110-182); float32 like the reference."""
         assert residuals.shape == (self.n_kpts, 3)
-        assert w_pts.shape in ((self.n_kpts, 1), (self.n_kpts, 3))
+        # without the weights the linearization must recompute them in-kernel (pix2d given)
+        assert (w_pts is None and J.tensors['pix2d'] is not None) or w_pts.shape in ((self.n_kpts, 1),
+                                                                                   (self.n_kpts, 3))
         zp = None
         if z_prior is not None:
             H_z, g_z = z_prior
@@ -152,6 +155,20 @@ class GaussNewtonSolver:
                     raise TypeError('z_prior with a partial depth-coefficient mask is not supported')
                 zp = (H_z, g_z)
         s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw, z_prior=zp)
+        return self._solve(s)
+
+    def solve_with_objective(self, J, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
+        """solve_delta for a linearization that recomputes residuals in-kernel (compute_jacobians
+        given pix2d), which also returns the objective at the linearization point from the same
+        passes: (delta, loss, residuals) with loss the mean Huber error over the (n_obs, 3)
+        errors (0-d float32, what lm_step's objective computes, engine.py:263-281) and residuals
+        an (n_obs, 3) view."""
+        assert J.tensors['pix2d'] is not None, 'the objective needs in-kernel residuals (pix2d)'
+        s = self.linearize(J, None, None, clamp_w, lin_kw, z_prior=z_prior, objective=True)
+        loss = (s.loss_sum[0] / max(3 * self.n_kpts, 1)).to(torch.float32)
+        return self._solve(s), loss, s.residuals.transpose(0, 1)
+
+    def _solve(self, s):
         dt = torch.float64 if self.dtype == torch.float64 else torch.float32
         # the reference's PCG (ba_solver.py:202, 1197-1238) as one device kernel on the explicit S
         delta_c, niter, conv = s.plan.pcg(s.S_vals, s.precond, s.b.to(dt), tol=1e-6, maxiter=300)

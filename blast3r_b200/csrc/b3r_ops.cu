@@ -3,6 +3,7 @@
 // so the reference's Python solver can bind this library in place of its extension.
 // Layouts, argument meaning and numerics follow the reference; outputs are written in
 // full (the reference zero-fills them with torch::zeros before its kernels run).
+#include <algorithm>
 #include "b3r_common.cuh"
 #include "b3r_status.h"
 
@@ -44,6 +45,48 @@ __global__ void k_residuals(const int* __restrict__ infos, int n_imgs, const flo
       out[(3 + i) * n_obs + idx] = L.err[i];
       out[(6 + i) * n_obs + idx] = L.w[i];
     }
+  }
+}
+
+// The objective of lm_step (engine.py:263-281) without its [9, n_obs] buffer: every
+// observation's residual and Huber error as the residual kernel forms them; the errors
+// summed in double (one atomic per block), the residuals written component-major when
+// asked for.
+constexpr int kLossThreads = 256;
+__global__ void __launch_bounds__(kLossThreads) k_residual_loss(
+    const int* __restrict__ infos, int n_imgs, const float* __restrict__ K, const float* __restrict__ P_rig2c,
+    int64_t P_stride, const float* __restrict__ P_w2rig, const float* __restrict__ z_coefs, int C,
+    const float* __restrict__ pts3d, const int* __restrict__ pids, int64_t n_obs, const float* __restrict__ pix2d,
+    const float* __restrict__ pix2d_std, const float* __restrict__ pix2d_dep, LinOpts o, double* __restrict__ loss,
+    float* __restrict__ res) {
+  __shared__ double red[kLossThreads / 32];
+  double acc = 0.0;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n_obs;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int img = search_image(infos, n_imgs, idx);
+    const int node = infos[n_imgs + img];
+    const int cam = infos[2 * n_imgs + img];
+    const int pt = pids[idx];
+    const Cam c = load_cam_ref<float>(K, P_rig2c, P_stride, P_w2rig, cam, node);
+    const float X[3] = {pts3d[3 * (int64_t)pt], pts3d[3 * (int64_t)pt + 1], pts3d[3 * (int64_t)pt + 2]};
+    ObsLin L;
+    linearize_obs<float, true, false, 0>(c, X, pix2d[2 * idx], pix2d[2 * idx + 1], pix2d_std[2 * idx],
+                                         pix2d_std[2 * idx + 1], pix2d_dep + idx * C,
+                                         z_coefs + (int64_t)img * C, C, o, L);
+    if (res) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) res[i * n_obs + idx] = L.r[i];
+    }
+    acc += (double)L.err[0] + (double)L.err[1] + (double)L.err[2];
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kLossThreads / 32; ++w) t += red[w];
+    atomicAdd(loss, t);
   }
 }
 
@@ -193,6 +236,27 @@ extern "C" int b3r_residuals_with_rigs(const int32_t* infos, int n_imgs, const f
       infos, n_imgs, K, P_rig2c, P_rig2c_stride, P_w2rig, z_coefs, C, pts3d, pids, n_obs, pix2d,
       pix2d_std, pix2d_dep, o, out);
   return check_launch("b3r_residuals_with_rigs");
+}
+
+extern "C" int b3r_residual_loss(const int32_t* infos, int n_imgs, const float* K, int n_cams, const float* P_rig2c,
+                                 int64_t P_rig2c_stride, const float* P_w2rig, int n_nodes, const float* z_coefs,
+                                 int C, const float* pts3d, int n_tracks, const int32_t* pids, int64_t n_obs,
+                                 const float* pix2d, const float* pix2d_std, const float* pix2d_dep,
+                                 int is_depth_log, float weight_z, float pnorm, float max_pix_err,
+                                 float huber_delta, double* loss_sum, float* residuals, void* stream) {
+  B3R_TRY(check_common(infos, n_imgs, K, n_cams, P_rig2c, P_rig2c_stride, P_w2rig, n_nodes, z_coefs,
+                       C, pts3d, n_tracks, pids, n_obs));
+  B3R_REQUIRE(pnorm > 0.f && pnorm <= 2.f, "pnorm must be in ]0,2] for a loss");
+  B3R_REQUIRE(loss_sum != nullptr, "NULL loss_sum");
+  B3R_REQUIRE(n_obs == 0 || (pix2d && pix2d_std && pix2d_dep), "NULL observation pointer");
+  cudaStream_t s = as_stream(stream);
+  B3R_TRY(check_cuda(cudaMemsetAsync(loss_sum, 0, sizeof(double), s), "b3r_residual_loss memset"));
+  if (n_obs == 0) return B3R_OK;
+  LinOpts o = make_opts(is_depth_log, weight_z, pnorm, max_pix_err, huber_delta, 1e-16f);
+  const int g = (int)std::min<int64_t>(grid_for(n_obs, kLossThreads), 148 * 8);
+  k_residual_loss<<<g, kLossThreads, 0, s>>>(infos, n_imgs, K, P_rig2c, P_rig2c_stride, P_w2rig, z_coefs, C, pts3d,
+                                             pids, n_obs, pix2d, pix2d_std, pix2d_dep, o, loss_sum, residuals);
+  return check_launch("b3r_residual_loss");
 }
 
 extern "C" int b3r_jacobians_with_rigs(const int32_t* infos, int n_imgs, const float* K, int n_cams,

@@ -102,7 +102,7 @@ struct PlanBuild {
   // pattern
   std::vector<int> row_ptr, col_idx, val_off;
   std::vector<int> seg_dst, seg_mode, img_dst, sdiag_pos, blk_row, trk_ptr, img_zdiag, img_zsc;
-  std::vector<int4> t_idx, c1_idx;
+  std::vector<int4> t_idx, c1_idx, rest_idx;
   std::vector<int> sym_ptr, sym_ent;
   std::vector<int4> mv_task, mv_row, mv_ent;
   std::vector<int4> pcg_grp;
@@ -256,7 +256,11 @@ static int build_tracks(PlanBuild& B) {
   int last_img = -1, in_chunk = 0;
   for (int64_t o = 0; o < d.n_obs; ++o) {
     const int t = d.pids[o];
-    if (!B.owned[t] || !B.obs_live[o]) continue;
+    if (!B.owned[t]) continue;
+    if (!B.obs_live[o]) {                  // evaluated for the objective only
+      B.rest_idx.push_back(make_int4((int)o, B.img_of[o], t, 0));
+      continue;
+    }
     const int i = B.img_of[o];
     if (i != last_img || in_chunk == kDiagChunk) {
       B.c1_chunk.push_back((int)B.c1_obs.size());
@@ -741,6 +745,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
       B.t_idx[k].w = own[B.t_idx[k].w];
     }
     for (auto& x : B.c1_idx) x.x = own[x.x];
+    for (auto& x : B.rest_idx) x.x = own[x.x];
     d.first_in = desc->n_obs > 0 ? own[0] : -1;
     d.n_in = (int64_t)P->in_obs.size();
   }
@@ -754,6 +759,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add_mut<float>((size_t)d.n_loc * desc->C, &d.t_dep);
   A.add(B.c1_obs, &d.c1_obs); A.add(B.c1_k, &d.c1_k); A.add(B.c1_pid, &d.c1_pid); A.add(B.c1_chunk, &d.c1_chunk);
   A.add(B.c1_img, &d.c1_img);
+  A.add(B.rest_idx, &d.rest_idx);
+  d.n_rest = (int64_t)B.rest_idx.size();
   A.add(B.seg_dst, &d.seg_dst); A.add(B.seg_mode, &d.seg_mode);
   A.add(B.pairs, &d.pairs); A.add(B.task_pb, &d.task_pb); A.add(B.task_pe, &d.task_pe);
   A.add(B.task_seg, &d.task_seg);
@@ -781,7 +788,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   P->ws_trec = align256(P->ws_img + sizeof(float) * kImgRecFloats * (size_t)d.n_imgs);
   P->ws_rec = align256(P->ws_trec + sizeof(float) * 24 * (size_t)d.nT_loc);
   P->ws_rw = align256(P->ws_rec + sizeof(float) * (size_t)d.R * (size_t)d.n_c1);
-  P->ws_misc = align256(P->ws_rw + sizeof(float) * 6 * (size_t)d.n_loc);
+  P->ws_loss = align256(P->ws_rw + sizeof(float) * 6 * (size_t)d.n_loc);
+  P->ws_misc = align256(P->ws_loss + sizeof(double) * ((size_t)d.n_c1_chunks + kRestBlocks));
   const size_t ws_total = P->ws_misc + 256;
 
   P->pat.row_ptr = std::move(B.row_ptr); P->pat.col_idx = std::move(B.col_idx);

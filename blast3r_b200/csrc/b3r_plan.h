@@ -23,6 +23,7 @@ constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal ch
 constexpr int kPointTask = 32;     // max observations per point task (one warp)
 constexpr int kImgRecFloats = 32;  // floats per per-image camera record
 constexpr int kMvCols = 256;       // max panel columns per matvec task (8 per lane)
+constexpr int kRestBlocks = 64;     // blocks of the objective pass over observations without an image-major entry
 constexpr int kPcgSlots = 1024;    // per-task partial row sums one PCG row group keeps in shared memory
 constexpr int kPcgBlocksPerSm = 3; // resident PCG blocks per SM the row groups are sized for
 
@@ -69,6 +70,10 @@ struct DevPlan {
   const int* c1_pid;      // [n_c1] track id (point index) of the observation
   int n_c1_chunks;
   const int* c1_chunk;    // [n_c1_chunks+1]
+  // this rank's observations in images without an active block (no image-major entry): only
+  // their residuals and losses are evaluated
+  int64_t n_rest;
+  const int4* rest_idx;   // [n_rest] (input row, image, track id, 0)
   const int* c1_img;      // [n_c1_chunks]
 
   // segments and their pair lists
@@ -143,7 +148,7 @@ struct b3r_plan {
   // workspace layout (byte offsets): image records | track records (24 floats: Hpp, g_p,
   // then the Cholesky factor in reciprocal form and L^-1 g_p) | elimination records (one
   // per image-major slot e) | staged r/w | misc scalars
-  size_t ws_img = 0, ws_trec = 0, ws_rec = 0, ws_rw = 0, ws_misc = 0;
+  size_t ws_img = 0, ws_trec = 0, ws_rec = 0, ws_rw = 0, ws_loss = 0, ws_misc = 0;
   int64_t n_pairs_total = 0;
   std::vector<int> in_obs;   // global observation of each input row (empty: the identity)
   bool staged = false;

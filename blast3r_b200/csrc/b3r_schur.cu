@@ -43,6 +43,8 @@ struct Ctx {
   float* rec;         // [n_loc*R]
   float* t_rw;        // [6][n_loc] staged residual (0..2) and weight (3..5), general path
   float* misc;        // [64]: 4..6 per-type max |diag A|
+  float* res_out;     // [3][n_in] residual outputs, or NULL
+  double* loss_part;  // [n_c1_chunks + kRestBlocks] per-block Huber-error sums, or NULL
   float* hpp_max;     // [1] max |diag(Hpp)| (caller-visible, all-reduced across ranks)
   int no_grad_f_from_rz, optim_Z0, optim_Z_1st_cam;
   float dampen;
@@ -274,13 +276,19 @@ __device__ __forceinline__ void load_obs_in(const Ctx& c, int e, int ee, ObsIn<C
 // Linearize a prefetched image-major observation of image img.
 template <int CT>
 __device__ __forceinline__ void view_in(const Ctx& c, const ObsIn<CT>& in, int img, const Cam& cam, const float* zc,
-                                        ObsView<CT>& V) {
+                                        ObsView<CT>& V, float& esum) {
   const int64_t o = in.ix.x;
   ObsLin L;
   float r0, r1, r2, w0, w1, w2;
+  esum = 0.f;
   if (c.pix2d) {
     linearize_obs<float, true, true, CT>(cam, in.X, in.px, in.py, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
+    if (c.res_out) {                              // the objective's residuals, at the input row
+      const int64_t n = c.d.n_in;
+      c.res_out[o] = r0; c.res_out[n + o] = r1; c.res_out[2 * n + o] = r2;
+    }
+    esum = L.err[0] + L.err[1] + L.err[2];
   } else {
     linearize_obs<float, false, true, CT>(cam, in.X, 0.f, 0.f, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = c.res[o * c.rs_n]; r1 = c.res[o * c.rs_n + c.rs_c]; r2 = c.res[o * c.rs_n + 2 * c.rs_c];
@@ -458,6 +466,65 @@ __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   t4[5] = make_float4(z[2], (float)dd[0], (float)dd[1], (float)dd[2]);   // floats 20..23
 }
 
+__device__ __forceinline__ double warp_sum_dbl(double v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+
+// The objective over this rank's observations in images without an active block (they have
+// no image-major entry): residuals and Huber errors only.
+template <int CT>
+__global__ void __launch_bounds__(256) k_rest(Ctx c) {
+  __shared__ double red[8];
+  float acc = 0.f;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < c.d.n_rest;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const int4 ix = __ldg(c.d.rest_idx + j);      // input row, image, track id
+    const int64_t o = ix.x, pid = ix.z;
+    const Cam cam = load_cam(c.img_rec + (int64_t)ix.y * kImgRec);
+    const float X[3] = {__ldg(c.pts3d + 3 * pid), __ldg(c.pts3d + 3 * pid + 1), __ldg(c.pts3d + 3 * pid + 2)};
+    float dep[CT], zc[CT];
+#pragma unroll
+    for (int ch = 0; ch < CT; ++ch) {
+      dep[ch] = __ldg(c.pix2d_dep + o * CT + ch);
+      zc[ch] = __ldg(c.z_coefs + (int64_t)ix.y * CT + ch);
+    }
+    const float2 q = __ldg(reinterpret_cast<const float2*>(c.pix2d) + o);
+    const float2 sd = __ldg(reinterpret_cast<const float2*>(c.pix2d_std) + o);
+    ObsLin L;
+    linearize_obs<float, true, false, CT>(cam, X, q.x, q.y, sd.x, sd.y, dep, zc, CT, c.o, L);
+    if (c.res_out) {
+      const int64_t n = c.d.n_in;
+      c.res_out[o] = L.r[0]; c.res_out[n + o] = L.r[1]; c.res_out[2 * n + o] = L.r[2];
+    }
+    acc += L.err[0] + L.err[1] + L.err[2];
+  }
+  const double t = warp_sum_dbl((double)acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+  __syncthreads();
+  if (threadIdx.x == 0 && c.loss_part) {
+    double u = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) u += red[w];
+    c.loss_part[c.d.n_c1_chunks + blockIdx.x] = u;
+  }
+}
+
+// The objective's sum of Huber errors from the per-block partial sums, in a fixed order.
+__global__ void __launch_bounds__(256) k_loss_sum(const double* __restrict__ part, int n, double* __restrict__ loss) {
+  __shared__ double red[8];
+  double acc = 0.0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) acc += part[j];
+  acc = warp_sum_dbl(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    *loss = t;
+  }
+}
+
 // ------------------------------------------------------------------------------------
 // pass "diag": image-major per-observation terms
 // ------------------------------------------------------------------------------------
@@ -596,13 +663,16 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
   for (int j = 0; j < NGL; ++j) run[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   ObsIn<CT> nxt;
   load_obs_in<CT>(c, eb + warp * kWarp + lane, ee, nxt);
+  float err_acc = 0.f;
   for (int base = eb + warp * kWarp; base < ee; base += NW * kWarp) {
     const int e = base + lane;
     const ObsIn<CT> cur = nxt;
     if (base + NW * kWarp < ee) load_obs_in<CT>(c, e + NW * kWarp, ee, nxt);   // next batch, warp-uniform
     if (e < ee) {
       ObsView<CT> V;
-      view_in<CT>(c, cur, img, cam, zc, V);
+      float es;
+      view_in<CT>(c, cur, img, cam, zc, V, es);
+      err_acc += es;
       diag_terms<CT>(c, V, cur.ix.y >= 0, e, cur.tf0, cur.tf1, cur.tf2, rw + lane * RS);
     } else {
       for (int v = 0; v < Lay::N; ++v) rw[lane * RS + v] = 0.f;
@@ -629,7 +699,18 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     const int g = lane + 32 * j;
     if (g < NG) *reinterpret_cast<float4*>(rw + 4 * g) = run[j];
   }
+  __shared__ double esm[NW];
+  if (c.loss_part) {                              // the chunk's Huber-error sum (no atomics)
+    const double t = warp_sum_dbl((double)err_acc);
+    if (lane == 0) esm[warp] = t;
+  }
   __syncthreads();
+  if (c.loss_part && threadIdx.x == 0) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) t += esm[w];
+    c.loss_part[chunk] = t;
+  }
   const int* dst = c.d.img_dst + 6 * img;
   const int* sc = c.d.img_sc + 3 * img;
   for (int e = threadIdx.x; e < Lay::E; e += kDiagThreads) {
@@ -1023,6 +1104,7 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
   float acc[NV];
 #pragma unroll
   for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+  float err_acc = 0.f;
   ObsIn<CT> nxt;
   load_obs_in<CT>(c, eb + threadIdx.x, ee, nxt);
   for (int base = eb; base < ee; base += kDiagZThreads) {
@@ -1031,7 +1113,9 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
     if (base + kDiagZThreads < ee) load_obs_in<CT>(c, e + kDiagZThreads, ee, nxt);   // CTA-uniform
     if (e >= ee) continue;
     ObsView<CT> V;
-    view_in<CT>(c, cur, img, cam, zc, V);
+    float es;
+    view_in<CT>(c, cur, img, cam, zc, V, es);
+    err_acc += es;
     const float zw = V.Jcw[26];
     const float d = zw * zw;
     float a = d, g = zw * V.sWr[2];
@@ -1068,7 +1152,18 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
     const float t = warp_sum(acc[v]);
     if (lane == 0) red[warp][v] = t;
   }
+  __shared__ double esm[NW];
+  if (c.loss_part) {                              // the chunk's Huber-error sum (no atomics)
+    const double t = warp_sum_dbl((double)err_acc);
+    if (lane == 0) esm[warp] = t;
+  }
   __syncthreads();
+  if (c.loss_part && threadIdx.x == 0) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) t += esm[w];
+    c.loss_part[chunk] = t;
+  }
   const int dzz = c.d.img_dst[6 * img + 5], sz = c.d.img_sc[3 * img + 2];
   for (int e = threadIdx.x; e < CT * CT + 2 * CT; e += kDiagZThreads) {
     int v;
@@ -1542,12 +1637,29 @@ extern "C" int b3r_lin_assemble(b3r_plan* plan, const b3r_params* params, const 
   B3R_TRY(check_cuda(cudaMemsetAsync(out->b, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset b"));
   B3R_TRY(check_cuda(cudaMemsetAsync(out->diagA, 0, sizeof(float) * (size_t)c.d.n_cam_params, s), "memset diagA"));
   B3R_TRY(check_cuda(cudaMemsetAsync(c.misc + 8, 0, sizeof(float), s), "memset prior flag"));
+  if (out->residuals || out->loss) {
+    B3R_REQUIRE(params->pix2d, "residual and loss outputs need pix2d (in-kernel residuals)");
+    c.res_out = out->residuals;
+    c.loss_part = out->loss ? reinterpret_cast<double*>(reinterpret_cast<char*>(workspace) + plan->ws_loss) : nullptr;
+  }
   switch (c.d.C) {
-#define X(CC) case CC: return launch_assemble<CC>(c, out->S_vals, out->b, out->diagA, s);
+#define X(CC)                                                                                    \
+    case CC:                                                                                     \
+      B3R_TRY(launch_assemble<CC>(c, out->S_vals, out->b, out->diagA, s));                       \
+      if (c.res_out || c.loss_part) {                                                            \
+        k_rest<CC><<<kRestBlocks, 256, 0, s>>>(c);                                               \
+        B3R_TRY(check_launch("objective of the remaining observations"));                        \
+      }                                                                                          \
+      break;
     B3R_FOR_EACH_C(X)
 #undef X
     default: return fail(B3R_E_UNSUPPORTED, "no kernels compiled for C=%d depth channels", c.d.C);
   }
+  if (c.loss_part) {
+    k_loss_sum<<<1, 256, 0, s>>>(c.loss_part, c.d.n_c1_chunks + kRestBlocks, out->loss);
+    B3R_TRY(check_launch("loss sum"));
+  }
+  return B3R_OK;
 }
 
 extern "C" int b3r_lin_pass(b3r_plan* plan, const b3r_params* params, const b3r_lin_opts* opts,

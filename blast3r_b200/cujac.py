@@ -76,6 +76,26 @@ def residuals_with_rigs(infos, K, P_rig2c, P_w2rig, z_coefs, pts3d, pids, pix2d,
     return out.transpose(0, 1)
 
 
+def residual_loss(infos, K, P_rig2c, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep, is_depth_log,
+                  weight_z=1.0, pnorm=1.0, max_pix_err=100.0, huber_delta=0.5, residuals=True):
+    """The objective of ``lm_step`` in one pass (b3r_residual_loss): (loss, residuals) with loss =
+    the mean Huber error (the reference's ``err.mean()`` over the (n_obs, 3) errors, a 0-d float32
+    tensor) and residuals the (n_obs, 3) residuals (a transposed view of a [3, n_obs] buffer), or
+    None when ``residuals`` is False."""
+    n_imgs, n_obs, C = _check_inputs(infos, K, P_rig2c, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std,
+                                     pix2d_dep)
+    dev = pix2d.device
+    loss = torch.empty(1, dtype=torch.float64, device=dev)
+    res = torch.empty((3, n_obs), dtype=torch.float32, device=dev) if residuals else None
+    L.call('b3r_residual_loss', infos.data_ptr(), n_imgs, K.data_ptr(), len(K), P_rig2c.data_ptr(),
+           P_rig2c.stride(0), P_w2rig.data_ptr(), len(P_w2rig), z_coefs.data_ptr(), C, pts3d.data_ptr(),
+           len(pts3d), pids.data_ptr(), n_obs, pix2d.data_ptr(), pix2d_std.data_ptr(), pix2d_dep.data_ptr(),
+           int(bool(is_depth_log)), float(weight_z), float(pnorm), float(max_pix_err), float(huber_delta),
+           loss.data_ptr(), res.data_ptr() if res is not None else None, _stream())
+    mean = (loss[0] / max(3 * n_obs, 1)).to(torch.float32)
+    return mean, (res.transpose(0, 1) if res is not None else None)
+
+
 def jacobians_with_rigs(infos, K, P_rig2c, P_w2rig, z_coefs, pts3d, pids, pix2d_std, pix2d_dep,
                         is_depth_log, float64=False):
     """[J_cam (n,3,8), J_zcf (n,1,C), J_pts (n,3,3)] (``sfm_jacobian_rigs.cu:1105-1148``)."""

@@ -98,16 +98,16 @@ def sharded_lm_step(sharded, rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2c
     same parameters.  The plan must enable whole parameter types (bool optim flags, the
     reference's default), not masks.  Returns (update, BA_Status) like ``engine.lm_step``.
     """
-    from .cujac import residuals_with_rigs as residual_func
+    from .cujac import residual_loss
     from .engine import BA_Status, line_search
     from .plan import BAPlan
     plan = sharded.plan
     is_log = depth_mode == 'log'
 
     def objective(K, P_w2rig, pts3d, z_coefs):
-        res, err, w = residual_func(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep,
-                                    is_log, weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
-        return err.mean(), res, w
+        loss, res = residual_loss(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep,
+                                  is_log, weight_z, pnorm, clip_pix_err, huber_delta)
+        return loss, res, None
 
     init_loss, init_residuals, _ = objective(K, P_w2rig, pts3d, z_coefs)
     lo = BAPlan.lin_opts(is_depth_log=is_log, weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err,

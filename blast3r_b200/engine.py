@@ -15,7 +15,7 @@ import torch
 
 from . import _lib as L
 from .ba_solver import GaussNewtonSolver
-from .cujac import exp_se3, residuals_with_rigs as residual_func
+from .cujac import exp_se3, residual_loss, residuals_with_rigs as residual_func
 from .prior import dense_tangent_prior_terms
 
 BA_Status = namedtuple('BA_Status', 'init_loss, init_residuals, new_loss, new_residuals')
@@ -141,11 +141,19 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
     # the prior treats the intrinsics as constant within a step (engine.py:258-260)
     K_tan = K.detach()
 
-    def objective(K, P_w2rig, pts3d, z_coefs):
-        residuals_, err_pts_, w_pts_ = residual_func(
-            rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep, is_depth_log,
-            weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
-        loss = err_pts_.mean()
+    def objective(K, P_w2rig, pts3d, z_coefs, need_w=False):
+        # the residual op's (n, 9) output is needed only for the IRLS weights that a
+        # linearization without in-kernel recomputation reads; otherwise one fused pass gives
+        # the loss and the residuals the line search scores (b3r_residual_loss)
+        if need_w:
+            residuals_, err_pts_, w_pts_ = residual_func(
+                rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std, pix2d_dep, is_depth_log,
+                weight_z, pnorm, clip_pix_err, huber_delta).view(-1, 3, 3).unbind(dim=1)
+            loss = err_pts_.mean()
+        else:
+            loss, residuals_ = residual_loss(rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d, pix2d_std,
+                                             pix2d_dep, is_depth_log, weight_z, pnorm, clip_pix_err, huber_delta)
+            w_pts_ = None
         if weight_tan > 0:
             tan_loss, _, _ = dense_tangent_prior_terms(
                 rigs, K_tan, z_coefs, log_depth_maps, conf, pts3d_ref, weight_tan=float(weight_tan),
@@ -154,11 +162,10 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
             loss = loss + tan_loss
         return loss, residuals_, w_pts_
 
-    init_loss, init_residuals, w_pts = objective(K, P_w2rig, pts3d, z_coefs)
     jac = GaussNewtonSolver(n_cams, n_nodes, n_imgs, n_tracks, pts3d.device, dampen=dampen, **ba_options)
-    z_prior = None
+    z_prior = tan_loss0 = None
     if weight_tan > 0:                 # adds only to the depth-coefficient normal equations
-        _, g_z, H_z = dense_tangent_prior_terms(
+        tan_loss0, g_z, H_z = dense_tangent_prior_terms(
             rigs, K_tan, z_coefs, log_depth_maps, conf, pts3d_ref, weight_tan=float(weight_tan),
             tan_stride=int(tan_stride), optim_Z0=optim_Z0, dtype=jac.dtype, compute_gn=True,
             normalize_tangents=bool(normalize_tangents))
@@ -168,7 +175,15 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
                               optim_X=optim_X, is_depth_log=is_depth_log,
                               pix2d=pix2d if recompute_residuals else None)
     lin_kw = dict(weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err, huber_delta=huber_delta)
-    delta = jac.solve_delta(J, init_residuals, w_pts, z_prior=z_prior, lin_kw=lin_kw)
+    if recompute_residuals:
+        # the objective at the current parameters comes out of the linearization's own passes
+        # (the same residuals and Huber errors the residual op computes)
+        delta, init_loss, init_residuals = jac.solve_with_objective(J, z_prior=z_prior, lin_kw=lin_kw)
+        if tan_loss0 is not None:
+            init_loss = init_loss + tan_loss0.to(init_loss.dtype)
+    else:
+        init_loss, init_residuals, w_pts = objective(K, P_w2rig, pts3d, z_coefs, need_w=True)
+        delta = jac.solve_delta(J, init_residuals, w_pts, z_prior=z_prior, lin_kw=lin_kw)
     delta_K, delta_P, delta_zcf, delta_pts = jac.unpack_delta_inplace(delta)
 
     update, new_loss, new_residuals = line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P,

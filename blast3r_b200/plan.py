@@ -33,6 +33,7 @@ class SchurSystem:
     def __init__(self, plan, S_vals, b, diagA, precond, hpp_max, workspace, params, opts):
         self.plan, self.S_vals, self.b, self.diagA, self.precond = plan, S_vals, b, diagA, precond
         self.hpp_max, self.workspace, self.params, self.opts = hpp_max, workspace, params, opts
+        self.residuals = self.loss_sum = None
 
     def matvec(self, x):
         """y = S x (float32 or float64 x)."""
@@ -171,13 +172,21 @@ class BAPlan:
         self._live = live
         return p
 
-    def linearize(self, params, opts, outputs=None, stream=None, z_prior=None):
+    def linearize(self, params, opts, outputs=None, stream=None, z_prior=None, objective=False):
         """Full single-GPU linearization; returns a SchurSystem.  ``z_prior`` = (H_z, g_z), the
         dense tangent prior's terms ([n_imgs, C, C], [n_imgs, C]), is added to the system before
-        its damping (solve_delta's z_prior, ba_solver.py:141-173)."""
+        its damping (solve_delta's z_prior, ba_solver.py:141-173).  With ``objective`` the
+        system also carries the objective at the linearization point, evaluated by the same
+        passes: ``residuals`` [3, n_obs_input] and ``loss_sum`` (double, the sum of the Huber
+        errors)."""
         S, b, dA, pc, hm = outputs if outputs is not None else self.new_outputs()
+        res = loss = None
+        if objective:
+            res = torch.empty((3, int(self.info.n_obs_input)), dtype=torch.float32, device=self.device)
+            loss = torch.empty(1, dtype=torch.float64, device=self.device)
         out = L.Outputs(S_vals=S.data_ptr(), b=b.data_ptr(), diagA=dA.data_ptr(), precond=pc.data_ptr(),
-                        hpp_max=hm.data_ptr())
+                        hpp_max=hm.data_ptr(), residuals=res.data_ptr() if res is not None else None,
+                        loss=loss.data_ptr() if loss is not None else None)
         ws = self.workspace()
         s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
         if z_prior is None:
@@ -190,7 +199,9 @@ class BAPlan:
             L.call('b3r_lin_add_zprior', self._h, Hz.data_ptr(), gz.data_ptr(), ws, C.byref(out), s)
             L.call('b3r_lin_finalize', self._h, C.byref(opts), ws, C.byref(out), s)
             self._live_prior = (Hz, gz)
-        return SchurSystem(self, S, b, dA, pc, hm, ws, params, opts)
+        sysm = SchurSystem(self, S, b, dA, pc, hm, ws, params, opts)
+        sysm.residuals, sysm.loss_sum = res, loss
+        return sysm
 
     def capture(self, params, opts, outputs=None):
         """CUDA graph of one full linearization on fixed buffers (the tensors `params` points

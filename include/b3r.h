@@ -65,6 +65,21 @@ int b3r_residuals_with_rigs(const int32_t* infos, int n_imgs, const float* K, in
                             float weight_z, float pnorm, float max_pix_err, float huber_delta,
                             float w_pts_nul, float* out, void* stream);
 
+/* The objective of lm_step (inference/engine.py:263-281: the residual op's Huber errors,
+ * summed) in one pass, without the [9, n_obs] buffer: loss_sum (device double [1]) = the sum
+ * over observations and components of the Huber error (the reference's loss is
+ * loss_sum / (3 n_obs)); residuals (device float [3, n_obs], or NULL) receives rows 0..2 of
+ * b3r_residuals_with_rigs (the residuals the line search scores).  Same inputs and numerics as
+ * b3r_residuals_with_rigs; pnorm in (0, 2]; the zero-weight value of clipped residuals does not
+ * enter the loss.  No counterpart among the reference's native ops: it fuses its residual op
+ * with the torch reduction that follows it. */
+int b3r_residual_loss(const int32_t* infos, int n_imgs, const float* K, int n_cams, const float* P_rig2c,
+                      int64_t P_rig2c_stride, const float* P_w2rig, int n_nodes, const float* z_coefs, int C,
+                      const float* pts3d, int n_tracks, const int32_t* pids, int64_t n_obs, const float* pix2d,
+                      const float* pix2d_std, const float* pix2d_dep, int is_depth_log, float weight_z,
+                      float pnorm, float max_pix_err, float huber_delta, double* loss_sum, float* residuals,
+                      void* stream);
+
 /* Explicit Jacobians per observation.
  * Replaces jacobians_with_rigs (sfm_jacobian_rigs.cu:1105-1148, kernel :323-509).
  * J_cam [n_obs,3,8] (d/dfx, d/dfy, d/dtau x6), J_zcf [n_obs,1,C] (depth row only),
@@ -233,6 +248,13 @@ typedef struct {
     float* precond;    /* [n_cam_params]  max(diag(A) + damping, 1e-12), or NULL           */
     float* hpp_max;    /* [1]             max |diag(Hpp)| over this rank's tracks (NULL:
                           kept in the workspace; sharded callers pass it to all-reduce it) */
+    float* residuals;  /* [3, n_obs_input] or NULL: the residuals of this plan's observations
+                          (rows x, y, depth, at each observation's input row; others untouched),
+                          as b3r_residuals_with_rigs computes them                            */
+    double* loss;      /* [1] or NULL: the sum of their Huber errors (the objective's numerator;
+                          a partial sum on each rank of a sharded problem).  Both need
+                          params->pix2d (in-kernel residuals) and are written by
+                          b3r_lin_assemble                                                    */
 } b3r_outputs;
 
 /* One full linearization on one GPU: b3r_lin_points, b3r_lin_assemble and

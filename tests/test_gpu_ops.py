@@ -121,3 +121,21 @@ def test_fused_einsum(K, I, J):
     right = torch.randn(500, K, J, generator=g, dtype=torch.float64)
     got = cujac.fused_einsum_bki_bkj(left.cuda(), right.cuda()).cpu()
     assert rel_err(got.numpy(), torch.einsum('bki,bkj->bij', left, right).numpy()) < 1e-12
+
+
+@pytest.mark.parametrize('cfg', [0, 3])
+def test_residual_loss_equals_residual_op_mean(cfg):
+    """b3r_residual_loss: the objective lm_step forms from the residual op (err.mean()) and
+    the residuals the line search scores, in one pass."""
+    from blast3r_b200.synthetic import make_scene
+    sc = make_scene(cfg)
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in sc.lm_inputs().items()}
+    o = sc.options
+    args = (t['rigs'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pids'], t['pix2d'],
+            t['pix2d_std'], t['pix2d_dep'], True, o['weight_z'], o['pnorm'], o['clip_pix_err'], o['huber_delta'])
+    full = cujac.residuals_with_rigs(*args)
+    res, err, _ = full.view(-1, 3, 3).unbind(dim=1)
+    loss, r2 = cujac.residual_loss(*args)
+    torch.cuda.synchronize()
+    assert torch.equal(r2, res)
+    assert abs(float(loss) - float(err.double().mean())) <= 1e-6 * abs(float(err.double().mean()))

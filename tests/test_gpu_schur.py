@@ -238,3 +238,33 @@ def test_local_inputs_equal_global_inputs(cfg):
     assert torch.equal(h0, h1)
     for a, b in ((S0, S1), (b0, b1), (d0, d1), (p0, p1)):
         assert rel_err(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize('cfg,edit', [(0, None), (3, None), (4, None), (0, 'frozen-image')])
+def test_linearization_objective_outputs(cfg, edit):
+    """The linearization's residual and loss outputs equal the residual op's rows 0..2 and the
+    sum of its Huber errors, for every observation (also those of an image whose blocks are
+    all switched off, which the image-major passes do not visit)."""
+    sc = make_scene(cfg, n_imgs=40 if cfg == 4 else None, n_tracks=3000 if cfg == 4 else None)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    t = to_cuda(inp)
+    kw = {}
+    if edit == 'frozen-image':          # image 3: focal shared (mono), pose and depth masked out
+        mP = torch.ones(sc.n_nodes, dtype=torch.bool); mP[3] = False
+        mZ = torch.ones(sc.n_imgs, dtype=torch.bool); mZ[3] = False
+        kw = dict(optim_K=False, optim_P=mP, optim_Z=mZ)
+    plan = BAPlan(t['infos'], t['pids'], len(inp['K']), len(inp['P_w2rig']), len(inp['pts3d']), sc.n_zcf,
+                  optim_K=kw.get('optim_K', opts['optim_K']), optim_P=kw.get('optim_P', opts['optim_P']),
+                  optim_Z=kw.get('optim_Z', True))
+    p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                    t['pix2d_dep'], pix2d=t['pix2d'])
+    lo = BAPlan.lin_opts(weight_z=opts['weight_z'], pnorm=opts['pnorm'], max_pix_err=opts['clip_pix_err'],
+                         huber_delta=opts['huber_delta'])
+    s = plan.linearize(p, lo, objective=True)
+    full = cujac.residuals_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'],
+                                     t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], True, opts['weight_z'],
+                                     opts['pnorm'], opts['clip_pix_err'], opts['huber_delta'])
+    torch.cuda.synchronize()
+    assert rel_err(s.residuals.cpu().numpy(), full[:, :3].t().cpu().numpy()) < TOL_OBS
+    want = float(full[:, 3:6].double().sum())
+    assert abs(float(s.loss_sum) - want) <= 1e-6 * abs(want)
