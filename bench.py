@@ -583,6 +583,15 @@ def latency_record(cfg, dev, n=1000):
 # ------------------------------------------------------------------------------------------
 # the reference's own code (subprocesses: its GPU path, its CPU path)
 # ------------------------------------------------------------------------------------------
+# The reference's GPU path cannot run this workload: its fused_einsum_bki_bkj dispatch
+# (extensions/cujac/sfm_jacobian_rigs.cu:965-1006) has no (I, J, K) case for the blocks of 5
+# depth coefficients against 6 pose columns, and on a B200 the call crashed the process
+# (SIGSEGV in ba_solver.py:875, __matmul__obpc_obpr) instead of raising.  It is not run again.
+REFERENCE_GPU_UNAVAILABLE = ('the reference\'s CUDA einsum has no kernel for the 5-coefficient x 6-pose blocks of '
+                             'this configuration (sfm_jacobian_rigs.cu:965-1006); on a B200 its solver crashed with '
+                             'SIGSEGV at ba_solver.py:875, so it is not run')
+
+
 def internal_ref_gpu(args):
     """Child process: the reference's GaussNewtonSolver on this B200 with its own compiled
     CUDA ops, float64 (its production dtype) and float32; the linearization up to the PCG, and
@@ -826,19 +835,10 @@ def run_b200(args):
     if world == 1 and not args.no_extras:
         extras['configs3_latency'] = latency_record(3, dev, n=1000)
         extras['configs1_lm_iterations'] = lm_iterations(1, 10, 2, dev)
-        from oracle import ref_runner as RR
-        if RR.available():
-            extras['reference_gpu'] = run_child('ref-gpu', ['--config', str(args.config)] +
-                                                (['--tracks', str(args.tracks)] if args.tracks else []))
-            rg = extras['reference_gpu']
-            if 'linearize_f64_ms' in rg:
-                rg['what'] = ('the reference\'s own GaussNewtonSolver.compute_jacobians -> solve_delta with its '
-                              'compiled CUDA ops (baseline/_ref, built by its setup.py for sm_100a) on this B200: '
-                              'linearization up to its PCG (float64 production dtype, and float32), and the full '
-                              'solve_delta (PCG, back-substitution), wall clock with the device synchronised')
-                rg['fused_speedup_vs_f64_linearization'] = round(rg['linearize_f64_ms'] / head['ms_per_step'], 1)
-        else:
-            extras['reference_gpu'] = {'unavailable': 'the installed reference copy (baseline/_ref) is absent'}
+        extras['reference_gpu'] = {
+            'unavailable': REFERENCE_GPU_UNAVAILABLE,
+            'what': 'the reference\'s own GaussNewtonSolver.compute_jacobians -> solve_delta on this B200 with its '
+                    'compiled CUDA ops (bench.py --internal ref-gpu runs it where the configuration is supported)'}
 
     if rank == 0:
         line = {'metric': METRIC, 'value': head['value'], 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,

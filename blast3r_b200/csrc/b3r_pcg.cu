@@ -44,11 +44,19 @@ constexpr int kPcgVectors = 11;      // double vectors in the work buffer
 // own partial sums, and every block sums all partials in the same fixed order.
 constexpr int kPcgMaxBlocks = 1024;
 constexpr size_t kPcgFlagsOff = 256, kPcgPartOff = kPcgFlagsOff + 4 * kPcgMaxBlocks;
-constexpr size_t kPcgVecOff = kPcgPartOff + 4 * 8 * kPcgMaxBlocks;
+constexpr size_t kPcgHelpOff = kPcgPartOff + 4 * 8 * kPcgMaxBlocks;   // helper flags, then helper sums
+constexpr int kPcgSrcMax = 3;        // source vectors of one matvec pass
 static_assert(kPcgMaxBlocks % kPcgThreads == 0, "barrier flags per polling thread");
+static_assert(kPcgThreads == 32 * kPcgWarps, "PCG block size");
 
-inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the vectors
-  return (kPcgVecOff + kPcgVectors * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
+__host__ __device__ inline size_t pcg_hsum_off(const DevPlan& d) {         // helper partial row sums [help][src][32]
+  return (kPcgHelpOff + 4 * (size_t)d.n_pcg_help + 255) & ~size_t(255);
+}
+__host__ __device__ inline size_t pcg_vec_off(const DevPlan& d) {
+  return (pcg_hsum_off(d) + 8 * (size_t)d.n_pcg_help * kPcgSrcMax * 32 + 255) & ~size_t(255);
+}
+__host__ __device__ inline size_t pcg_panel_off(const DevPlan& d) {        // panels after the vectors
+  return (pcg_vec_off(d) + kPcgVectors * 8 * (size_t)d.n_cam_params + 255) & ~size_t(255);
 }
 
 struct PcgWords {
@@ -88,13 +96,15 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
 // the next one.
 // With cfg.unreachable (a test of the failure path) block 0 waits for flag values one
 // generation beyond what any block publishes, so its wait always runs out.
+// A block arriving with ok == false (a helper wait ran out) arrives with kFlagAbort, so that
+// every block leaves at this barrier.
 __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, unsigned int target,
-                                             const BarrierCfg& cfg) {
+                                             const BarrierCfg& cfg, bool arrive_ok) {
   __shared__ int ok_s;
   __syncthreads();                                       // the block's writes precede its arrival
   if (threadIdx.x == 0) {
-    ok_s = 1;
-    st_release(flags + blockIdx.x, target);
+    ok_s = arrive_ok ? 1 : 0;
+    st_release(flags + blockIdx.x, arrive_ok ? target : kFlagAbort);
   }
   __syncthreads();
   if (blockIdx.x == 0) {
@@ -197,20 +207,26 @@ __device__ __forceinline__ void panel_matvec(const float* __restrict__ P, const 
   }
 }
 
-// The matvec of row group g: every task's partial row sums into its shared-memory slots.
-template <typename TS, int MAXB, bool DIV>
+// The matvec of one row group over NS source vectors at once (the panel values are loaded
+// once): every task's partial row sums go to its shared-memory slots slots[s][.].
+template <typename TS, int MAXB, int NS, bool DIV>
 __device__ __forceinline__ void group_matvec(const DevPlan& d, const float* __restrict__ pan, int4 g,
-                                             const TS* __restrict__ src, const float* __restrict__ M, double* slots) {
+                                             const TS* const (&src)[NS], const float* __restrict__ M,
+                                             double (*slots)[kPcgSlots]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int task = g.x + warp; task < g.y; task += kPcgThreads / 32) {
+  for (int task = g.x + warp; task < g.y; task += kPcgWarps) {
     const int4 tk = __ldg(d.mv_task + task);             // block row, panel columns [c0, c1), flags
     const int4 rw = __ldg(d.mv_row + task);              // boff, W, panel offset / 4, column-list offset
     const int bp = tk.w >> 8, slot = __ldg(d.mv_slot + task);
-    double yo[MAXB];
-    panel_matvec<TS, MAXB, DIV>(pan + 4 * (int64_t)rw.z, d.pan_col + rw.w, rw.y, bp, tk.y, tk.z, src, M, lane, yo);
 #pragma unroll
-    for (int rr = 0; rr < MAXB; ++rr)
-      if (lane == rr && rr < bp) slots[slot + rr] = yo[rr];
+    for (int sv = 0; sv < NS; ++sv) {
+      double yo[MAXB];
+      panel_matvec<TS, MAXB, DIV>(pan + 4 * (int64_t)rw.z, d.pan_col + rw.w, rw.y, bp, tk.y, tk.z, src[sv], M, lane,
+                                  yo);
+#pragma unroll
+      for (int rr = 0; rr < MAXB; ++rr)
+        if (lane == rr && rr < bp) slots[sv][slot + rr] = yo[rr];
+    }
   }
 }
 
@@ -221,6 +237,73 @@ __device__ __forceinline__ double slot_sum(const DevPlan& d, int j, const double
   double v = 0.0;
   for (int t = 0; t < nt; ++t) v += slots[sc.x + t * stride];
   return v;
+}
+
+struct HelpCfg {
+  unsigned int* flags;    // [n_pcg_help] generation of the last partial sums published
+  double* sums;           // [n_pcg_help][kPcgSrcMax][32]
+  long long spins;
+};
+
+// One matvec pass of the PCG over this block's row groups: y = S v for NS source vectors, and
+// for every scalar j the block owns, on_scalar(j, y_0..y_{NS-1}).  Helper groups of a split
+// row go first in every block (they never wait): they publish their partial row sums with a
+// release store of the pass's generation; the owner of the row adds them, in helper order,
+// after an acquire poll (bounded; a poll that runs out clears ok).
+template <typename TS, int MAXB, int NS, bool DIV, typename F>
+__device__ __forceinline__ void matvec_pass(const DevPlan& d, const float* __restrict__ pan,
+                                            const TS* const (&src)[NS], const float* __restrict__ M,
+                                            double (*slots)[kPcgSlots], const HelpCfg& hc, unsigned int gen, bool& ok,
+                                            F&& on_scalar) {
+  __shared__ int wait_ok;
+  for (int pass = 0; pass < 2; ++pass) {               // 0: helper groups, 1: the others
+    for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+      const int4 h = __ldg(d.pcg_grp2 + gi);
+      const bool helper = h.z >= 0;
+      if (helper != (pass == 0)) continue;
+      const int4 g = __ldg(d.pcg_grp + gi);
+      group_matvec<TS, MAXB, NS, DIV>(d, pan, g, src, M, slots);
+      __syncthreads();
+      if (helper) {
+        const int bp = h.w, nt = h.x;
+        for (int idx = threadIdx.x; idx < NS * bp; idx += blockDim.x) {
+          const int sv = idx / bp, r = idx - sv * bp;
+          double v = 0.0;
+          for (int t = 0; t < nt; ++t) v += slots[sv][t * bp + r];
+          hc.sums[((int64_t)h.z * kPcgSrcMax + sv) * 32 + r] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) st_release(hc.flags + h.z, gen);
+      } else {
+        if (h.y > 0) {                                  // the owner of a split row waits for its helpers
+          if (threadIdx.x == 0) wait_ok = 1;
+          __syncthreads();
+          if (threadIdx.x < h.y) {
+            long long spins = 0;
+            while (ld_acquire(hc.flags + h.x + threadIdx.x) < gen) {
+              if (++spins > hc.spins) { wait_ok = 0; break; }
+              __nanosleep(32);
+            }
+          }
+          __syncthreads();
+          if (!wait_ok) ok = false;
+        }
+        for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+          double y[NS];
+#pragma unroll
+          for (int sv = 0; sv < NS; ++sv) y[sv] = slot_sum(d, j, slots[sv]);
+          if (h.y > 0) {
+            const int r = j - g.z;
+            for (int i = 0; i < h.y; ++i)
+#pragma unroll
+              for (int sv = 0; sv < NS; ++sv) y[sv] += __ldcg(hc.sums + ((int64_t)(h.x + i) * kPcgSrcMax + sv) * 32 + r);
+          }
+          on_scalar(j, y);
+        }
+      }
+      __syncthreads();
+    }
+  }
 }
 
 // Sums of (u, v, w) over the block (valid on thread 0).
@@ -262,13 +345,15 @@ template <typename TI, int MAXB>
 __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
     DevPlan d, const float* __restrict__ M, const TI* __restrict__ b, TI* __restrict__ xo, double tol, int maxiter,
     char* work, const float* __restrict__ pan, int* result, long long spin_limit, int test_flags) {
-  __shared__ double slots[kPcgSlots];
+  __shared__ double slots[kPcgSrcMax][kPcgSlots];
   __shared__ double3 red3[kPcgThreads / 32];
   __shared__ double3 bc3;
   PcgWords* wd = reinterpret_cast<PcgWords*>(work);
   unsigned int* flags = reinterpret_cast<unsigned int*>(work + kPcgFlagsOff);
   PcgPart* part = reinterpret_cast<PcgPart*>(work + kPcgPartOff);
-  double* vec = reinterpret_cast<double*>(work + kPcgVecOff);
+  const HelpCfg hc{reinterpret_cast<unsigned int*>(work + kPcgHelpOff),
+                   reinterpret_cast<double*>(work + pcg_hsum_off(d)), spin_limit};
+  double* vec = reinterpret_cast<double*>(work + pcg_vec_off(d));
   const int64_t n = d.n_cam_params;
   double* x = vec;                     // every vector element is owned by the block of its row group
   double* r = vec + n;
@@ -281,39 +366,43 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
   double* bx = vec + 8 * n;            // best-so-far iterate
   double* mb[2] = {vec + 9 * n, vec + 10 * n};   // m = M^-1 w by iteration parity (read by every block)
   BarrierCfg bcfg{spin_limit, (test_flags & 1) != 0};
-  unsigned int target = 0;
+  unsigned int target = 0, gen = 0;
+  bool ok = true;
   auto publish = [&](double a, double b2, double c) {
     const double3 t = block_sum3(a, b2, c, red3);
     if (threadIdx.x == 0) { part[blockIdx.x].v[0] = t.x; part[blockIdx.x].v[1] = t.y; part[blockIdx.x].v[2] = t.z; }
+  };
+  auto own_scalars = [&](auto&& fn) {                  // the scalars of this block's row groups
+    for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
+      const int4 g = __ldg(d.pcg_grp + gi);
+      for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) fn(j);
+    }
   };
 
   // prologue: x0 = 0, r0 = b, u0 = M^-1 b, w0 = S u0, m0 = M^-1 w0, and the partial sums of
   // r0.u0, w0.u0, b.b
   double s_g = 0.0, s_d = 0.0, s_bb = 0.0;
-  for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-    const int4 g = __ldg(d.pcg_grp + gi);
-    group_matvec<TI, MAXB, true>(d, pan, g, b, M, slots);
-    __syncthreads();
-    for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
+  {
+    const TI* const src[1] = {b};
+    matvec_pass<TI, MAXB, 1, true>(d, pan, src, M, slots, hc, ++gen, ok, [&](int j, const double* y) {
       const double bj = (double)b[j], Mj = (double)M[j];
-      const double uj = bj / Mj, wj = slot_sum(d, j, slots);
+      const double uj = bj / Mj, wj = y[0];
       x[j] = 0.0; r[j] = bj; u[j] = uj; w[j] = wj; mb[0][j] = wj / Mj;
       z[j] = 0.0; q[j] = 0.0; s[j] = 0.0; p[j] = 0.0; bx[j] = 0.0;
       s_g += bj * uj;
       s_d += wj * uj;
       s_bb += bj * bj;
-    }
-    __syncthreads();
+    });
   }
   publish(s_g, s_d, s_bb);
-  bool ok = grid_barrier(wd, flags, ++target, bcfg);
+  ok = grid_barrier(wd, flags, ++target, bcfg, ok);
   double3 t3 = grid_sum3(part, red3, &bc3);
   double gamma = t3.x, delta = t3.y;
   const double bnorm = fmax(sqrt(t3.z), 1e-12);
   double rn = sqrt(t3.z), gamma_old = 0.0, alpha_old = 1.0;
 
   double best = __longlong_as_double(0x7ff0000000000000LL);   // +inf
-  int best_k = 0, k_stop = 0;
+  int best_k = 0, k_stop = 0, replaced = 0;
   bool converged = false;
   for (int k = 1; ok && k <= maxiter + 1; ++k) {
     // ---- decisions on iterate k-1 (x_{k-1}, r_{k-1}; identical in every thread) ----
@@ -324,48 +413,36 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
         // true values (residual replacement): r = b - S x, u = M^-1 r, w = S u, s = S p,
         // z = S q, m = M^-1 w.
         double s_rr = 0.0;
-        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-          const int4 g = __ldg(d.pcg_grp + gi);
-          group_matvec<double, MAXB, false>(d, pan, g, x, M, slots);
-          __syncthreads();
-          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
-            const double rj = (double)b[j] - slot_sum(d, j, slots);
+        {
+          const double* const src[1] = {x};
+          matvec_pass<double, MAXB, 1, false>(d, pan, src, M, slots, hc, ++gen, ok, [&](int j, const double* y) {
+            const double rj = (double)b[j] - y[0];
             r[j] = rj;
             u[j] = rj / (double)M[j];
             s_rr += rj * rj;
-          }
-          __syncthreads();
+          });
         }
         publish(0.0, 0.0, s_rr);
-        if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
         t3 = grid_sum3(part, red3, &bc3);
         rn = sqrt(t3.z);
         if (rn <= tol * bnorm) { converged = true; k_stop = k - 1; break; }
+        ++replaced;
         s_g = 0.0; s_d = 0.0;
         double* mc = mb[(k - 1) & 1];
-        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-          const int4 g = __ldg(d.pcg_grp + gi);
-          group_matvec<double, MAXB, false>(d, pan, g, u, M, slots);
-          __syncthreads();
-          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
-            const double wj = slot_sum(d, j, slots);
-            w[j] = wj;
-            mc[j] = wj / (double)M[j];
+        {
+          const double* const src[3] = {u, p, q};
+          matvec_pass<double, MAXB, 3, false>(d, pan, src, M, slots, hc, ++gen, ok, [&](int j, const double* y) {
+            w[j] = y[0];
+            s[j] = y[1];
+            z[j] = y[2];
+            mc[j] = y[0] / (double)M[j];
             s_g += r[j] * u[j];
-            s_d += wj * u[j];
-          }
-          __syncthreads();
-          group_matvec<double, MAXB, false>(d, pan, g, p, M, slots);
-          __syncthreads();
-          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) s[j] = slot_sum(d, j, slots);
-          __syncthreads();
-          group_matvec<double, MAXB, false>(d, pan, g, q, M, slots);
-          __syncthreads();
-          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) z[j] = slot_sum(d, j, slots);
-          __syncthreads();
+            s_d += y[0] * u[j];
+          });
         }
         publish(s_g, s_d, 0.0);
-        if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
         t3 = grid_sum3(part, red3, &bc3);
         gamma = t3.x;
         delta = t3.y;
@@ -373,10 +450,7 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
       if (rn < best) {                                   // best-so-far iterate
         best = rn;
         best_k = k - 1;
-        for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-          const int4 g = __ldg(d.pcg_grp + gi);
-          for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) bx[j] = x[j];
-        }
+        own_scalars([&](int j) { bx[j] = x[j]; });
       }
       if (!isfinite(gamma)) break;                       // the reference's r.z
     }
@@ -385,16 +459,13 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
     const double beta = k > 1 ? gamma / fmax(gamma_old, 1e-32) : 0.0;
     const double den = k > 1 ? delta - beta * gamma / alpha_old : delta;   // = p.S p
     const double alpha = gamma / fmax(den, 1e-32);
-    const double* mc = mb[(k - 1) & 1];
     double* mn = mb[k & 1];
     double s_rr = 0.0;
     s_g = 0.0; s_d = 0.0;
-    for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-      const int4 g = __ldg(d.pcg_grp + gi);
-      group_matvec<double, MAXB, false>(d, pan, g, mc, M, slots);
-      __syncthreads();
-      for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) {
-        const double nj = slot_sum(d, j, slots), mj = mc[j], wj = w[j], uj = u[j];
+    {
+      const double* const src[1] = {mb[(k - 1) & 1]};
+      matvec_pass<double, MAXB, 1, false>(d, pan, src, M, slots, hc, ++gen, ok, [&](int j, const double* y) {
+        const double nj = y[0], mj = src[0][j], wj = w[j], uj = u[j];
         const double zj = nj + beta * z[j], qj = mj + beta * q[j], sj = wj + beta * s[j], pj = uj + beta * p[j];
         const double xj = x[j] + alpha * pj, rj = r[j] - alpha * sj, un = uj - alpha * qj, wn = wj - alpha * zj;
         z[j] = zj; q[j] = qj; s[j] = sj; p[j] = pj;
@@ -403,11 +474,10 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
         s_g += rj * un;
         s_d += wn * un;
         s_rr += rj * rj;
-      }
-      __syncthreads();
+      });
     }
     publish(s_g, s_d, s_rr);
-    if (!(ok = grid_barrier(wd, flags, ++target, bcfg))) break;
+    if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
     t3 = grid_sum3(part, red3, &bc3);
     gamma_old = gamma;
     alpha_old = alpha;
@@ -415,16 +485,13 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
     delta = t3.y;
     rn = sqrt(t3.z);
   }
-  // the converging iterate, else the best-so-far one (zeros if none improved or a barrier
-  // gave up)
-  for (int gi = blockIdx.x; gi < d.n_pcg_groups; gi += gridDim.x) {
-    const int4 g = __ldg(d.pcg_grp + gi);
-    for (int j = g.z + threadIdx.x; j < g.w; j += blockDim.x) xo[j] = ok ? (TI)(converged ? x[j] : bx[j]) : TI(0);
-  }
+  // the converging iterate, else the best-so-far one (zeros if none improved or a wait gave up)
+  own_scalars([&](int j) { xo[j] = ok ? (TI)(converged ? x[j] : bx[j]) : TI(0); });
   if (!ok && threadIdx.x == 0) atomicOr(result + 2, 1);   // any block that gave up flags the solve
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     result[0] = converged ? k_stop : best_k;
     result[1] = converged ? 1 : 0;
+    result[3] = replaced;
   }
 }
 
@@ -448,7 +515,10 @@ int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b,
   // barrier words and arrival flags start at zero (targets count up from 1 in every launch);
   // result[2] is set by any block whose barrier wait runs out
   B3R_TRY(check_cuda(cudaMemsetAsync(work, 0, kPcgPartOff, s), "clear PCG barrier words"));
-  B3R_TRY(check_cuda(cudaMemsetAsync(result, 0, 3 * sizeof(int), s), "clear PCG result"));
+  if (d.n_pcg_help > 0)
+    B3R_TRY(check_cuda(cudaMemsetAsync((char*)work + kPcgHelpOff, 0, 4 * (size_t)d.n_pcg_help, s),
+                       "clear PCG helper flags"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(result, 0, 4 * sizeof(int), s), "clear PCG result"));
   DevPlan dv = d;
   char* wk = reinterpret_cast<char*>(work);
   float* pan = reinterpret_cast<float*>(wk + pcg_panel_off(d));

@@ -105,7 +105,8 @@ struct PlanBuild {
   std::vector<int4> t_idx, c1_idx, rest_idx;
   std::vector<int> sym_ptr, sym_ent;
   std::vector<int4> mv_task, mv_row, mv_ent;
-  std::vector<int4> pcg_grp;
+  std::vector<int4> pcg_grp, pcg_grp2;
+  int n_pcg_help = 0;
   std::vector<int> mv_slot;
   std::vector<int2> pcg_scl;
   int pcg_target_groups = 444;
@@ -579,15 +580,42 @@ static int build_pattern(PlanBuild& B) {
     }
     B.pan_floats = poff;
     // PCG row groups: cut the block rows into contiguous groups of about total / target
-    // panel work (a heavier row is a group of its own), at most kPcgSlots task-row sums each
+    // panel work, at most kPcgSlots task-row sums each.  A row heavier than 1.5 targets (the
+    // focal row of a mono camera couples to every block) is split by its tasks into an owner
+    // group and helper groups on other blocks: helpers publish their partial row sums, the
+    // owner adds them (in helper order) before it updates the row.
     int64_t total = 0;
     for (int pr = 0; pr < nb; ++pr) total += (int64_t)B.bsize[pr] * B.pan_w[pr];
     const int64_t target = std::max<int64_t>(1, total / std::max(1, B.pcg_target_groups));
     B.mv_slot.assign(B.mv_task.size(), 0);
     const int ncp_all = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
     B.pcg_scl.assign(ncp_all, make_int2(0, 0));
-    int task0 = 0;
+    int task0 = 0, n_help = 0;
     for (int pr = 0; pr < nb;) {
+      const int nt0 = (B.pan_w[pr] + kMvCols - 1) / kMvCols;
+      const int64_t w0 = (int64_t)B.bsize[pr] * B.pan_w[pr];
+      const int bp0 = B.bsize[pr];
+      if (w0 > target + target / 2 && nt0 > 1) {
+        const int parts = (int)std::min<int64_t>(nt0, std::max<int64_t>((w0 + target - 1) / target,
+                                                                        (nt0 + kPcgWarps - 1) / kPcgWarps));
+        const int first_help = n_help;
+        for (int part = 0; part < parts; ++part) {
+          const int tb = task0 + (int)((int64_t)nt0 * part / parts), te = task0 + (int)((int64_t)nt0 * (part + 1) / parts);
+          for (int t = tb; t < te; ++t) B.mv_slot[t] = (t - tb) * bp0;
+          if (part == 0) {
+            for (int r = 0; r < bp0; ++r) B.pcg_scl[B.boff[pr] + r] = make_int2(r, (te - tb) | (bp0 << 16));
+            B.pcg_grp.push_back(make_int4(tb, te, B.boff[pr], B.boff[pr] + bp0));
+            B.pcg_grp2.push_back(make_int4(first_help, parts - 1, -1, bp0));
+          } else {
+            B.pcg_grp.push_back(make_int4(tb, te, 0, 0));
+            B.pcg_grp2.push_back(make_int4(te - tb, 0, n_help++, bp0));   // helper: its task count, slot
+          }
+        }
+        B3R_REQUIRE(nt0 * bp0 <= kPcgSlots * kPcgWarps, "internal: PCG row of %d tasks", nt0);
+        task0 += nt0;
+        ++pr;
+        continue;
+      }
       int slots = 0, t_begin = task0;
       int64_t work = 0;
       const int sc_begin = B.boff[pr];
@@ -595,7 +623,8 @@ static int build_pattern(PlanBuild& B) {
       for (; q < nb; ++q) {
         const int nt = (B.pan_w[q] + kMvCols - 1) / kMvCols;
         const int64_t wq = (int64_t)B.bsize[q] * B.pan_w[q];
-        if (q > pr && (work + wq > target || slots + nt * B.bsize[q] > kPcgSlots)) break;
+        if (q > pr && (work + wq > target || slots + nt * B.bsize[q] > kPcgSlots ||
+                       wq > target + target / 2)) break;
         for (int t = 0; t < nt; ++t) B.mv_slot[task0 + t] = slots + t * B.bsize[q];
         for (int r = 0; r < B.bsize[q]; ++r) B.pcg_scl[B.boff[q] + r] = make_int2(slots + r, nt | (B.bsize[q] << 16));
         slots += nt * B.bsize[q];
@@ -604,8 +633,10 @@ static int build_pattern(PlanBuild& B) {
       }
       B3R_REQUIRE(slots <= kPcgSlots, "internal: PCG row group needs %d slots", slots);
       B.pcg_grp.push_back(make_int4(t_begin, task0, sc_begin, B.boff[q - 1] + B.bsize[q - 1]));
+      B.pcg_grp2.push_back(make_int4(0, 0, -1, 0));
       pr = q;
     }
+    B.n_pcg_help = n_help;
     B3R_REQUIRE(task0 == (int)B.mv_task.size(), "internal: PCG groups cover %d of %zu tasks", task0,
                 B.mv_task.size());
   }
@@ -771,8 +802,10 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.sym_ptr, &d.sym_ptr); A.add(B.sym_ent, &d.sym_ent);
   A.add(B.mv_task, &d.mv_task); A.add(B.mv_row, &d.mv_row); A.add(B.mv_ent, &d.mv_ent);
   d.n_mv_tasks = (int)B.mv_task.size();
-  A.add(B.pcg_grp, &d.pcg_grp); A.add(B.mv_slot, &d.mv_slot); A.add(B.pcg_scl, &d.pcg_scl);
+  A.add(B.pcg_grp, &d.pcg_grp); A.add(B.pcg_grp2, &d.pcg_grp2);
+  A.add(B.mv_slot, &d.mv_slot); A.add(B.pcg_scl, &d.pcg_scl);
   d.n_pcg_groups = (int)B.pcg_grp.size();
+  d.n_pcg_help = B.n_pcg_help;
   A.add(B.pan_off, &d.pan_off); A.add(B.pan_w, &d.pan_w); A.add(B.col_off, &d.col_off);
   A.add(B.pan_col, &d.pan_col); A.add(B.ent_col, &d.ent_col); A.add(B.ent_row, &d.ent_row);
   d.pan_floats = B.pan_floats;

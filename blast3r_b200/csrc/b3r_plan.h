@@ -26,6 +26,7 @@ constexpr int kMvCols = 256;       // max panel columns per matvec task (8 per l
 constexpr int kRestBlocks = 64;     // blocks of the objective pass over observations without an image-major entry
 constexpr int kPcgSlots = 1024;    // per-task partial row sums one PCG row group keeps in shared memory
 constexpr int kPcgBlocksPerSm = 3; // resident PCG blocks per SM the row groups are sized for
+constexpr int kPcgWarps = 8;       // warps of a PCG block
 
 // sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
 constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
@@ -125,8 +126,11 @@ struct DevPlan {
   // PCG row groups: contiguous block rows whose matvec tasks and vector updates one CTA does
   // (so the update of a row never waits for another CTA's matvec); about one group per
   // resident CTA, balanced by panel work
-  int n_pcg_groups;
+  int n_pcg_groups, n_pcg_help;
   const int4* pcg_grp;    // [n_pcg_groups] (first task, end task, first scalar, end scalar)
+  const int4* pcg_grp2;   // [n_pcg_groups] owner of a split row: (first helper slot, helpers, -1,
+                          //  block size); helper: (tasks, 0, its helper slot, block size);
+                          //  others (0, 0, -1, 0)
   const int* mv_slot;     // [n_mv_tasks] first shared-memory slot of the task's row sums
   const int2* pcg_scl;    // [n_cam_params] (slot of the scalar's first task, the row's task
                           //  count | block size << 16): the scalar sums its tasks' slots in order

@@ -7,10 +7,11 @@
 //   points    track-major, one warp per <=32-observation task: per-track Hpp and g_p by a
 //             segmented warp scan, and the max |diag(Hpp)| for adaptive damping
 //   factor    per track: damped guarded 3x3 Cholesky Hpp = L L^T (sfm_jacobian_rigs.cu
-//             :578-617), stored in reciprocal form, and the point step Hpp^-1 g_p (double)
+//             :578-617) computed in double and rounded once, stored in reciprocal form, and
+//             z = L^-1 g_p from the rounded factor (the one the elimination records use)
 //   diag      image-major: per observation the elimination record Y = L^-1 Hpc in reduced
 //             form (3 x [f0 f1 tau0..5 zscale]) + its depth channels, written to its
-//             image-major slot; Hcc - Y^T Y and g_c - Hcp Hpp^-1 g_p expanded to the typed blocks of
+//             image-major slot; Hcc - Y^T Y and g_c - Y^T z expanded to the typed blocks of
 //             its image, reduced per image chunk, one atomic per value per chunk; also
 //             diag(Hcc) for the damping and preconditioner
 //   pairs     segment-major: for every image pair (i, i') the sum over shared tracks of
@@ -247,7 +248,7 @@ struct ObsIn {
   float px, py, sx, sy;
   float dep[CT];
   float4 tf0, tf1;  // track factor (reciprocal form) and z, track-record floats 12..19
-  float4 tf2;       // track-record floats 20..23: z[2], delta = Hpp^-1 g_p
+  float4 tf2;       // track-record floats 20..23: z[2] (21..23 unused)
 };
 
 template <int CT>
@@ -274,7 +275,7 @@ __device__ __forceinline__ void load_obs_in(const Ctx& c, int e, int ee, ObsIn<C
 }
 
 // Linearize a prefetched image-major observation of image img.
-template <int CT>
+template <int CT, bool OBJ>
 __device__ __forceinline__ void view_in(const Ctx& c, const ObsIn<CT>& in, int img, const Cam& cam, const float* zc,
                                         ObsView<CT>& V, float& esum) {
   const int64_t o = in.ix.x;
@@ -284,11 +285,13 @@ __device__ __forceinline__ void view_in(const Ctx& c, const ObsIn<CT>& in, int i
   if (c.pix2d) {
     linearize_obs<float, true, true, CT>(cam, in.X, in.px, in.py, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = L.r[0]; r1 = L.r[1]; r2 = L.r[2]; w0 = L.w[0]; w1 = L.w[1]; w2 = L.w[2];
-    if (c.res_out) {                              // the objective's residuals, at the input row
-      const int64_t n = c.d.n_in;
-      c.res_out[o] = r0; c.res_out[n + o] = r1; c.res_out[2 * n + o] = r2;
+    if (OBJ) {
+      if (c.res_out) {                            // the objective's residuals, at the input row
+        const int64_t n = c.d.n_in;
+        c.res_out[o] = r0; c.res_out[n + o] = r1; c.res_out[2 * n + o] = r2;
+      }
+      esum = L.err[0] + L.err[1] + L.err[2];
     }
-    esum = L.err[0] + L.err[1] + L.err[2];
   } else {
     linearize_obs<float, false, true, CT>(cam, in.X, 0.f, 0.f, in.sx, in.sy, in.dep, zc, CT, c.o, L);
     r0 = c.res[o * c.rs_n]; r1 = c.res[o * c.rs_n + c.rs_c]; r2 = c.res[o * c.rs_n + 2 * c.rs_c];
@@ -435,10 +438,12 @@ __global__ void __launch_bounds__(128) k_points(Ctx c) {
 }
 
 // Pass "factor": damped Cholesky factor of every local track (BlockDiagMat.dampen_ then
-// chol3x3_solve's guarded factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599),
-// z = L^-1 g_p and the point step delta = Hpp^-1 g_p.  The factor is stored in reciprocal
-// form (1/l00, l10, l20, 1/l11, l21, 1/l22) at track-record floats 12..17, z at 18..20,
-// delta at 21..23, so the per-observation elimination Y = L^-1 Hpc needs no division.
+// chol3x3_solve's guarded factorisation with jitter 1e-12, ba_solver.py:572-582, 589-599).
+// The factor is computed in double and rounded once to the reciprocal form (1/l00, l10, l20,
+// 1/l11, l21, 1/l22) stored at track-record floats 12..17, so the per-observation elimination
+// Y = L^-1 Hpc needs no division; z = L^-1 g_p (floats 18..20) is solved from the same
+// rounded factor, so that S (through Y^T Y) and b (through Y^T z) are eliminated with one
+// factor: their rounding then stays consistent, which matters on ill-conditioned systems.
 __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   const int tl = blockIdx.x * blockDim.x + threadIdx.x;
   const float lam = c.dampen * (c.adaptive ? *c.hpp_max : 1.f);
@@ -449,21 +454,19 @@ __global__ void __launch_bounds__(256) k_factor(Ctx c) {
   const float4 a = t4[0], b = t4[1];
   const float g8 = c.trec[(int64_t)tl * 24 + 8];
   const float h00 = a.x + lam, h01 = a.y, h02 = a.z, h11 = a.w + lam, h12 = b.x, h22 = b.y + lam;
-  float l[6], z[3];
-  chol3<float>(h00, h01, h02, h01, h11, h12, h02, h12, h22, 1e-12f, l);
-  const float g[3] = {b.z, b.w, g8};
-  chol3_fwd<float>(l, g, z);
-  // the point step delta = Hpp^-1 g_p, solved in double (the gradient's elimination term
-  // Hcp delta is formed with it, as the reference's rhs g_c - B D^-1 g_p, ba_solver.py:188)
-  double ld[6], zd[3], dd[3];
-  const double gd[3] = {(double)b.z, (double)b.w, (double)g8};
+  // the factor in double, rounded once; z from the rounded factor (the same one S uses)
+  double ld[6];
   chol3<double>((double)h00, (double)h01, (double)h02, (double)h01, (double)h11, (double)h12, (double)h02,
                 (double)h12, (double)h22, 1e-12, ld);
-  chol3_fwd<double>(ld, gd, zd);
-  chol3_bwd<double>(ld, zd, dd);
-  t4[3] = make_float4(1.f / l[0], l[1], l[2], 1.f / l[3]);    // floats 12..15
-  t4[4] = make_float4(l[4], 1.f / l[5], z[0], z[1]);          // floats 16..19
-  t4[5] = make_float4(z[2], (float)dd[0], (float)dd[1], (float)dd[2]);   // floats 20..23
+  const float r0 = (float)(1.0 / ld[0]), l1 = (float)ld[1], l2 = (float)ld[2], r3 = (float)(1.0 / ld[3]);
+  const float l4 = (float)ld[4], r5 = (float)(1.0 / ld[5]);
+  const double z0 = (double)b.z * r0;
+  const double z1 = ((double)b.w - (double)l1 * z0) * r3;
+  const double z2 = ((double)g8 - (double)l2 * z0 - (double)l4 * z1) * r5;
+  const float z[3] = {(float)z0, (float)z1, (float)z2};
+  t4[3] = make_float4(r0, l1, l2, r3);                        // floats 12..15
+  t4[4] = make_float4(l4, r5, z[0], z[1]);                    // floats 16..19
+  t4[5] = make_float4(z[2], 0.f, 0.f, 0.f);                   // floats 20..23 (21..23 unused)
 }
 
 __device__ __forceinline__ double warp_sum_dbl(double v) {
@@ -579,23 +582,17 @@ __device__ __forceinline__ void diag_terms(const Ctx& c, const ObsView<CT>& V, b
   for (int t = 0; t < 6; ++t) out[Lay::DA + 2 + t] = H[2 + t][2 + t];
 #pragma unroll
   for (int ch = 0; ch < CT; ++ch) out[Lay::DA + 8 + ch] = H[8][8] * V.dep[ch] * V.dep[ch];
-  if (elim) {              // eliminated track: record Y, subtract Y^T Y and Hcp delta (delta = Hpp^-1 g_p)
+  if (elim) {                                     // eliminated track: record Y, subtract Y^T Y, Y^T z
     const float li[6] = {tf0.x, tf0.y, tf0.z, tf0.w, tf1.x, tf1.y};
     float Y[9][3];
     elim_record<CT>(c, e, V, li, Y);
-    float jd[3];                                  // Jpw delta, so that Hcp delta = Jcw^T (Jpw delta)
-#pragma unroll
-    for (int i = 0; i < 3; ++i) jd[i] = fmaf(V.Jpw[3 * i + 2], tf2.w, fmaf(V.Jpw[3 * i + 1], tf2.z, V.Jpw[3 * i] * tf2.y));
+    const float z0 = tf1.z, z1 = tf1.w, z2 = tf2.x;
 #pragma unroll
     for (int a = 0; a < 9; ++a) {
 #pragma unroll
       for (int b = a; b < 9; ++b)
         H[a][b] = fmaf(-Y[a][2], Y[b][2], fmaf(-Y[a][1], Y[b][1], fmaf(-Y[a][0], Y[b][0], H[a][b])));
-      float hd = V.Jcw[18 + a] * jd[2];
-#pragma unroll
-      for (int i = 1; i >= 0; --i)
-        if (jc_nz(i, a)) hd = fmaf(V.Jcw[9 * i + a], jd[i], hd);
-      g[a] -= hd;
+      g[a] = fmaf(-Y[a][2], z2, fmaf(-Y[a][1], z1, fmaf(-Y[a][0], z0, g[a])));
     }
   }
   out[Lay::FF + 0] = H[0][0];
@@ -640,7 +637,7 @@ template <int CT> __host__ __device__ constexpr int diag_row_stride() {
 // transpose buffer; then each lane sums a group of four neighbouring values down the 32
 // rows with 16-byte reads and keeps the running sums, so the N values never sit in every
 // thread's registers across observations.
-template <int CT>
+template <int CT, bool OBJ>
 __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restrict__ S, float* __restrict__ b,
                                                        float* __restrict__ diagA) {
   using Lay = DiagLayout<CT>;
@@ -671,8 +668,8 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     if (e < ee) {
       ObsView<CT> V;
       float es;
-      view_in<CT>(c, cur, img, cam, zc, V, es);
-      err_acc += es;
+      view_in<CT, OBJ>(c, cur, img, cam, zc, V, es);
+      if (OBJ) err_acc += es;
       diag_terms<CT>(c, V, cur.ix.y >= 0, e, cur.tf0, cur.tf1, cur.tf2, rw + lane * RS);
     } else {
       for (int v = 0; v < Lay::N; ++v) rw[lane * RS + v] = 0.f;
@@ -700,12 +697,12 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     if (g < NG) *reinterpret_cast<float4*>(rw + 4 * g) = run[j];
   }
   __shared__ double esm[NW];
-  if (c.loss_part) {                              // the chunk's Huber-error sum (no atomics)
+  if (OBJ && c.loss_part) {                       // the chunk's Huber-error sum (no atomics)
     const double t = warp_sum_dbl((double)err_acc);
     if (lane == 0) esm[warp] = t;
   }
   __syncthreads();
-  if (c.loss_part && threadIdx.x == 0) {
+  if (OBJ && c.loss_part && threadIdx.x == 0) {
     double t = 0.0;
 #pragma unroll
     for (int w = 0; w < NW; ++w) t += esm[w];
@@ -1053,7 +1050,7 @@ __global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* _
 // observation's depth channels, and every Schur term is a scalar times an outer product of
 // depth vectors:
 //   image block      (zw^2 - y.y) dep dep^T
-//   gradient         (zw sqrt(W_z) r_z - zw Jpw[2].delta) dep   (delta = Hpp^-1 g_p)
+//   gradient         (zw sqrt(W_z) r_z - y.z) dep          (z = L^-1 g_p)
 //   diag(A)          zw^2 dep_c^2
 //   pair product     (y_o . y_o') dep_o dep_o'^T
 // These are the general passes' values with the focal and pose columns left out (the same
@@ -1088,7 +1085,7 @@ constexpr int kDiagZThreads = 128;
 // Image-major pass of a depth-stitch plan: one CTA per <= 1024-observation chunk of one
 // image, thread per observation (the next batch's inputs loaded ahead); the image's zcf
 // block, gradient and diag(A) summed per thread, then over the CTA, one atomic per value.
-template <int CT>
+template <int CT, bool OBJ>
 __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restrict__ S, float* __restrict__ b,
                                                          float* __restrict__ diagA) {
   constexpr int NZZ = CT * (CT + 1) / 2, NV = NZZ + 2 * CT, R = zrec_floats<CT>();
@@ -1114,19 +1111,18 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
     if (e >= ee) continue;
     ObsView<CT> V;
     float es;
-    view_in<CT>(c, cur, img, cam, zc, V, es);
-    err_acc += es;
+    view_in<CT, OBJ>(c, cur, img, cam, zc, V, es);
+    if (OBJ) err_acc += es;
     const float zw = V.Jcw[26];
     const float d = zw * zw;
     float a = d, g = zw * V.sWr[2];
-    if (cur.ix.y >= 0) {                          // eliminated track: record y, subtract y.y and Hcp delta
+    if (cur.ix.y >= 0) {                          // eliminated track: record y, subtract y.y, y.z
       const float h0 = V.Jpw[6] * zw, h1 = V.Jpw[7] * zw, h2 = V.Jpw[8] * zw;
       const float y0 = h0 * cur.tf0.x;
       const float y1 = (h1 - cur.tf0.y * y0) * cur.tf0.w;
       const float y2 = (h2 - cur.tf0.z * y0 - cur.tf1.x * y1) * cur.tf1.y;
       a = fmaf(-y2, y2, fmaf(-y1, y1, fmaf(-y0, y0, a)));
-      // Hcp delta = zw (Jpw[2] . delta), delta = Hpp^-1 g_p
-      g -= zw * fmaf(V.Jpw[8], cur.tf2.w, fmaf(V.Jpw[7], cur.tf2.z, V.Jpw[6] * cur.tf2.y));
+      g = fmaf(-y2, cur.tf2.x, fmaf(-y1, cur.tf1.w, fmaf(-y0, cur.tf1.z, g)));
       float rv[R];
       rv[0] = y0; rv[1] = y1; rv[2] = y2;
 #pragma unroll
@@ -1153,12 +1149,12 @@ __global__ void __launch_bounds__(kDiagZThreads) k_diag_z(Ctx c, float* __restri
     if (lane == 0) red[warp][v] = t;
   }
   __shared__ double esm[NW];
-  if (c.loss_part) {                              // the chunk's Huber-error sum (no atomics)
+  if (OBJ && c.loss_part) {                       // the chunk's Huber-error sum (no atomics)
     const double t = warp_sum_dbl((double)err_acc);
     if (lane == 0) esm[warp] = t;
   }
   __syncthreads();
-  if (c.loss_part && threadIdx.x == 0) {
+  if (OBJ && c.loss_part && threadIdx.x == 0) {
     double t = 0.0;
 #pragma unroll
     for (int w = 0; w < NW; ++w) t += esm[w];
@@ -1491,11 +1487,16 @@ int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) 
   const size_t smem = (size_t)(kDiagThreads / kWarp) * 32 * diag_row_stride<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
   if (!configured) {
-    B3R_TRY(check_cuda(cudaFuncSetAttribute(k_diag<CT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                       "diag smem attribute"));
+    B3R_TRY(check_cuda(cudaFuncSetAttribute(k_diag<CT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem), "diag smem attribute"));
+    B3R_TRY(check_cuda(cudaFuncSetAttribute(k_diag<CT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem), "diag smem attribute"));
     configured = true;
   }
-  k_diag<CT><<<c.d.n_c1_chunks, kDiagThreads, smem, s>>>(c, S, b, diagA);
+  if (c.res_out || c.loss_part)
+    k_diag<CT, true><<<c.d.n_c1_chunks, kDiagThreads, smem, s>>>(c, S, b, diagA);
+  else
+    k_diag<CT, false><<<c.d.n_c1_chunks, kDiagThreads, smem, s>>>(c, S, b, diagA);
   return check_launch("diag pass");
 }
 
@@ -1515,7 +1516,10 @@ int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
 template <int CT>
 int diag_z_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) {
   if constexpr (CT <= kZonlyMaxC) {
-    k_diag_z<CT><<<c.d.n_c1_chunks, kDiagZThreads, 0, s>>>(c, S, b, diagA);
+    if (c.res_out || c.loss_part)
+      k_diag_z<CT, true><<<c.d.n_c1_chunks, kDiagZThreads, 0, s>>>(c, S, b, diagA);
+    else
+      k_diag_z<CT, false><<<c.d.n_c1_chunks, kDiagZThreads, 0, s>>>(c, S, b, diagA);
     return check_launch("diag pass (depth-stitch)");
   } else {
     return fail(B3R_E_INVALID, "internal: depth-stitch kernels for C=%d", CT);

@@ -300,9 +300,12 @@ int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
  * stopping at the first iterate with ||r|| <= tol ||b|| (converged, returned), breaking on a
  * non-finite r.z, else returning the best-so-far iterate after maxiter iterations.  One
  * cooperative kernel runs the whole loop on `stream`, in the pipelined form of the
- * iteration (one grid-wide barrier per iteration; every barrier wait is bounded).  `work` is a 256-byte aligned device
- * buffer of b3r_pcg_work_bytes(plan) bytes; `result` is a device int[3] receiving
- * (iterations, converged, device error) -- read it after synchronising the stream.
+ * iteration (one grid-wide barrier per iteration; every wait is bounded); a stop is taken
+ * only when the true residual b - S x meets the tolerance (if the recurrences' residual
+ * has drifted, the iteration continues from true values).  `work` is a 256-byte aligned device
+ * buffer of b3r_pcg_work_bytes(plan) bytes; `result` is a device int[4] receiving
+ * (iterations, converged, device error, residual replacements) -- read it after
+ * synchronising the stream.
  * b3r_pcg uses float vectors, b3r_pcg_f64 double vectors; S stays float either way.
  * Replaces the reference's per-iteration Python loop; no counterpart in its native ops. */
 int64_t b3r_pcg_work_bytes(const b3r_plan* plan);
