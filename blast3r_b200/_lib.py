@@ -15,6 +15,8 @@ ENABLE_ALL, ENABLE_ZERO, ENABLE_MASK = 0, 1, 2
 PASS_PREP, PASS_POINTS, PASS_FACTOR, PASS_DIAG, PASS_PAIRS = 0, 1, 2, 3, 4
 PASS_ELIMINATE = PASS_FACTOR   # former name
 PCG_TEST_UNREACHABLE_BARRIER = 1
+PCG_STREAMING = 2
+PCG_TEST_GLOBAL_TILES = 4
 
 _i32, _i64, _f32, _f64, _vp = C.c_int32, C.c_int64, C.c_float, C.c_double, C.c_void_p
 _pi32 = C.POINTER(C.c_int32)
@@ -37,7 +39,8 @@ class PlanInfo(C.Structure):
                 ('n_pair_tasks', _i64), ('n_point_tasks', _i64), ('n_diag_chunks', _i64),
                 ('workspace_bytes', _i64), ('nb_K', _i32), ('nb_P', _i32), ('nb_Z', _i32),
                 ('off_P', _i32), ('off_Z', _i32), ('record_floats', _i32), ('n_obs_input', _i64),
-                ('depth_stitch', _i32)]
+                ('depth_stitch', _i32), ('pcg_row_groups', _i32),
+                ('pcg_resident', _i32)]
 
 
 class Params(C.Structure):

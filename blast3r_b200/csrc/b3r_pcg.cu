@@ -108,15 +108,15 @@ __device__ __forceinline__ bool grid_barrier(PcgWords* w, unsigned int* flags, u
   }
   __syncthreads();
   if (blockIdx.x == 0) {
-    // each thread polls its (up to kPcgMaxBlocks / kPcgThreads) flags with loads issued
-    // together, so a thread's second flag costs no extra round trip
+    // each thread polls its (up to kPcgMaxBlocks / kPcgThreads, blockDim.x >= kPcgThreads)
+    // flags with loads issued together, so a thread's second flag costs no extra round trip
     constexpr int kPer = kPcgMaxBlocks / kPcgThreads;
     bool bad = false;
     for (int spins = 0;; ++spins) {
       unsigned int f[kPer];
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
-        const int b = threadIdx.x + j * kPcgThreads;
+        const int b = threadIdx.x + j * (int)blockDim.x;
         f[j] = b < (int)gridDim.x ? ld_acquire(flags + b) : target;
       }
       bool all = true;
@@ -320,7 +320,7 @@ __device__ __forceinline__ double3 block_sum3(double u, double v, double w, doub
   __syncthreads();
   double3 t = make_double3(0.0, 0.0, 0.0);
   if (threadIdx.x == 0)
-    for (int i = 0; i < kPcgThreads / 32; ++i) { t.x += red3[i].x; t.y += red3[i].y; t.z += red3[i].z; }
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { t.x += red3[i].x; t.y += red3[i].y; t.z += red3[i].z; }
   return t;
 }
 
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
     DevPlan d, const float* __restrict__ M, const TI* __restrict__ b, TI* __restrict__ xo, double tol, int maxiter,
     char* work, const float* __restrict__ pan, int* result, long long spin_limit, int test_flags) {
   __shared__ double slots[kPcgSrcMax][kPcgSlots];
-  __shared__ double3 red3[kPcgThreads / 32];
+  __shared__ double3 red3[kResWarps];
   __shared__ double3 bc3;
   PcgWords* wd = reinterpret_cast<PcgWords*>(work);
   unsigned int* flags = reinterpret_cast<unsigned int*>(work + kPcgFlagsOff);
@@ -495,6 +495,376 @@ __global__ void __launch_bounds__(kPcgThreads, kPcgBlocksPerSm) k_pcg(
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// The resident kernel: the same iteration, row groups and stopping rule as k_pcg, laid out for
+// latency.  One block of kResThreads threads per SM and one row group per block.  The group's
+// panel tiles and column lists are copied into shared memory once per solve (tasks that do not
+// fit read the panel in global memory), and scalar j of the group lives in registers of thread
+// j - (first scalar), so the only global traffic of an iteration is the gather of the previous
+// m = M^-1 w by the panel columns, this block's new m, its partial sums and the barrier.  x,
+// u, p and q are written to global memory only when the true residual is checked (the
+// verification matvec reads x, the replacement matvecs read u, p, q).
+
+struct ResTask {
+  long long pbase;   // global panel: float index of the task's row 0, column c0
+  int W;             // global panel row stride
+  int cbase;         // global column list: index of the task's column c0
+  int soff;          // word offset of the tile (bp x len, row-major) and columns in shared memory, -1: global
+  int len, bp, slot;
+};
+
+// Sum over the warp of eight per-lane values: a reduce-scatter in nine shuffles.  Lane l ends
+// with the sum of y[((l >> 4) & 1) * 4 + ((l >> 3) & 1) * 2 + ((l >> 2) & 1)].
+__device__ __forceinline__ double warp_rsum8(const double (&y)[8], int lane) {
+  double a[4], b2[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const double keep = h16 ? y[i + 4] : y[i], send = h16 ? y[i] : y[i + 4];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const double keep = h8 ? a[i + 2] : a[i], send = h8 ? a[i] : a[i + 2];
+    b2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  double c = (h4 ? b2[1] : b2[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b2[0] : b2[1], 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
+// The group's matvec over one source vector: warp w takes tasks w, w + 16, ..., two at a time
+// with the source values of both gathered before either is multiplied; every task's partial
+// row sums go to its shared-memory slots.
+template <typename TS, bool DIV>
+__device__ __forceinline__ void res_matvec(const ResTask* tasks, int ntask, const float* sm,
+                                           const float* __restrict__ pan, const int* __restrict__ pan_col,
+                                           const TS* __restrict__ src, const float* __restrict__ M, double* slots) {
+  constexpr int CPL = kMvCols / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t0 = warp; t0 < ntask; t0 += 2 * kResWarps) {
+    double xc[2][CPL];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = t0 + hh * kResWarps;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) xc[hh][j] = 0.0;
+      if (t >= ntask) continue;
+      const ResTask tk = tasks[t];
+      const int* cols = tk.soff >= 0 ? reinterpret_cast<const int*>(sm + tk.soff + tk.bp * tk.len) : pan_col + tk.cbase;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < tk.len) {
+          const int col = cols[c];
+          xc[hh][j] = DIV ? (double)src[col] / (double)__ldg(M + col) : (double)__ldcg(src + col);
+        }
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = t0 + hh * kResWarps;
+      if (t >= ntask) continue;
+      const ResTask tk = tasks[t];
+      const float* P = tk.soff >= 0 ? sm + tk.soff : pan + tk.pbase;
+      const int stride = tk.soff >= 0 ? tk.len : tk.W;
+      double y[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) y[r] = 0.0;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c >= tk.len) continue;
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          if (r < tk.bp) y[r] += (double)P[r * stride + c] * xc[hh][j];
+      }
+      const double v = warp_rsum8(y, lane);
+      const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+      if ((lane & 3) == 0 && row < tk.bp) slots[tk.slot + row] = v;
+    }
+  }
+}
+
+struct ResGroup {
+  int4 g, h;          // pcg_grp, pcg_grp2 of the block's group
+  int ntask;
+  bool helper, own;   // a helper group; this thread owns scalar g.z + threadIdx.x
+  int2 sc;            // the owned scalar's slot map
+};
+
+// One matvec pass of the resident kernel: (S v)_j for the scalar this thread owns (0 for the
+// others).  Helper groups publish their row sums (source slot sv of their helper record) with a
+// release store of gen; the owner of a split row adds them, in helper order, after a bounded
+// acquire poll.
+template <typename TS, bool DIV>
+__device__ __forceinline__ double res_pass(const DevPlan& d, const ResGroup& rg, const ResTask* tasks, const float* sm,
+                                           const float* __restrict__ pan, const TS* __restrict__ src,
+                                           const float* __restrict__ M, double* slots, const HelpCfg& hc, int sv,
+                                           unsigned int gen, bool& ok, int* wait_ok) {
+  res_matvec<TS, DIV>(tasks, rg.ntask, sm, pan, d.pan_col, src, M, slots);
+  __syncthreads();
+  double y = 0.0;
+  if (rg.helper) {
+    const int bp = rg.h.w, nt = rg.h.x;
+    if ((int)threadIdx.x < bp) {
+      double v = 0.0;
+      for (int t = 0; t < nt; ++t) v += slots[t * bp + threadIdx.x];
+      hc.sums[((int64_t)rg.h.z * kPcgSrcMax + sv) * 32 + threadIdx.x] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) st_release(hc.flags + rg.h.z, gen);
+  } else {
+    if (rg.h.y > 0) {                                  // the owner of a split row waits for its helpers
+      if (threadIdx.x == 0) *wait_ok = 1;
+      __syncthreads();
+      if ((int)threadIdx.x < rg.h.y) {
+        long long spins = 0;
+        while (ld_acquire(hc.flags + rg.h.x + threadIdx.x) < gen) {
+          if (++spins > hc.spins) { *wait_ok = 0; break; }
+          __nanosleep(32);
+        }
+      }
+      __syncthreads();
+      if (!*wait_ok) ok = false;
+    }
+    if (rg.own) {
+      const int nt = rg.sc.y & 0xffff, stride = rg.sc.y >> 16;
+      for (int t = 0; t < nt; ++t) y += slots[rg.sc.x + t * stride];
+      for (int i = 0; i < rg.h.y; ++i)
+        y += __ldcg(hc.sums + ((int64_t)(rg.h.x + i) * kPcgSrcMax + sv) * 32 + threadIdx.x);
+    }
+  }
+  __syncthreads();                                     // the slots are reused by the next pass
+  return y;
+}
+
+template <typename TI>
+__global__ void __launch_bounds__(kResThreads, 1) k_pcg_res(
+    DevPlan d, const float* __restrict__ M, const TI* __restrict__ b, TI* __restrict__ xo, double tol, int maxiter,
+    char* work, const float* __restrict__ pan, int* result, long long spin_limit, int test_flags) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ double slots[kPcgSlots];
+  __shared__ ResTask tasks[kPcgGroupTasks];
+  __shared__ double3 red3[kResWarps];
+  __shared__ double3 bc3;
+  __shared__ int wait_ok;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  ResGroup rg;
+  rg.g = __ldg(d.pcg_grp + blockIdx.x);
+  rg.h = __ldg(d.pcg_grp2 + blockIdx.x);
+  rg.ntask = rg.g.y - rg.g.x;
+  rg.helper = rg.h.z >= 0;
+  const int j = rg.g.z + threadIdx.x;                  // the scalar this thread owns
+  rg.own = !rg.helper && j < rg.g.w;
+  rg.sc = rg.own ? __ldg(d.pcg_scl + j) : make_int2(0, 0);
+  // the group's task records, then its tiles and column lists
+  for (int t = threadIdx.x; t < rg.ntask; t += blockDim.x) {
+    const int4 tk = __ldg(d.mv_task + rg.g.x + t), rw = __ldg(d.mv_row + rg.g.x + t);
+    ResTask r;
+    r.pbase = 4LL * rw.z + tk.y;
+    r.W = rw.y;
+    r.cbase = rw.w + tk.y;
+    r.soff = (test_flags & B3R_PCG_TEST_GLOBAL_TILES) ? -1 : __ldg(d.mv_soff + rg.g.x + t);
+    r.len = tk.z - tk.y;
+    r.bp = tk.w >> 8;
+    r.slot = __ldg(d.mv_slot + rg.g.x + t);
+    tasks[t] = r;
+  }
+  __syncthreads();
+  for (int t = warp; t < rg.ntask; t += kResWarps) {
+    const ResTask r = tasks[t];
+    if (r.soff < 0) continue;
+    for (int rr = 0; rr < r.bp; ++rr)
+      for (int c = lane; c < r.len; c += 32) sm[r.soff + rr * r.len + c] = __ldg(pan + r.pbase + (int64_t)rr * r.W + c);
+    int* cs = reinterpret_cast<int*>(sm + r.soff + r.bp * r.len);
+    for (int c = lane; c < r.len; c += 32) cs[c] = __ldg(d.pan_col + r.cbase + c);
+  }
+  __syncthreads();
+
+  PcgWords* wd = reinterpret_cast<PcgWords*>(work);
+  unsigned int* flags = reinterpret_cast<unsigned int*>(work + kPcgFlagsOff);
+  PcgPart* part = reinterpret_cast<PcgPart*>(work + kPcgPartOff);
+  const HelpCfg hc{reinterpret_cast<unsigned int*>(work + kPcgHelpOff),
+                   reinterpret_cast<double*>(work + pcg_hsum_off(d)), spin_limit};
+  double* vec = reinterpret_cast<double*>(work + pcg_vec_off(d));
+  const int64_t n = d.n_cam_params;
+  double* const mb0 = vec;             // m = M^-1 w by iteration parity (read by every block)
+  double* const mb1 = vec + n;
+  double* xg = vec + 2 * n;            // x, u, p, q published for the true-residual check
+  double* ug = vec + 3 * n;
+  double* pg = vec + 4 * n;
+  double* qg = vec + 5 * n;
+  BarrierCfg bcfg{spin_limit, (test_flags & B3R_PCG_TEST_UNREACHABLE_BARRIER) != 0};
+  unsigned int target = 0, gen = 0;
+  bool ok = true;
+  auto publish = [&](double a, double b2, double c) {
+    const double3 t = block_sum3(a, b2, c, red3);
+    if (threadIdx.x == 0) { part[blockIdx.x].v[0] = t.x; part[blockIdx.x].v[1] = t.y; part[blockIdx.x].v[2] = t.z; }
+  };
+  // the owned scalar's elements of b, M and of the iteration's vectors
+  const double bj = rg.own ? (double)b[j] : 0.0, Mj = rg.own ? (double)M[j] : 1.0;
+  double xj = 0.0, rj = bj, uj = bj / Mj, wj = 0.0, zj = 0.0, qj = 0.0, sj = 0.0, pj = 0.0, bxj = 0.0, mj = 0.0;
+
+  // prologue: w0 = S u0, m0 = M^-1 w0, and the partial sums of r0.u0, w0.u0, b.b
+  double s_g = 0.0, s_d = 0.0, s_bb = 0.0;
+  {
+    const double y = res_pass<TI, true>(d, rg, tasks, sm, pan, b, M, slots, hc, 0, ++gen, ok, &wait_ok);
+    if (rg.own) {
+      wj = y;
+      mj = wj / Mj;
+      mb0[j] = mj;
+      s_g = bj * uj;
+      s_d = wj * uj;
+      s_bb = bj * bj;
+    }
+  }
+  publish(s_g, s_d, s_bb);
+  ok = grid_barrier(wd, flags, ++target, bcfg, ok);
+  double3 t3 = grid_sum3(part, red3, &bc3);
+  double gamma = t3.x, delta = t3.y;
+  const double bnorm = fmax(sqrt(t3.z), 1e-12);
+  double rn = sqrt(t3.z), gamma_old = 0.0, alpha_old = 1.0;
+
+  double best = __longlong_as_double(0x7ff0000000000000LL);   // +inf
+  int best_k = 0, k_stop = 0, replaced = 0;
+  bool converged = false;
+  for (int k = 1; ok && k <= maxiter + 1; ++k) {
+    // ---- decisions on iterate k-1 (identical in every thread) ----
+    if (k > 1) {
+      if (rn <= tol * bnorm) {
+        // confirm with the true residual r = b - S x; if it misses the tolerance, continue
+        // from true values: u = M^-1 r, w = S u, s = S p, z = S q, m = M^-1 w
+        if (rg.own) xg[j] = xj;
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
+        double s_rr = 0.0;
+        {
+          const double y = res_pass<double, false>(d, rg, tasks, sm, pan, xg, M, slots, hc, 0, ++gen, ok, &wait_ok);
+          if (rg.own) {
+            rj = bj - y;
+            uj = rj / Mj;
+            s_rr = rj * rj;
+            ug[j] = uj;
+            pg[j] = pj;
+            qg[j] = qj;
+          }
+        }
+        publish(0.0, 0.0, s_rr);
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
+        t3 = grid_sum3(part, red3, &bc3);
+        rn = sqrt(t3.z);
+        if (rn <= tol * bnorm) { converged = true; k_stop = k - 1; break; }
+        ++replaced;
+        const double yu = res_pass<double, false>(d, rg, tasks, sm, pan, ug, M, slots, hc, 0, ++gen, ok, &wait_ok);
+        const double yp = res_pass<double, false>(d, rg, tasks, sm, pan, pg, M, slots, hc, 1, ++gen, ok, &wait_ok);
+        const double yq = res_pass<double, false>(d, rg, tasks, sm, pan, qg, M, slots, hc, 2, ++gen, ok, &wait_ok);
+        s_g = 0.0; s_d = 0.0;
+        if (rg.own) {
+          wj = yu;
+          sj = yp;
+          zj = yq;
+          mj = wj / Mj;
+          ((k - 1) & 1 ? mb1 : mb0)[j] = mj;
+          s_g = rj * uj;
+          s_d = wj * uj;
+        }
+        publish(s_g, s_d, 0.0);
+        if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
+        t3 = grid_sum3(part, red3, &bc3);
+        gamma = t3.x;
+        delta = t3.y;
+      }
+      if (rn < best) {                                   // best-so-far iterate
+        best = rn;
+        best_k = k - 1;
+        bxj = xj;
+      }
+      if (!isfinite(gamma)) break;                       // the reference's r.z
+    }
+    if (k > maxiter) break;
+    // ---- iteration k-1 of the pipelined recurrences ----
+    const double beta = k > 1 ? gamma / fmax(gamma_old, 1e-32) : 0.0;
+    const double den = k > 1 ? delta - beta * gamma / alpha_old : delta;   // = p.S p
+    const double alpha = gamma / fmax(den, 1e-32);
+    double s_rr = 0.0;
+    s_g = 0.0; s_d = 0.0;
+    {
+      const double nj = res_pass<double, false>(d, rg, tasks, sm, pan, (k - 1) & 1 ? mb1 : mb0, M, slots, hc, 0, ++gen, ok,
+                                                &wait_ok);
+      if (rg.own) {
+        zj = nj + beta * zj;
+        qj = mj + beta * qj;
+        sj = wj + beta * sj;
+        pj = uj + beta * pj;
+        xj += alpha * pj;
+        rj -= alpha * sj;
+        uj -= alpha * qj;
+        wj -= alpha * zj;
+        mj = wj / Mj;
+        (k & 1 ? mb1 : mb0)[j] = mj;
+        s_g = rj * uj;
+        s_d = wj * uj;
+        s_rr = rj * rj;
+      }
+    }
+    publish(s_g, s_d, s_rr);
+    if (!(ok = grid_barrier(wd, flags, ++target, bcfg, ok))) break;
+    t3 = grid_sum3(part, red3, &bc3);
+    gamma_old = gamma;
+    alpha_old = alpha;
+    gamma = t3.x;
+    delta = t3.y;
+    rn = sqrt(t3.z);
+  }
+  // the converging iterate, else the best-so-far one (zeros if none improved or a wait gave up)
+  if (rg.own) xo[j] = ok ? (TI)(converged ? xj : bxj) : TI(0);
+  if (!ok && threadIdx.x == 0) atomicOr(result + 2, 1);   // any block that gave up flags the solve
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    result[0] = converged ? k_stop : best_k;
+    result[1] = converged ? 1 : 0;
+    result[3] = replaced;
+  }
+}
+
+template <typename T>
+int pcg_res_launch(const b3r_plan* plan, const float* S, const float* M, const T* b, T* xo, double tol, int maxiter,
+                   long long spin_limit, int test_flags, void* work, int* result, cudaStream_t s) {
+  const DevPlan& d = plan->d;
+  constexpr int kSmem = kResSmemWords * 4;
+  static int per_sm = 0, n_sm = 0;         // one attribute set and occupancy query per instantiation
+  if (per_sm == 0) {
+    int dev = 0;
+    B3R_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+    B3R_TRY(check_cuda(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev), "SM count"));
+    B3R_TRY(check_cuda(cudaFuncSetAttribute((const void*)k_pcg_res<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kSmem),
+                       "resident PCG shared memory"));
+    B3R_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pcg_res<T>, kResThreads, kSmem),
+                       "resident PCG occupancy"));
+    B3R_REQUIRE(per_sm >= 1, "the resident PCG kernel does not fit on an SM");
+  }
+  const int grid = d.n_pcg_groups;                          // one block per row group, all co-resident
+  B3R_REQUIRE(grid >= 1 && grid <= per_sm * n_sm && grid <= kPcgMaxBlocks, "internal: resident PCG grid %d", grid);
+  B3R_TRY(check_cuda(cudaMemsetAsync(work, 0, kPcgPartOff, s), "clear PCG barrier words"));
+  if (d.n_pcg_help > 0)
+    B3R_TRY(check_cuda(cudaMemsetAsync((char*)work + kPcgHelpOff, 0, 4 * (size_t)d.n_pcg_help, s),
+                       "clear PCG helper flags"));
+  B3R_TRY(check_cuda(cudaMemsetAsync(result, 0, 4 * sizeof(int), s), "clear PCG result"));
+  DevPlan dv = d;
+  char* wk = reinterpret_cast<char*>(work);
+  float* pan = reinterpret_cast<float*>(wk + pcg_panel_off(d));
+  const int n_ent = (int)(2 * d.nnzb - d.nb);
+  k_build_panels<<<grid_for((int64_t)n_ent * 32, 256), 256, 0, s>>>(dv, S, pan);
+  B3R_TRY(check_launch("pcg panels"));
+  const float* panc = pan;
+  void* args[] = {&dv, &M, &b, &xo, &tol, &maxiter, &wk, &panc, &result, &spin_limit, &test_flags};
+  B3R_TRY(check_cuda(cudaLaunchCooperativeKernel((const void*)k_pcg_res<T>, dim3(grid), dim3(kResThreads), args,
+                                                 kSmem, s),
+                     "resident pcg cooperative launch"));
+  return B3R_OK;
+}
+
 template <typename T, int MAXB>
 int pcg_launch(const b3r_plan* plan, const float* S, const float* M, const T* b, T* xo, double tol, int maxiter,
                long long spin_limit, int test_flags, void* work, int* result, cudaStream_t s) {
@@ -540,7 +910,8 @@ int pcg_impl(const b3r_plan* plan, const float* S, const float* M, const T* b, T
   B3R_REQUIRE(((uintptr_t)work & 255) == 0, "PCG work buffer must be 256-byte aligned");
   B3R_REQUIRE(maxiter >= 0, "maxiter must be >= 0");
   B3R_REQUIRE(spin_limit >= 1, "the barrier spin limit must be >= 1");
-  B3R_REQUIRE((flags & ~B3R_PCG_TEST_UNREACHABLE_BARRIER) == 0, "unknown PCG flags %d", flags);
+  B3R_REQUIRE((flags & ~(B3R_PCG_TEST_UNREACHABLE_BARRIER | B3R_PCG_STREAMING | B3R_PCG_TEST_GLOBAL_TILES)) == 0,
+              "unknown PCG flags %d", flags);
   int dev = -1;
   B3R_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   B3R_REQUIRE(dev == plan->device, "current device %d differs from the plan's device %d", dev, plan->device);
@@ -548,6 +919,8 @@ int pcg_impl(const b3r_plan* plan, const float* S, const float* M, const T* b, T
   int maxb = 0;
   for (int v : plan->pat.bsize) maxb = std::max(maxb, v);
   cudaStream_t s = as_stream(stream);
+  if (plan->d.pcg_resident && !(flags & B3R_PCG_STREAMING))
+    return pcg_res_launch<T>(plan, S, M, b, xo, tol, maxiter, spin_limit, flags, work, result, s);
   if (maxb <= 8) return pcg_launch<T, 8>(plan, S, M, b, xo, tol, maxiter, spin_limit, flags, work, result, s);
   B3R_REQUIRE(maxb <= 32, "block size %d > 32", maxb);
   return pcg_launch<T, 32>(plan, S, M, b, xo, tol, maxiter, spin_limit, flags, work, result, s);

@@ -109,7 +109,9 @@ struct PlanBuild {
   int n_pcg_help = 0;
   std::vector<int> mv_slot;
   std::vector<int2> pcg_scl;
-  int pcg_target_groups = 444;
+  std::vector<int> mv_soff;
+  int pcg_target_groups = 148;   // SMs of the plan's device (a B200's without one)
+  int pcg_resident = 0;
   std::vector<int64_t> pan_off;
   std::vector<int> pan_w, col_off, pan_col, ent_col, ent_row;
   int64_t pan_floats = 0;
@@ -579,66 +581,126 @@ static int build_pattern(PlanBuild& B) {
       }
     }
     B.pan_floats = poff;
-    // PCG row groups: cut the block rows into contiguous groups of about total / target
-    // panel work, at most kPcgSlots task-row sums each.  A row heavier than 1.5 targets (the
-    // focal row of a mono camera couples to every block) is split by its tasks into an owner
-    // group and helper groups on other blocks: helpers publish their partial row sums, the
-    // owner adds them (in helper order) before it updates the row.
+    // PCG row groups, at most one per SM: the resident PCG kernel runs one block per SM,
+    // holding its group's panel tiles in shared memory and its scalars in registers.  Rows are
+    // packed into contiguous groups of at most X work ((bp + 1) W words: the panel and its
+    // column list), kPcgGroupTasks tasks, kPcgSlots task-row sums and kResThreads scalars.  A
+    // row above the cap (the focal row of a mono camera couples to every block) is split by
+    // its tasks into an owner group and helper groups on other blocks: helpers publish their
+    // partial row sums, the owner adds them (in helper order) before it updates the row.
+    const int G = std::max(1, B.pcg_target_groups);
     int64_t total = 0;
-    for (int pr = 0; pr < nb; ++pr) total += (int64_t)B.bsize[pr] * B.pan_w[pr];
-    const int64_t target = std::max<int64_t>(1, total / std::max(1, B.pcg_target_groups));
+    auto work_of = [&](int pr) { return (int64_t)(B.bsize[pr] + 1) * B.pan_w[pr]; };
+    for (int pr = 0; pr < nb; ++pr) total += work_of(pr);
+    auto n_tasks_of = [&](int pr) { return (B.pan_w[pr] + kMvCols - 1) / kMvCols; };
+    // Greedy packing under a cap X on a group's work (optimal in the number of groups for
+    // contiguous groups); a row above the cap is split into ceil(w / X) parts by its tasks.
+    // The smallest cap that needs at most G groups is found by bisection.
     B.mv_slot.assign(B.mv_task.size(), 0);
     const int ncp_all = nb ? B.boff[nb - 1] + B.bsize[nb - 1] : 0;
     B.pcg_scl.assign(ncp_all, make_int2(0, 0));
     int task0 = 0, n_help = 0;
-    for (int pr = 0; pr < nb;) {
-      const int nt0 = (B.pan_w[pr] + kMvCols - 1) / kMvCols;
-      const int64_t w0 = (int64_t)B.bsize[pr] * B.pan_w[pr];
-      const int bp0 = B.bsize[pr];
-      if (w0 > target + target / 2 && nt0 > 1) {
-        const int parts = (int)std::min<int64_t>(nt0, std::max<int64_t>((w0 + target - 1) / target,
-                                                                        (nt0 + kPcgWarps - 1) / kPcgWarps));
-        const int first_help = n_help;
-        for (int part = 0; part < parts; ++part) {
-          const int tb = task0 + (int)((int64_t)nt0 * part / parts), te = task0 + (int)((int64_t)nt0 * (part + 1) / parts);
-          for (int t = tb; t < te; ++t) B.mv_slot[t] = (t - tb) * bp0;
-          if (part == 0) {
-            for (int r = 0; r < bp0; ++r) B.pcg_scl[B.boff[pr] + r] = make_int2(r, (te - tb) | (bp0 << 16));
-            B.pcg_grp.push_back(make_int4(tb, te, B.boff[pr], B.boff[pr] + bp0));
-            B.pcg_grp2.push_back(make_int4(first_help, parts - 1, -1, bp0));
-          } else {
-            B.pcg_grp.push_back(make_int4(tb, te, 0, 0));
-            B.pcg_grp2.push_back(make_int4(te - tb, 0, n_help++, bp0));   // helper: its task count, slot
+    int g_t0 = -1, g_slots = 0, g_sc0 = 0, g_sc1 = 0, n_groups = 0;
+    int64_t g_work = 0;
+    bool emit = false;
+    auto close_group = [&]() {
+      if (g_t0 < 0) return;
+      ++n_groups;
+      if (emit) {
+        B.pcg_grp.push_back(make_int4(g_t0, task0, g_sc0, g_sc1));
+        B.pcg_grp2.push_back(make_int4(0, 0, -1, 0));
+      }
+      g_t0 = -1;
+      g_slots = 0;
+      g_work = 0;
+    };
+    auto parts_of = [&](int pr, int64_t X) -> int {    // > 1: a split row
+      const int nt = n_tasks_of(pr);
+      const int64_t w = work_of(pr);
+      const int by_caps = std::max((nt * B.bsize[pr] + kPcgSlots - 9) / (kPcgSlots - 8),   // ceil(nt / parts) tasks fit
+                                   (nt + kPcgGroupTasks - 1) / kPcgGroupTasks);
+      if (nt <= 1 || (w <= X && by_caps <= 1)) return 1;
+      return (int)std::min<int64_t>(nt, std::max<int64_t>((w + X - 1) / X, by_caps));
+    };
+    auto pack = [&](int64_t X) {
+      task0 = 0; n_help = 0; g_t0 = -1; g_slots = 0; g_work = 0; n_groups = 0;
+      for (int pr = 0; pr < nb; ++pr) {
+        const int nt0 = n_tasks_of(pr), bp0 = B.bsize[pr];
+        const int parts = parts_of(pr, X);
+        if (parts > 1) {
+          close_group();
+          const int first_help = n_help;
+          for (int part = 0; part < parts; ++part) {
+            const int tb = task0 + (int)((int64_t)nt0 * part / parts), te = task0 + (int)((int64_t)nt0 * (part + 1) / parts);
+            ++n_groups;
+            if (!emit) { if (part > 0) ++n_help; continue; }
+            for (int t = tb; t < te; ++t) B.mv_slot[t] = (t - tb) * bp0;
+            if (part == 0) {
+              for (int r = 0; r < bp0; ++r) B.pcg_scl[B.boff[pr] + r] = make_int2(r, (te - tb) | (bp0 << 16));
+              B.pcg_grp.push_back(make_int4(tb, te, B.boff[pr], B.boff[pr] + bp0));
+              B.pcg_grp2.push_back(make_int4(first_help, parts - 1, -1, bp0));
+            } else {
+              B.pcg_grp.push_back(make_int4(tb, te, 0, 0));
+              B.pcg_grp2.push_back(make_int4(te - tb, 0, n_help++, bp0));   // helper: its task count, slot
+            }
           }
+          task0 += nt0;
+          continue;
         }
-        B3R_REQUIRE(nt0 * bp0 <= kPcgSlots * kPcgWarps, "internal: PCG row of %d tasks", nt0);
+        const int64_t w = work_of(pr);
+        if (g_t0 >= 0 && (g_work + w > X || (task0 - g_t0) + nt0 > kPcgGroupTasks || g_slots + nt0 * bp0 > kPcgSlots ||
+                          B.boff[pr] + bp0 - g_sc0 > kResThreads))
+          close_group();
+        if (g_t0 < 0) { g_t0 = task0; g_sc0 = B.boff[pr]; }
+        if (emit) {
+          for (int t = 0; t < nt0; ++t) B.mv_slot[task0 + t] = g_slots + t * bp0;
+          for (int r = 0; r < bp0; ++r) B.pcg_scl[B.boff[pr] + r] = make_int2(g_slots + r, nt0 | (bp0 << 16));
+        }
+        g_slots += nt0 * bp0;
+        g_sc1 = B.boff[pr] + bp0;
+        g_work += w;
         task0 += nt0;
-        ++pr;
-        continue;
       }
-      int slots = 0, t_begin = task0;
-      int64_t work = 0;
-      const int sc_begin = B.boff[pr];
-      int q = pr;
-      for (; q < nb; ++q) {
-        const int nt = (B.pan_w[q] + kMvCols - 1) / kMvCols;
-        const int64_t wq = (int64_t)B.bsize[q] * B.pan_w[q];
-        if (q > pr && (work + wq > target || slots + nt * B.bsize[q] > kPcgSlots ||
-                       wq > target + target / 2)) break;
-        for (int t = 0; t < nt; ++t) B.mv_slot[task0 + t] = slots + t * B.bsize[q];
-        for (int r = 0; r < B.bsize[q]; ++r) B.pcg_scl[B.boff[q] + r] = make_int2(slots + r, nt | (B.bsize[q] << 16));
-        slots += nt * B.bsize[q];
-        work += wq;
-        task0 += nt;
+      close_group();
+      return n_groups;
+    };
+    int64_t lo = std::max<int64_t>(1, (total + G - 1) / G), hi = std::max<int64_t>(lo, total);
+    if (pack(hi) > G) {
+      lo = hi;                                        // no cap gets down to G groups: the streaming kernel
+    } else {
+      while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if (pack(mid) <= G) hi = mid; else lo = mid + 1;
       }
-      B3R_REQUIRE(slots <= kPcgSlots, "internal: PCG row group needs %d slots", slots);
-      B.pcg_grp.push_back(make_int4(t_begin, task0, sc_begin, B.boff[q - 1] + B.bsize[q - 1]));
-      B.pcg_grp2.push_back(make_int4(0, 0, -1, 0));
-      pr = q;
     }
+    emit = true;
+    pack(lo);
     B.n_pcg_help = n_help;
     B3R_REQUIRE(task0 == (int)B.mv_task.size(), "internal: PCG groups cover %d of %zu tasks", task0,
                 B.mv_task.size());
+    for (size_t gi = 0; gi < B.pcg_grp.size(); ++gi) {       // the kernels' shared-memory bounds
+      const int4 g = B.pcg_grp[gi];
+      for (int t = g.x; t < g.y; ++t)
+        B3R_REQUIRE(B.mv_slot[t] + (B.mv_task[t].w >> 8) <= kPcgSlots, "internal: PCG group %zu needs more than %d slots",
+                    gi, kPcgSlots);
+    }
+    // resident layout: each group's tasks take, in task order while they fit, (bp + 1) len
+    // words of their block's shared memory (the tile bp x len, row-major, then the columns)
+    B.mv_soff.assign(B.mv_task.size(), -1);
+    int maxb = 0;
+    for (int pr = 0; pr < nb; ++pr) maxb = std::max(maxb, B.bsize[pr]);
+    bool fits = (int)B.pcg_grp.size() <= G && maxb <= 8;
+    for (size_t gi = 0; gi < B.pcg_grp.size(); ++gi) {
+      const int4 g = B.pcg_grp[gi];
+      if (g.w - g.z > kResThreads || g.y - g.x > kPcgGroupTasks) fits = false;
+      int off = 0;
+      for (int t = g.x; t < g.y; ++t) {
+        const int4 tk = B.mv_task[t];
+        const int words = ((tk.w >> 8) + 1) * (tk.z - tk.y);
+        if (off + words <= kResSmemWords) { B.mv_soff[t] = off; off += words; }
+      }
+    }
+    B.pcg_resident = fits ? 1 : 0;
   }
   // every image's zcf diagonal block, also when the type is switched off (a dense prior can
   // still be added there)
@@ -707,7 +769,7 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   if (desc->device >= 0) {
     int n_sm = 0;
     if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, desc->device) == cudaSuccess && n_sm > 0)
-      B.pcg_target_groups = kPcgBlocksPerSm * n_sm;
+      B.pcg_target_groups = n_sm;
   }
   try {
     B3R_TRY(build_maps(B));
@@ -803,7 +865,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   A.add(B.mv_task, &d.mv_task); A.add(B.mv_row, &d.mv_row); A.add(B.mv_ent, &d.mv_ent);
   d.n_mv_tasks = (int)B.mv_task.size();
   A.add(B.pcg_grp, &d.pcg_grp); A.add(B.pcg_grp2, &d.pcg_grp2);
-  A.add(B.mv_slot, &d.mv_slot); A.add(B.pcg_scl, &d.pcg_scl);
+  A.add(B.mv_slot, &d.mv_slot); A.add(B.pcg_scl, &d.pcg_scl); A.add(B.mv_soff, &d.mv_soff);
+  d.pcg_resident = B.pcg_resident;
   d.n_pcg_groups = (int)B.pcg_grp.size();
   d.n_pcg_help = B.n_pcg_help;
   A.add(B.pan_off, &d.pan_off); A.add(B.pan_w, &d.pan_w); A.add(B.col_off, &d.col_off);
@@ -839,6 +902,8 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   I.record_floats = d.R;
   I.n_obs_input = d.n_in;
   I.depth_stitch = d.zonly;
+  I.pcg_row_groups = d.n_pcg_groups;
+  I.pcg_resident = d.pcg_resident;
   *out = P;
   return B3R_OK;
 }

@@ -25,8 +25,15 @@ constexpr int kImgRecFloats = 32;  // floats per per-image camera record
 constexpr int kMvCols = 256;       // max panel columns per matvec task (8 per lane)
 constexpr int kRestBlocks = 64;     // blocks of the objective pass over observations without an image-major entry
 constexpr int kPcgSlots = 1024;    // per-task partial row sums one PCG row group keeps in shared memory
-constexpr int kPcgBlocksPerSm = 3; // resident PCG blocks per SM the row groups are sized for
-constexpr int kPcgWarps = 8;       // warps of a PCG block
+constexpr int kPcgBlocksPerSm = 3; // blocks per SM of the streaming PCG kernel
+constexpr int kPcgWarps = 8;       // warps of a streaming PCG block
+// The resident PCG kernel: one block of kResWarps warps per SM and one row group per block,
+// the group's panel tiles and column lists in kResSmemWords words of shared memory, each of
+// its scalars (at most kResThreads) in the registers of one thread.
+constexpr int kResWarps = 16;
+constexpr int kResThreads = 32 * kResWarps;
+constexpr int kResSmemWords = 51200;   // 200 KiB
+constexpr int kPcgGroupTasks = 128;    // matvec tasks of a PCG row group
 
 // sub-block destination modes of a segment (2 bits each, 9 sub-blocks)
 constexpr int kModeNone = 0, kModeDirect = 1, kModeTrans = 2, kModeSym = 3;
@@ -132,6 +139,10 @@ struct DevPlan {
                           //  block size); helper: (tasks, 0, its helper slot, block size);
                           //  others (0, 0, -1, 0)
   const int* mv_slot;     // [n_mv_tasks] first shared-memory slot of the task's row sums
+  const int* mv_soff;     // [n_mv_tasks] resident kernel: word offset of the task's tile and
+                          //  column list in its block's shared memory, -1: read from the panel
+  int pcg_resident;       // 1: the row groups fit the resident kernel (one per SM, <= kResThreads
+                          //  scalars, block sizes <= 8)
   const int2* pcg_scl;    // [n_cam_params] (slot of the scalar's first task, the row's task
                           //  count | block size << 16): the scalar sums its tasks' slots in order
 };

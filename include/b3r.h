@@ -176,6 +176,10 @@ typedef struct {
     int32_t depth_stitch;             /* 1: only depth-coefficient blocks are active (focal
                                          and pose types off, C <= 8) and the linearization
                                          runs its depth-stitch passes                       */
+    int32_t pcg_row_groups;           /* row groups of the PCG (one per block)             */
+    int32_t pcg_resident;             /* 1: the PCG runs its resident kernel (one block per
+                                         SM holding its rows of S in shared memory), 0: the
+                                         streaming kernel (rows of S read from L2)          */
 } b3r_plan_info;
 
 /* Build the plan: image -> block maps, the track-sorted observation order, per-warp
@@ -300,7 +304,10 @@ int b3r_lin_finalize(b3r_plan* plan, const b3r_lin_opts* opts, void* workspace,
  * stopping at the first iterate with ||r|| <= tol ||b|| (converged, returned), breaking on a
  * non-finite r.z, else returning the best-so-far iterate after maxiter iterations.  One
  * cooperative kernel runs the whole loop on `stream`, in the pipelined form of the
- * iteration (one grid-wide barrier per iteration; every wait is bounded); a stop is taken
+ * iteration (one grid-wide barrier per iteration; every wait is bounded).  Where the plan's
+ * row groups fit (b3r_plan_info.pcg_resident) each SM's block keeps its rows of S in shared
+ * memory and its elements of the vectors in registers for the whole solve; else the rows of
+ * S are streamed from L2 every iteration.  A stop is taken
  * only when the true residual b - S x meets the tolerance (if the recurrences' residual
  * has drifted, the iteration continues from true values).  `work` is a 256-byte aligned device
  * buffer of b3r_pcg_work_bytes(plan) bytes; `result` is a device int[4] receiving
@@ -320,8 +327,13 @@ int b3r_pcg_f64(const b3r_plan* plan, const float* S_vals, const float* precond,
  * that runs out makes every block leave the kernel at that barrier or the next, x is zeroed
  * and result[2] = 1; the context stays usable.  flags: 0, or
  * B3R_PCG_TEST_UNREACHABLE_BARRIER, a test of that failure path in which the first barrier
- * waits for an arrival that no block makes. */
+ * waits for an arrival that no block makes, B3R_PCG_STREAMING, which runs the streaming
+ * kernel also where the resident one fits (both compute the same iteration), and
+ * B3R_PCG_TEST_GLOBAL_TILES, a test of the resident kernel's path for rows of S beyond its
+ * shared memory, taken here for every row. */
 #define B3R_PCG_TEST_UNREACHABLE_BARRIER 1
+#define B3R_PCG_STREAMING 2
+#define B3R_PCG_TEST_GLOBAL_TILES 4
 int b3r_pcg_ex(const b3r_plan* plan, const float* S_vals, const float* precond, const void* b, void* x, int dtype,
                double tol, int maxiter, int64_t barrier_spin_limit, int flags, void* work, int* result,
                void* stream);
