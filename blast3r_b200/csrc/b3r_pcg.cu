@@ -534,56 +534,92 @@ __device__ __forceinline__ double warp_rsum8(const double (&y)[8], int lane) {
   return c;
 }
 
-// The group's matvec over one source vector: warp w takes tasks w, w + 16, ..., two at a time
-// with the source values of both gathered before either is multiplied; every task's partial
-// row sums go to its shared-memory slots.
+// Source value of panel column col: v[col] (or v[col] / M[col] for the prologue's M^-1 b).
+template <typename TS, bool DIV>
+__device__ __forceinline__ double res_src(const TS* __restrict__ src, const float* __restrict__ M, int col) {
+  return DIV ? (double)src[col] / (double)__ldg(M + col) : (double)__ldcg(src + col);
+}
+
+// The source values a lane needs for one task.  A task in shared memory has its columns
+// padded to lenp = a multiple of 64 (padding: column 0 of the task, zero panel values); lane l
+// takes columns 2l, 2l + 1 of each 64-column step (xc[2 step], xc[2 step + 1]).  A task read
+// from the global panel: lane l takes columns l + 32 j (xc[j]).
+template <typename TS, bool DIV>
+__device__ __forceinline__ void res_gather(const ResTask& tk, const float* sm, const int* __restrict__ pan_col,
+                                           const TS* __restrict__ src, const float* __restrict__ M, int lane,
+                                           double (&xc)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) xc[j] = 0.0;
+  if (tk.soff >= 0) {
+    const int lenp = (tk.len + 63) & ~63;
+    const int2* cols = reinterpret_cast<const int2*>(sm + tk.soff + tk.bp * lenp);
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+      if (st * 64 >= lenp) break;
+      const int2 cc = cols[st * 32 + lane];
+      xc[2 * st] = res_src<TS, DIV>(src, M, cc.x);
+      xc[2 * st + 1] = res_src<TS, DIV>(src, M, cc.y);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = lane + 32 * j;
+      if (c < tk.len) xc[j] = res_src<TS, DIV>(src, M, __ldg(pan_col + tk.cbase + c));
+    }
+  }
+}
+
+// The row sums of one task into its slots: a shared-memory tile (two columns per lane per
+// step, 8-byte loads, no per-element bounds; the row count is warp-uniform), or a tile read
+// from the global panel.
+__device__ __forceinline__ void res_task(const ResTask& tk, const float* sm, const float* __restrict__ pan,
+                                         double (&xc)[8], int lane, double* slots) {
+  double y[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) y[r] = 0.0;
+  if (tk.soff >= 0) {
+    const int lenp = (tk.len + 63) & ~63;
+    const float2* P = reinterpret_cast<const float2*>(sm + tk.soff) + lane;
+#pragma unroll 1
+    for (int st = 0; st < lenp; st += 64) {            // the step's values are xc[0], xc[1]
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r >= tk.bp) break;
+        const float2 pv = P[(r * lenp + st) >> 1];
+        y[r] = fma((double)pv.x, xc[0], y[r]);
+        y[r] = fma((double)pv.y, xc[1], y[r]);
+      }
+#pragma unroll
+      for (int j = 0; j < 6; ++j) xc[j] = xc[j + 2];
+    }
+  } else {
+    const float* P = pan + tk.pbase;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = lane + 32 * j;
+      if (c >= tk.len) continue;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < tk.bp) y[r] = fma((double)__ldg(P + (int64_t)r * tk.W + c), xc[j], y[r]);
+    }
+  }
+  const double v = warp_rsum8(y, lane);
+  const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+  if ((lane & 3) == 0 && row < tk.bp) slots[tk.slot + row] = v;
+}
+
+// The group's matvec over one source vector: warp w takes tasks w, w + 16, ...; every task's
+// partial row sums go to its shared-memory slots.
 template <typename TS, bool DIV>
 __device__ __forceinline__ void res_matvec(const ResTask* tasks, int ntask, const float* sm,
                                            const float* __restrict__ pan, const int* __restrict__ pan_col,
                                            const TS* __restrict__ src, const float* __restrict__ M, double* slots) {
-  constexpr int CPL = kMvCols / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int t0 = warp; t0 < ntask; t0 += 2 * kResWarps) {
-    double xc[2][CPL];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int t = t0 + hh * kResWarps;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) xc[hh][j] = 0.0;
-      if (t >= ntask) continue;
-      const ResTask tk = tasks[t];
-      const int* cols = tk.soff >= 0 ? reinterpret_cast<const int*>(sm + tk.soff + tk.bp * tk.len) : pan_col + tk.cbase;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < tk.len) {
-          const int col = cols[c];
-          xc[hh][j] = DIV ? (double)src[col] / (double)__ldg(M + col) : (double)__ldcg(src + col);
-        }
-      }
-    }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int t = t0 + hh * kResWarps;
-      if (t >= ntask) continue;
-      const ResTask tk = tasks[t];
-      const float* P = tk.soff >= 0 ? sm + tk.soff : pan + tk.pbase;
-      const int stride = tk.soff >= 0 ? tk.len : tk.W;
-      double y[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) y[r] = 0.0;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c >= tk.len) continue;
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-          if (r < tk.bp) y[r] += (double)P[r * stride + c] * xc[hh][j];
-      }
-      const double v = warp_rsum8(y, lane);
-      const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-      if ((lane & 3) == 0 && row < tk.bp) slots[tk.slot + row] = v;
-    }
+  for (int t0 = warp; t0 < ntask; t0 += kResWarps) {
+    double xa[8];
+    const ResTask ta = tasks[t0];
+    res_gather<TS, DIV>(ta, sm, pan_col, src, M, lane, xa);
+    res_task(ta, sm, pan, xa, lane, slots);
   }
 }
 
@@ -676,10 +712,13 @@ __global__ void __launch_bounds__(kResThreads, 1) k_pcg_res(
   for (int t = warp; t < rg.ntask; t += kResWarps) {
     const ResTask r = tasks[t];
     if (r.soff < 0) continue;
+    const int lenp = (r.len + 63) & ~63;
     for (int rr = 0; rr < r.bp; ++rr)
-      for (int c = lane; c < r.len; c += 32) sm[r.soff + rr * r.len + c] = __ldg(pan + r.pbase + (int64_t)rr * r.W + c);
-    int* cs = reinterpret_cast<int*>(sm + r.soff + r.bp * r.len);
-    for (int c = lane; c < r.len; c += 32) cs[c] = __ldg(d.pan_col + r.cbase + c);
+      for (int c = lane; c < lenp; c += 32)
+        sm[r.soff + rr * lenp + c] = c < r.len ? __ldg(pan + r.pbase + (int64_t)rr * r.W + c) : 0.f;
+    int* cs = reinterpret_cast<int*>(sm + r.soff + r.bp * lenp);
+    const int c0 = __ldg(d.pan_col + r.cbase);
+    for (int c = lane; c < lenp; c += 32) cs[c] = c < r.len ? __ldg(d.pan_col + r.cbase + c) : c0;
   }
   __syncthreads();
 

@@ -684,8 +684,9 @@ static int build_pattern(PlanBuild& B) {
         B3R_REQUIRE(B.mv_slot[t] + (B.mv_task[t].w >> 8) <= kPcgSlots, "internal: PCG group %zu needs more than %d slots",
                     gi, kPcgSlots);
     }
-    // resident layout: each group's tasks take, in task order while they fit, (bp + 1) len
-    // words of their block's shared memory (the tile bp x len, row-major, then the columns)
+    // resident layout: each group's tasks take, in task order while they fit, (bp + 1) lenp
+    // words of their block's shared memory, lenp = len rounded up to 64 (the tile bp x lenp,
+    // row-major and zero-padded, then the columns)
     B.mv_soff.assign(B.mv_task.size(), -1);
     int maxb = 0;
     for (int pr = 0; pr < nb; ++pr) maxb = std::max(maxb, B.bsize[pr]);
@@ -696,7 +697,7 @@ static int build_pattern(PlanBuild& B) {
       int off = 0;
       for (int t = g.x; t < g.y; ++t) {
         const int4 tk = B.mv_task[t];
-        const int words = ((tk.w >> 8) + 1) * (tk.z - tk.y);
+        const int words = ((tk.w >> 8) + 1) * ((tk.z - tk.y + 63) & ~63);
         if (off + words <= kResSmemWords) { B.mv_soff[t] = off; off += words; }
       }
     }

@@ -139,8 +139,9 @@ struct DevPlan {
                           //  block size); helper: (tasks, 0, its helper slot, block size);
                           //  others (0, 0, -1, 0)
   const int* mv_slot;     // [n_mv_tasks] first shared-memory slot of the task's row sums
-  const int* mv_soff;     // [n_mv_tasks] resident kernel: word offset of the task's tile and
-                          //  column list in its block's shared memory, -1: read from the panel
+  const int* mv_soff;     // [n_mv_tasks] resident kernel: word offset (a multiple of 64) of the
+                          //  task's tile (bp x lenp, lenp = len rounded up to 64) and column list
+                          //  in its block's shared memory, -1: read from the panel
   int pcg_resident;       // 1: the row groups fit the resident kernel (one per SM, <= kResThreads
                           //  scalars, block sizes <= 8)
   const int2* pcg_scl;    // [n_cam_params] (slot of the scalar's first task, the row's task

@@ -71,6 +71,37 @@ class ShardedSchur:
         self.precond = torch.empty(ncp, dtype=torch.float32, device=dev)
         self.hpp_max = torch.empty(1, dtype=torch.float32, device=dev)
         self.outputs = (self.S, self.b, self.diagA, self.precond, self.hpp_max)
+        self._own = self._order = None
+        if self.world > 1:                      # every rank's track list, once (for the point exchange)
+            own = torch.from_numpy(np.ascontiguousarray(plan.own_tracks, np.int64)).to(dev)
+            cnt = torch.tensor([own.numel()], dtype=torch.int64, device=dev)
+            cnts = [torch.empty_like(cnt) for _ in range(self.world)]
+            dist.all_gather(cnts, cnt, group=self.group)
+            self._counts = [int(c) for c in cnts]
+            self._cap = max(max(self._counts), 1)
+            padded = torch.zeros(self._cap, dtype=torch.int64, device=dev)
+            padded[:own.numel()] = own
+            lists = torch.empty(self.world * self._cap, dtype=torch.int64, device=dev)
+            dist.all_gather_into_tensor(lists, padded, group=self.group)
+            self._own = own
+            self._order = torch.cat([lists[r * self._cap:r * self._cap + c] for r, c in enumerate(self._counts)])
+            self._valid = torch.cat([torch.arange(r * self._cap, r * self._cap + c, device=dev)
+                                     for r, c in enumerate(self._counts)])
+
+    def gather_points(self, dp):
+        """The point update of every rank's tracks on every rank: each rank sends the 3-vectors
+        of its own tracks only (an all-gather of about 1/world of delta_p each), not a SUM
+        all-reduce of the whole, mostly zero, vector."""
+        if self.world == 1:
+            return dp
+        v = dp.view(-1, 3)
+        send = torch.zeros(self._cap, 3, dtype=dp.dtype, device=dp.device)
+        send[:self._own.numel()] = v[self._own]
+        recv = torch.empty(self.world * self._cap, 3, dtype=dp.dtype, device=dp.device)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        out = torch.zeros_like(v)
+        out[self._order] = recv[self._valid]
+        return out.view(-1)
 
     def linearize(self, params, opts):
         if self.world == 1:
@@ -92,7 +123,7 @@ def sharded_lm_step(sharded, rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2c
 
     Every rank holds all inputs.  The linearization is sharded (``ShardedSchur``); the root
     solves S delta_c = b with the device PCG and broadcasts delta_c; each rank back-substitutes
-    its own tracks' points and one all-reduce (SUM) assembles delta_p; the objective (the
+    its own tracks' points and an all-gather of those assembles delta_p; the objective (the
     residual op over all observations, cheap next to the linearization) is evaluated on every
     rank, so the line search takes the same decisions everywhere and every rank ends with the
     same parameters.  The plan must enable whole parameter types (bool optim flags, the
@@ -122,9 +153,7 @@ def sharded_lm_step(sharded, rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2c
         dc = torch.empty(plan.n_cam_params, dtype=dt, device=plan.device)
     if sharded.world > 1:
         dist.broadcast(dc, src=sharded.root, group=sharded.group)
-    dp = plan.backsub(p, lo, plan.workspace(), dc)        # this rank's tracks, zeros elsewhere
-    if sharded.world > 1:
-        dist.all_reduce(dp, op=dist.ReduceOp.SUM, group=sharded.group)
+    dp = sharded.gather_points(plan.backsub(p, lo, plan.workspace(), dc))   # own tracks, then all
     delta = torch.cat([dc.to(torch.float32), dp])
     i = plan.info
     n_cams, n_nodes, n_imgs, n_pts, C = i.nb_K, i.nb_P, i.nb_Z, i.n_points, plan.C

@@ -71,6 +71,9 @@ class BAPlan:
             if owner.shape != (n_tracks,):
                 raise ValueError(f'track_owner must have shape ({n_tracks},)')
             self._keep.append(owner)
+            self.own_tracks = np.flatnonzero(owner == rank)
+        else:
+            self.own_tracks = np.arange(t0, t1)
         desc = L.PlanDesc(n_imgs=n_imgs, n_cams=n_cams, n_nodes=n_nodes, n_tracks=n_tracks, n_obs=self.n_obs,
                           C=n_zcf, infos=infos_h.ctypes.data_as(C.POINTER(C.c_int32)),
                           pids=pids_h.ctypes.data_as(C.POINTER(C.c_int32)),

@@ -138,3 +138,34 @@ def test_gloo_two_ranks_partial_systems_sum_to_full(tmp_path, by_image):
     mp.spawn(_rank_main, args=(2, _free_port(), out, by_image), nprocs=2, join=True)
     errs = np.load(out)
     assert (errs < 1e-9).all(), errs
+
+
+def _gather_main(rank, world, port, result_path):
+    """Each rank holds the point update of its own tracks (zeros elsewhere), as the
+    back-substitution leaves it; ShardedSchur.gather_points must give every rank the full
+    update."""
+    from types import SimpleNamespace
+    from blast3r_b200.distributed import ShardedSchur
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        sc = make_scene(0, n_imgs=10, n_tracks=300, seed=9)
+        owner, _ = shard_tracks_by_image(sc.infos, sc.pids, sc.n_tracks, world)
+        own = np.flatnonzero(owner == rank)
+        plan = SimpleNamespace(device=torch.device('cpu'), n_cam_params=4, info=SimpleNamespace(nnz=8),
+                               own_tracks=own)
+        full = torch.from_numpy(np.random.default_rng(3).normal(size=(sc.n_tracks, 3)).astype(np.float32))
+        mine = torch.zeros_like(full)
+        mine[own] = full[own]
+        got = ShardedSchur(plan).gather_points(mine.view(-1))
+        np.save(result_path + f'.{rank}.npy', np.array([float((got.view(-1, 3) - full).abs().max())]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize('world', [2, 3])
+def test_gloo_point_update_gathered_on_every_rank(tmp_path, world):
+    out = str(tmp_path / 'gather')
+    mp.spawn(_gather_main, args=(world, _free_port(), out), nprocs=world, join=True)
+    for r in range(world):
+        assert np.load(out + f'.{r}.npy')[0] == 0.0
