@@ -59,9 +59,6 @@ def parse_args(argv=None):
                     help='tracks per step of the reference (CPU) arm')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--e2e-steps', type=int, default=8)
-    ap.add_argument('--pair-math', default='fp32', choices=['fp32', '3xtf32', 'tf32'],
-                    help='pair products in fp32 on the FMA pipes (default) or on the tensor cores (3xtf32: '
-                         'fp32-level accuracy; tf32: well-conditioned problems only)')
     ap.add_argument('--internal', default=None, help=argparse.SUPPRESS)
     return ap.parse_args(argv)
 
@@ -229,11 +226,11 @@ def profile_traffic(name):
 class Workload:
     PASSES = ['prep', 'points', 'factor', 'diag', 'pairs', 'finalize']
 
-    def __init__(self, cfg, n_tracks, world, rank, dev, obs_local, pair_math='fp32'):
+    def __init__(self, cfg, n_tracks, world, rank, dev, obs_local):
         import torch
         from blast3r_b200.distributed import ShardedSchur, shard_tracks_by_image
         from blast3r_b200.plan import BAPlan
-        self.cfg, self.world, self.rank, self.dev, self.pair_math = cfg, world, rank, dev, pair_math
+        self.cfg, self.world, self.rank, self.dev = cfg, world, rank, dev
         tg = time.perf_counter()
         sc = self.sc = cached_scene(cfg, n_tracks=n_tracks)
         self.scene_s = time.perf_counter() - tg
@@ -260,7 +257,7 @@ class Workload:
         self.t = {k: torch.from_numpy(v).to(dev) for k, v in {**self.host_obs, **self.host_par}.items()}
         self.p = self.params(self.t)
         self.lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
-                                  huber_delta=o['huber_delta'], pair_math=pair_math)
+                                  huber_delta=o['huber_delta'])
         self.sharded = ShardedSchur(plan)
 
     def params(self, t):
@@ -477,8 +474,6 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
                       'n_imgs': sc.n_imgs, 'mean_track_length': sc.meta['mean_track_length'],
                       'n_obs_pairs_rank0': int(plan.info.n_pairs), 'nnz_S': int(plan.info.nnz),
                       'depth_stitch_passes': bool(plan.info.depth_stitch),
-                      'pair_math': wl.pair_math + (' (FMA pipes)' if wl.pair_math == 'fp32'
-                                                   else ' (tensor cores, fp32 accumulation)'),
                       'parallelism': f'track-sharded x{wl.world} (tracks by first image)' +
                                      (' + NCCL reduce of S, b' if wl.world > 1 else ''),
                       'l2': 'inputs larger than L2, no flush'},
@@ -816,7 +811,7 @@ def run_b200(args):
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=600), device_id=dev)
     peak, peak_kind = measured_peaks()
 
-    wl = Workload(args.config, args.tracks, world, rank, dev, obs_local=world > 1, pair_math=args.pair_math)
+    wl = Workload(args.config, args.tracks, world, rank, dev, obs_local=world > 1)
     head = measure_workload(wl, args.steps, args.warmup, peak, peak_kind, want_clocks=True,
                             e2e_steps=args.e2e_steps)
     sc = wl.sc
@@ -830,7 +825,7 @@ def run_b200(args):
     wl.release()
     del wl
     if not args.no_configs4:
-        wl4 = Workload(4, args.configs4_tracks, world, rank, dev, obs_local=world > 1, pair_math=args.pair_math)
+        wl4 = Workload(4, args.configs4_tracks, world, rank, dev, obs_local=world > 1)
         r4 = measure_workload(wl4, args.configs4_steps, 3, peak, peak_kind, want_clocks=False, e2e_steps=4)
         r4['note'] = ('the depth-stitch phase of configs[4] (scripts/xps/co3d_offline.sh:38 second phase): focal '
                       'and poses fixed, only depth-coefficient blocks in S; measured like the headline step')

@@ -55,7 +55,7 @@ class LinOpts(C.Structure):
     _fields_ = [('is_depth_log', _i32), ('weight_z', _f32), ('pnorm', _f32), ('max_pix_err', _f32),
                 ('huber_delta', _f32), ('w_pts_nul', _f32), ('clamp_w_lo', _f32), ('clamp_w_hi', _f32),
                 ('dampen', _f64), ('adaptive_dampen', _i32), ('no_grad_f_from_rz', _i32),
-                ('optim_Z0', _i32), ('optim_Z_1st_cam', _i32), ('pair_math', _i32)]
+                ('optim_Z0', _i32), ('optim_Z_1st_cam', _i32)]
 
 
 class Outputs(C.Structure):

@@ -50,7 +50,6 @@ struct Ctx {
   int no_grad_f_from_rz, optim_Z0, optim_Z_1st_cam;
   float dampen;
   int adaptive;
-  int pair_math;      // B3R_PAIR_MATH_*: the pair products on the FMA pipes or the tensor cores
 };
 
 // ------------------------------------------------------------------------------------
@@ -1041,184 +1040,6 @@ __global__ void __launch_bounds__(pair_roles<CT>() * 32) k_pairs(Ctx c, float* _
 }
 
 // ------------------------------------------------------------------------------------
-// pair pass on the tensor cores (C <= 8): TF32 or 3xTF32 mma.sync, fp32 accumulation
-// ------------------------------------------------------------------------------------
-// A segment's block is -sum over its pairs of Y_o^T Y_o', a contraction over K = 3 x pairs
-// with a W x W (W = 8 + C <= 16) output: one m16 x n16 tile.  The M/N index is the
-// expanded camera column a (0..7 focal/tau, 8 + c depth channel c, the depth columns
-// being Y[r][8+c] = zs[r] dep[c]); the K index runs over (pair, row r).  Four pairs make
-// one k8 step (their rows 0 and 1) plus one k4 step (their row 2): lane (g, t) = (lane/4,
-// lane%4) owns pair t of the group and column g (A rows g, g+8; B column g of both n8
-// tiles), so a lane reads 5 values of each record per group (Y[0..2][g], zs[0..2],
-// dep[g]) and forms its two depth-column entries with one product each.  Operands are
-// rounded to TF32 (round to nearest), or split into TF32 high and low parts for the
-// three-product 3xTF32 scheme, and the products are accumulated in fp32 by the tensor
-// cores; the accumulators (8 floats a lane) stay in registers for the whole task
-// and are emitted with one atomic per value.  Records are staged exactly like the FMA
-// pass (coalesced 16-byte cp.async, kPairMmaStages - 1 steps ahead), into pair slots of
-// 72 floats (two records + padding, so that the four pairs of a group fall on distinct
-// banks for every column read).
-constexpr int kPairMmaStages = 4;     // cp.async ring depth
-constexpr int kPairMmaStep = 8;       // pairs per step (two groups of four)
-constexpr int kPairMmaSlot = 72;      // floats per staged pair slot (72 = 8 mod 32)
-constexpr int kPairMmaMaxC = 8;       // W = 8 + C fits one m16 tile
-
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t u;
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(u) : "f"(x));
-  return u;
-}
-__device__ __forceinline__ void mma_k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_k4(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm("mma.sync.aligned.m16n8k4.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(b0));
-}
-
-// The five values of one record a lane needs: Y[0..2][g], zs[0..2] (the z-scale column)
-// and dep[g] (0 for g >= C).
-template <int CT>
-__device__ __forceinline__ void pm_read(const float* __restrict__ rp, int g, float (&y)[3], float (&zs)[3],
-                                        float& dep) {
-  constexpr int ZS = rec_zs<CT>();
-  y[0] = rp[g]; y[1] = rp[8 + g]; y[2] = rp[16 + g];
-  if constexpr ((ZS & 3) <= 1) {           // zs[0..2] inside one aligned 16-byte piece
-    const float4 q = *reinterpret_cast<const float4*>(rp + (ZS & ~3));
-    const float v[4] = {q.x, q.y, q.z, q.w};
-    zs[0] = v[ZS & 3]; zs[1] = v[(ZS & 3) + 1]; zs[2] = v[(ZS & 3) + 2];
-  } else {
-    zs[0] = rp[ZS]; zs[1] = rp[ZS + 1]; zs[2] = rp[ZS + 2];
-  }
-  dep = g < CT ? rp[24 + g] : 0.f;
-}
-
-// One operand as the TF32 pair (hi, lo) with hi + lo = x to about 2^-22 |x|: the split
-// of the 3xTF32 products a b ~ a_hi b_hi + a_hi b_lo + a_lo b_hi (Ootomo and Yokota,
-// "Recovering single precision accuracy from Tensor Cores while surpassing the FP32
-// theoretical peak performance", 2022), whose error is that of an fp32 product.
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = to_tf32(x);
-  lo = to_tf32(x - __uint_as_float(hi));
-}
-
-template <int CT, bool X3>
-__global__ void __launch_bounds__(32) k_pairs_mma(Ctx c, float* __restrict__ S) {
-  constexpr int R = rec_floats<CT>(), Q = R / 4, W = 8 + CT;
-  constexpr int STEP = kPairMmaStep * kPairMmaSlot;
-  constexpr int PIECES = kPairMmaStep * 2 * Q;           // 16-byte pieces per step
-  static_assert(2 * R <= kPairMmaSlot, "pair slot layout");
-  __shared__ __align__(16) float stg[kPairMmaStages * STEP];
-  const int lane = threadIdx.x;
-  const int g = lane >> 2, t = lane & 3;
-  const int64_t task = blockIdx.x;
-  const int s = c.d.task_seg[task];
-  const int64_t pb = c.d.task_pb[task], pe = c.d.task_pe[task];
-  const int nit = (int)((pe - pb + kPairMmaStep - 1) / kPairMmaStep);
-  const int2* __restrict__ pairs = c.d.pairs;
-  // piece m of a step (lane + 32 m) is part (piece % Q) of side ((piece / Q) & 1) of pair
-  // piece / (2 Q); its pair index entry is loaded one step before its copy is issued
-  constexpr int PM = (PIECES + 31) / 32;
-  auto load_idx = [&](int j, int (&e)[PM]) {
-#pragma unroll
-    for (int m = 0; m < PM; ++m) {
-      const int piece = lane + 32 * m, p = piece / (2 * Q), side = (piece / Q) & 1;
-      e[m] = -1;
-      if (j < nit && piece < PIECES) {
-        int64_t q = pb + (int64_t)j * kPairMmaStep + p;
-        q = q < pe ? q : pe - 1;               // idle slots of the last step repeat its last pair
-        const int2 kk = __ldg(pairs + q);
-        e[m] = side ? kk.y : kk.x;
-      }
-    }
-  };
-  auto stage = [&](int j, const int (&e)[PM]) {
-    float* dst = stg + (j % kPairMmaStages) * STEP;
-#pragma unroll
-    for (int m = 0; m < PM; ++m) {
-      const int piece = lane + 32 * m, p = piece / (2 * Q), side = (piece / Q) & 1, part = piece % Q;
-      if (e[m] >= 0) cp_async16(dst + p * kPairMmaSlot + side * R + 4 * part, c.rec + (int64_t)e[m] * R + 4 * part);
-    }
-    cp_async_commit();                         // one group per step (empty past the end)
-  };
-  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};   // n8 tiles: columns 0..7, 8..15
-  {
-    int e[PM];
-#pragma unroll
-    for (int j = 0; j < kPairMmaStages - 1; ++j) { load_idx(j, e); stage(j, e); }
-  }
-  int e_next[PM];
-  load_idx(kPairMmaStages - 1, e_next);
-  for (int j = 0; j < nit; ++j) {
-    cp_async_wait<kPairMmaStages - 2>();      // this lane's copies of step j have landed
-    __syncwarp();                              // ... and every lane's; step j-1's buffer is free
-    stage(j + kPairMmaStages - 1, e_next);
-    load_idx(j + kPairMmaStages, e_next);
-    const float* buf = stg + (j % kPairMmaStages) * STEP;
-    // the step's products in fresh accumulators, added to the task's sums with fp32
-    // round-to-nearest adds: the tensor cores' own accumulation rounds toward zero, whose bias
-    // would otherwise grow along a task's chain of MMAs
-    float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int h = 0; h < kPairMmaStep / 4; ++h) {
-      const bool ok = pb + (int64_t)j * kPairMmaStep + 4 * h + t < pe;
-      const float* rp = buf + (4 * h + t) * kPairMmaSlot;
-      float yr[3], zr[3], dr, yc[3], zc[3], dc;
-      pm_read<CT>(rp, g, yr, zr, dr);
-      pm_read<CT>(rp + R, g, yc, zc, dc);
-      auto m = [ok](float x) { return ok ? x : 0.f; };   // pairs past the task's end add nothing
-      uint32_t a[3], ad[3], b[3], bd[3];       // row r: base column g, depth column g
-      uint32_t al[3], adl[3], bl[3], bdl[3];   // their low parts (3xTF32)
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-        if constexpr (X3) {
-          split_tf32(m(yr[r]), a[r], al[r]);
-          split_tf32(m(zr[r] * dr), ad[r], adl[r]);
-          split_tf32(m(yc[r]), b[r], bl[r]);
-          split_tf32(m(zc[r] * dc), bd[r], bdl[r]);
-        } else {
-          a[r] = to_tf32(m(yr[r]));
-          ad[r] = to_tf32(m(zr[r] * dr));
-          b[r] = to_tf32(m(yc[r]));
-          bd[r] = to_tf32(m(zc[r] * dc));
-        }
-      }
-      // k8: K rows t (row 0 of pair t) and t + 4 (row 1 of pair t); k4: row 2 of pair t.
-      // 3xTF32 adds the two cross terms first (small before large).
-      if constexpr (X3) {
-        mma_k8(e0, al[0], adl[0], al[1], adl[1], b[0], b[1]);
-        mma_k8(e1, al[0], adl[0], al[1], adl[1], bd[0], bd[1]);
-        mma_k4(e0, al[2], adl[2], b[2]);
-        mma_k4(e1, al[2], adl[2], bd[2]);
-        mma_k8(e0, a[0], ad[0], a[1], ad[1], bl[0], bl[1]);
-        mma_k8(e1, a[0], ad[0], a[1], ad[1], bdl[0], bdl[1]);
-        mma_k4(e0, a[2], ad[2], bl[2]);
-        mma_k4(e1, a[2], ad[2], bdl[2]);
-      }
-      mma_k8(e0, a[0], ad[0], a[1], ad[1], b[0], b[1]);
-      mma_k8(e1, a[0], ad[0], a[1], ad[1], bd[0], bd[1]);
-      mma_k4(e0, a[2], ad[2], b[2]);
-      mma_k4(e1, a[2], ad[2], bd[2]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) { d0[i] += e0[i]; d1[i] += e1[i]; }
-  }
-  cp_async_wait<0>();
-  // D[m][n]: d0/d1 hold rows g and g + 8, columns 2t, 2t + 1 of the n8 tiles 0 and 1
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int a = g + 8 * (i >> 1), col = 2 * t + (i & 1);
-    if (a < W && col < W) emit_pair_value<CT>(c, S, s, a, col, d0[i]);
-    if (a < W && col + 8 < W) emit_pair_value<CT>(c, S, s, a, col + 8, d1[i]);
-  }
-}
-
-// ------------------------------------------------------------------------------------
 // depth-stitch plans: only the depth-coefficient (zcf) blocks take part in S
 // ------------------------------------------------------------------------------------
 // With the focal and pose types switched off (the reference's second BA phase, optim_K =
@@ -1618,10 +1439,6 @@ int make_ctx(b3r_plan* plan, const b3r_params* p, const b3r_lin_opts* o, void* w
   c.optim_Z_1st_cam = o->optim_Z_1st_cam;
   c.dampen = (float)o->dampen;
   c.adaptive = o->adaptive_dampen;
-  B3R_REQUIRE(o->pair_math == B3R_PAIR_MATH_FP32 || o->pair_math == B3R_PAIR_MATH_TF32 ||
-                  o->pair_math == B3R_PAIR_MATH_3XTF32,
-              "pair_math must be one of B3R_PAIR_MATH_FP32, _TF32, _3XTF32");
-  c.pair_math = o->pair_math;
   char* w = (char*)ws;
   c.img_rec = (float*)(w + plan->ws_img);
   c.trec = (float*)(w + plan->ws_trec);
@@ -1685,16 +1502,6 @@ int diag_launch(const Ctx& c, float* S, float* b, float* diagA, cudaStream_t s) 
 
 template <int CT>
 int pairs_launch(const Ctx& c, float* S, cudaStream_t s) {
-  if constexpr (CT <= kPairMmaMaxC) {
-    if (c.pair_math == B3R_PAIR_MATH_TF32) {
-      k_pairs_mma<CT, false><<<(unsigned)c.d.n_tasks, 32, 0, s>>>(c, S);
-      return check_launch("pairs pass (tensor cores, TF32)");
-    }
-    if (c.pair_math == B3R_PAIR_MATH_3XTF32) {
-      k_pairs_mma<CT, true><<<(unsigned)c.d.n_tasks, 32, 0, s>>>(c, S);
-      return check_launch("pairs pass (tensor cores, 3xTF32)");
-    }
-  }
   const size_t smem = (size_t)pair_smem_floats<CT>() * sizeof(float);
   static bool configured = false;          // one attribute call per instantiation
   if (!configured) {

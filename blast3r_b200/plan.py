@@ -13,9 +13,6 @@ import torch
 
 from . import _lib as L
 
-# BAPlan.lin_opts(pair_math=...) -> B3R_PAIR_MATH_* of the C ABI
-PAIR_MATH = {'fp32': 0, 'tf32': 1, '3xtf32': 2}
-
 
 def _enable_mode(status, n):
     """(mode, host mask) for one parameter type, mirroring GaussNewtonSolver.enable
@@ -146,20 +143,13 @@ class BAPlan:
     @staticmethod
     def lin_opts(is_depth_log=True, weight_z=1.0, pnorm=1.0, max_pix_err=100.0, huber_delta=0.5,
                  w_pts_nul=1e-16, clamp_w=(1e-6, 1e6), dampen=1e-12, adaptive_dampen=True,
-                 no_grad_f_from_rz=False, optim_Z0=True, optim_Z_1st_cam=True, pair_math='fp32'):
-        """Options of one linearization.  ``pair_math`` sums the fill-in pair products in fp32
-        on the FMA pipes ('fp32', the default), on the tensor cores with each operand split
-        into TF32 high and low parts ('3xtf32', fp32-level accuracy), or on the tensor cores
-        with operands rounded once to TF32 ('tf32', for well-conditioned problems only)."""
-        if pair_math not in PAIR_MATH:
-            raise ValueError(f"pair_math must be one of {sorted(PAIR_MATH)}, not {pair_math!r}")
+                 no_grad_f_from_rz=False, optim_Z0=True, optim_Z_1st_cam=True):
         return L.LinOpts(is_depth_log=int(bool(is_depth_log)), weight_z=weight_z, pnorm=pnorm,
                          max_pix_err=max_pix_err, huber_delta=huber_delta, w_pts_nul=w_pts_nul,
                          clamp_w_lo=clamp_w[0], clamp_w_hi=clamp_w[1], dampen=dampen,
                          adaptive_dampen=int(bool(adaptive_dampen)),
                          no_grad_f_from_rz=int(bool(no_grad_f_from_rz)), optim_Z0=int(bool(optim_Z0)),
-                         optim_Z_1st_cam=int(bool(optim_Z_1st_cam)),
-                         pair_math=PAIR_MATH[pair_math])
+                         optim_Z_1st_cam=int(bool(optim_Z_1st_cam)))
 
     def params(self, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pix2d_std, pix2d_dep, pix2d=None,
                residuals=None, w_pts=None):

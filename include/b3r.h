@@ -242,23 +242,7 @@ typedef struct {
     double dampen;                    /* 1e-12                                           */
     int32_t adaptive_dampen;          /* damping x max |diag| per block type             */
     int32_t no_grad_f_from_rz, optim_Z0, optim_Z_1st_cam;
-    int32_t pair_math;                /* B3R_PAIR_MATH_*: how the pair products of S are
-                                         summed (no counterpart in the reference, whose
-                                         Gram blocks are fp32 CUDA-core products)         */
 } b3r_lin_opts;
-
-/* b3r_lin_opts.pair_math: how the fill-in blocks -sum Y_o^T Y_o' are summed.
- * FP32 (the default, 0): fp32 products on the FMA pipes (S within ~5e-7 of max|S_ij| of
- * the float64 system).  3XTF32 (2): tensor cores, each operand split into TF32 high and low
- * parts, three products per pair, fp32 accumulation: fp32-level accuracy.  TF32 (1): tensor
- * cores with operands rounded once to TF32: S within ~1.5e-5 of max|S_ij| on the configs'
- * generators, which is inside the linearization tolerance but moves the solve of an
- * ill-conditioned system (cond(S) 1e10..1e18 on the reference's test scenes) by several
- * percent, so it is for well-conditioned problems only.  The tensor-core modes need C <= 8
- * (larger C runs FP32). */
-#define B3R_PAIR_MATH_FP32 0
-#define B3R_PAIR_MATH_TF32 1
-#define B3R_PAIR_MATH_3XTF32 2
 
 /* Device outputs of one linearization (caller-owned, overwritten). */
 typedef struct {

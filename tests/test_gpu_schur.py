@@ -20,7 +20,7 @@ from tests.helpers import TOL_ACC, TOL_B, TOL_OBS, golden_files, load_golden, re
 pytestmark = pytest.mark.gpu
 
 
-def run_plan(inp, opts, recompute=True, pair_math='fp32'):
+def run_plan(inp, opts, recompute=True):
     t = to_cuda(inp)
     plan = BAPlan(t['infos'], t['pids'], len(inp['K']), len(inp['P_w2rig']), len(inp['pts3d']),
                   inp['pix2d_dep'].shape[1], optim_K=opts.get('optim_K', True), optim_P=opts.get('optim_P', True),
@@ -29,7 +29,7 @@ def run_plan(inp, opts, recompute=True, pair_math='fp32'):
     lo = BAPlan.lin_opts(is_depth_log=is_log, weight_z=opts['weight_z'], pnorm=opts['pnorm'],
                          max_pix_err=opts['clip_pix_err'], huber_delta=opts['huber_delta'],
                          no_grad_f_from_rz=opts.get('no_grad_f_from_rz', False), optim_Z0=opts.get('optim_Z0', True),
-                         optim_Z_1st_cam=opts.get('optim_Z_1st_cam', True), pair_math=pair_math)
+                         optim_Z_1st_cam=opts.get('optim_Z_1st_cam', True))
     if recompute:
         p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
                         t['pix2d_dep'], pix2d=t['pix2d'])
@@ -71,8 +71,8 @@ def test_general_path_equals_recompute(path):
     reference residual kernel calls powf, so the two agree to a few ulps, not bitwise:
     the bound is the float32 observation tolerance."""
     inp, opts, _ = load_golden(path)
-    _, a = run_plan(inp, opts, recompute=True, pair_math='fp32')
-    _, b = run_plan(inp, opts, recompute=False, pair_math='fp32')
+    _, a = run_plan(inp, opts, recompute=True)
+    _, b = run_plan(inp, opts, recompute=False)
     assert rel_err(b.S_vals.cpu().numpy(), a.S_vals.cpu().numpy()) < TOL_OBS
     assert rel_err(b.b.cpu().numpy(), a.b.cpu().numpy()) < TOL_OBS
 
@@ -89,36 +89,6 @@ def test_schur_matches_oracle(cfg, ni, nt):
     assert rel_err(s.to_dense().cpu().numpy(), want['S']) < TOL_ACC
     assert rel_err(s.b.cpu().numpy(), want['b']) < TOL_B
     assert rel_err(s.diagA.cpu().numpy() + want['lam'], want['diagA']) < TOL_ACC
-
-
-@pytest.mark.parametrize('cfg,ni,nt', SCENES, ids=lambda v: str(v))
-def test_pair_math_modes(cfg, ni, nt):
-    """The pair products in fp32 on the FMA pipes (the default), on the tensor cores with
-    3xTF32 split operands, and on the tensor cores with one TF32 rounding: all within the
-    accumulated-block tolerance of the float64 oracle, fp32 and 3xTF32 an order of magnitude
-    tighter; they differ only in the fill-in blocks, so b and diag(A) agree to rounding."""
-    sc = make_scene(cfg, n_imgs=ni, n_tracks=nt)
-    inp, opts = scene_inputs(sc), dict(sc.options)
-    want = O.linearize(inp, opts, dtype=np.float64, residual_dtype=np.float32)
-    runs = {m: run_plan(inp, opts, pair_math=m)[1] for m in ('fp32', '3xtf32', 'tf32')}
-    err = {m: rel_err(s.to_dense().cpu().numpy(), want['S']) for m, s in runs.items()}
-    assert err['fp32'] < TOL_ACC / 10 and err['3xtf32'] < TOL_ACC / 10 and err['tf32'] < TOL_ACC, err
-    for m in ('3xtf32', 'tf32'):
-        assert rel_err(runs[m].b.cpu().numpy(), runs['fp32'].b.cpu().numpy()) < TOL_OBS
-        assert rel_err(runs[m].diagA.cpu().numpy(), runs['fp32'].diagA.cpu().numpy()) < TOL_OBS
-
-
-@pytest.mark.parametrize('path', golden_files(), ids=lambda p: p.split('golden_')[-1][:-4])
-def test_pair_math_3xtf32_matches_reference_solver(path):
-    """3xTF32 pair products against the reference solver's float64 S on its test scenes, at
-    the fp32 path's own accuracy (these systems are ill-conditioned: one TF32 rounding
-    moves their solutions by several percent, the split operands do not)."""
-    inp, opts, ref = load_golden(path)
-    _, a = run_plan(inp, opts, pair_math='fp32')
-    _, b = run_plan(inp, opts, pair_math='3xtf32')
-    ea = rel_err(a.to_dense().cpu().numpy(), ref['f64_S'])
-    eb = rel_err(b.to_dense().cpu().numpy(), ref['f64_S'])
-    assert eb < max(2 * ea, 1e-6), (ea, eb)
 
 
 @pytest.mark.parametrize('cfg', [0, 3])
