@@ -59,6 +59,9 @@ def parse_args(argv=None):
                     help='tracks per step of the reference (CPU) arm')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--e2e-steps', type=int, default=8)
+    ap.add_argument('--channels', type=int, default=None,
+                    help='keep the first C depth channels of the scene (C = 2: one log-depth channel and beta)')
+    ap.add_argument('--no-reference-gpu', action='store_true', help='skip timing the reference\'s GPU path')
     ap.add_argument('--internal', default=None, help=argparse.SUPPRESS)
     return ap.parse_args(argv)
 
@@ -179,6 +182,17 @@ def cached_scene(cfg, n_tracks=None, seed=None):
         return sc
 
 
+def channel_subset(sc, C):
+    """The scene with its first C depth channels (and coefficients) only.  The generator's
+    channel 0 is the log-depth and channel 1 the constant 1 (beta), so C = 2 is the
+    one-channel depth model alpha F + beta of the reference's first BA phase."""
+    if C is None or C == sc.n_zcf:
+        return sc
+    import dataclasses
+    return dataclasses.replace(sc, pix2d_dep=np.ascontiguousarray(sc.pix2d_dep[:, :C]),
+                               z_coefs=np.ascontiguousarray(sc.z_coefs[:, :C]))
+
+
 # ------------------------------------------------------------------------------------------
 # roofline bookkeeping (SURVEY section 8(d))
 # ------------------------------------------------------------------------------------------
@@ -203,9 +217,13 @@ def kernel_source_sha():
     return h.hexdigest()[:16]
 
 
-def profile_traffic(name):
-    """Per-launch DRAM bytes from the committed ncu summary profiles/traffic_<name>.txt when its
-    recorded source hash equals the current sources', else None (a stale capture is never used)."""
+def profile_traffic(name, units):
+    """DRAM bytes per launch of each pass for this rank's workload, from the committed ncu
+    summary profiles/traffic_<name>.txt (a reduced case of the same generator): each pass's
+    captured bytes scaled by the units it processes (observations for points and diag, tracks
+    for factor, pairs for pairs).  Used only when the summary's source_sha equals the hash of
+    the current kernel and planner sources; otherwise (None, why): a capture of other sources
+    is never used."""
     path = os.path.join(ROOT, 'profiles', f'traffic_{name}.txt')
     if not os.path.isfile(path):
         return None, 'no capture'
@@ -217,7 +235,11 @@ def profile_traffic(name):
                 vals[k.strip()] = v.strip()
     if vals.get('source_sha') != kernel_source_sha():
         return None, 'capture is of other sources'
-    return vals, path
+    n_obs, n_tracks, n_pairs = units
+    scale = {'points': n_obs / float(vals['units_obs']), 'diag': n_obs / float(vals['units_obs']),
+             'factor': n_tracks / float(vals['units_tracks']), 'pairs': n_pairs / float(vals['units_pairs'])}
+    out = {p: (float(vals[f'{p}_dram_read']) + float(vals[f'{p}_dram_write'])) * scale[p] for p in scale}
+    return out, f'{os.path.relpath(path, ROOT)} (reduced case scaled by units)'
 
 
 # ------------------------------------------------------------------------------------------
@@ -452,10 +474,9 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
              'pair_lists': 8 * int(plan.info.n_pairs),
              'what': 'written by the diag pass and read by the pairs pass (records), read by the pairs pass '
                      '(pair lists): traffic of this design on top of the algorithmic bytes'}
-    trafficv, tsrc = profile_traffic(f'configs{wl.cfg}') if wl.world == 1 else (None, 'N > 1')
-    traffic = None
-    if trafficv is not None and f'{dom}_dram_bytes_per_launch' in trafficv:
-        traffic = float(trafficv[f'{dom}_dram_bytes_per_launch'])
+    trafficv, tsrc = (profile_traffic(f'configs{wl.cfg}', (wl.n_local, wl.tracks_local, int(plan.info.n_pairs)))
+                      if wl.world == 1 else (None, 'N > 1'))
+    traffic = trafficv.get(dom) if trafficv else None
     roof = {'bound': 'hbm', 'kernel': f'{dom} pass ({passes[dom]["share"]:.2f} of the step)',
             'achieved': round(B / (dom_ms * 1e-3) / 1e9, 2), 'peak': peak, 'unit': 'GB/s',
             'frac': round(B / (dom_ms * 1e-3) / 1e9 / peak, 4), 'traffic': traffic,
@@ -465,8 +486,7 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
                           '(this rank\'s observations and tracks)',
             'step': {'achieved': round(B / (ms_step * 1e-3) / 1e9, 2),
                      'frac': round(B / (ms_step * 1e-3) / 1e9 / peak, 4), 'ms': ms_step,
-                     'traffic': float(trafficv['dram_bytes_per_step']) if trafficv and
-                     'dram_bytes_per_step' in trafficv else None},
+                     'traffic': sum(trafficv.values()) if trafficv else None},
             'intermediate_bytes': inter, 'passes': passes}
     rec = {'value': sc.n_obs * steps / (ms_total * 1e-3), 'unit': UNIT, 'ms_per_step': ms_step, 'steps': steps,
            'warmup': warmup, 'roofline': roof,
@@ -601,9 +621,9 @@ def internal_ref_gpu(args):
     from oracle import ref_runner as RR
     faulthandler.enable()
     ba_solver, engine = RR.import_reference(cpu_ops=False)
-    sc = cached_scene(args.config, n_tracks=args.tracks)
+    sc = channel_subset(cached_scene(args.config, n_tracks=args.tracks), args.channels)
     t = RR.tensors(sc.lm_inputs(), 'cuda')
-    out = {'n_obs': sc.n_obs, 'workload': f'configs[{args.config}]'}
+    out = {'n_obs': sc.n_obs, 'workload': f'configs[{args.config}]', 'depth_channels': sc.n_zcf}
 
     def run(dtype, solve, reps=3):
         RR.linearize(ba_solver, engine, t, sc.options, dtype, solve)     # warm-up
@@ -621,7 +641,72 @@ def internal_ref_gpu(args):
         out[f'linearize_{name}_obs_per_s'] = sc.n_obs / (ms * 1e-3)
     ms = run(torch.float64, True, reps=2)
     out['solve_f64_ms'] = round(ms, 2)
+    out['peak_gpu_mem_gb'] = round(torch.cuda.max_memory_allocated() / 2**30, 2)
     print(json.dumps(out))
+
+
+def b200_same_workload(cfg, n_tracks, channels, dev, reps=5):
+    """This library on the reference-GPU workload: the fused linearization (host call to
+    result, synchronised, median of reps) and the linearization + device PCG (float64
+    vectors, the reference's tol and maxiter) + point back-substitution."""
+    import torch
+    from blast3r_b200.plan import BAPlan
+    sc = channel_subset(cached_scene(cfg, n_tracks=n_tracks), channels)
+    o = sc.options
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
+    plan = BAPlan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
+                  optim_P=o['optim_P'], device=dev)
+    p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
+                    t['pix2d_dep'], pix2d=t['pix2d'])
+    lo = BAPlan.lin_opts(weight_z=o['weight_z'], pnorm=o['pnorm'], max_pix_err=o['clip_pix_err'],
+                         huber_delta=o['huber_delta'])
+    outs = plan.new_outputs()
+
+    def lin():
+        return plan.linearize(p, lo, outs)
+
+    def solve():
+        s_ = plan.linearize(p, lo, outs)
+        x, _, _ = plan.pcg(s_.S_vals, s_.precond, s_.b.double())
+        return s_.backsub(x.float())
+
+    def wall(fn):
+        fn()
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(dev)
+            ts.append(time.perf_counter() - t0)
+        return 1e3 * float(np.median(ts))
+    out = {'linearize_ms': round(wall(lin), 3), 'solve_ms': round(wall(solve), 3)}
+    out['linearize_obs_per_s'] = sc.n_obs / (out['linearize_ms'] * 1e-3)
+    del plan, p, outs, t
+    torch.cuda.empty_cache()
+    return out
+
+
+def reference_gpu_record(dev, channels=2, cfg=2):
+    """The reference's own GaussNewtonSolver on this B200 (its compiled CUDA ops, a child
+    process) beside this library on the same workload: configs[cfg]'s scene with its first
+    `channels` depth channels, the depth model the reference's CUDA einsum dispatch covers
+    (extensions/cujac/sfm_jacobian_rigs.cu:965-1006 has no 5-coefficient x 6-pose kernel,
+    so the headline C = 5 workload does not run there)."""
+    ref = run_child('ref-gpu', ['--config', str(cfg), '--channels', str(channels)])
+    rec = {'workload': f'configs[{cfg}] scene, depth channels 0..{channels - 1} (alpha F + beta)',
+           'reference': ref,
+           'what': 'reference: residual_func + GaussNewtonSolver.compute_jacobians + solve_delta up to its PCG '
+                   '(linearize_*) and the whole solve_delta (solve_f64); b200: the fused linearization and the '
+                   'linearization + device PCG + back-substitution; host call to result, synchronised, median'}
+    if 'unavailable' in ref:
+        return rec
+    ours = b200_same_workload(cfg, None, channels, dev)
+    rec['b200'] = ours
+    rec['speedup'] = {'linearize_vs_ref_f32': ref['linearize_f32_ms'] / ours['linearize_ms'],
+                      'linearize_vs_ref_f64': ref['linearize_f64_ms'] / ours['linearize_ms'],
+                      'solve_vs_ref_f64': ref['solve_f64_ms'] / ours['solve_ms']}
+    return rec
 
 
 def internal_ref_cpu(args):
@@ -835,10 +920,9 @@ def run_b200(args):
     if world == 1 and not args.no_extras:
         extras['configs3_latency'] = latency_record(3, dev, n=1000)
         extras['configs1_lm_iterations'] = lm_iterations(1, 10, 2, dev)
-        extras['reference_gpu'] = {
-            'unavailable': REFERENCE_GPU_UNAVAILABLE,
-            'what': 'the reference\'s own GaussNewtonSolver.compute_jacobians -> solve_delta on this B200 with its '
-                    'compiled CUDA ops (bench.py --internal ref-gpu runs it where the configuration is supported)'}
+        if not args.no_reference_gpu:
+            extras['reference_gpu'] = reference_gpu_record(dev)
+            extras['reference_gpu']['headline_workload'] = REFERENCE_GPU_UNAVAILABLE
 
     if rank == 0:
         line = {'metric': METRIC, 'value': head['value'], 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
@@ -847,7 +931,7 @@ def run_b200(args):
                 'data': 'synthetic (seeded generator of the configuration)',
                 'config': dict(head['config'], workload=head['config']['workload'] +
                                (f' with {args.tracks} tracks' if args.tracks else '')),
-                'roofline': head['roofline'], 'clocks': head.get('clocks'), 'e2e': head['e2e'],
+                'roofline': head['roofline'], 'clocks': head.get('clocks'), 'e2e': head.get('e2e'),
                 'gpu_launches': 7 * args.steps,   # prep, points, factor, diag, pairs, fin_max, fin_apply
                 'setup_s': head['setup_s']}
         if 'parity' in head:
