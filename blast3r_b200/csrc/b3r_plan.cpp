@@ -12,9 +12,13 @@
 //     rank's observation-pair lists bucketed by segment, cut into pair tasks;
 //   * the block-sparse pattern of S (upper block triangle) and every destination offset.
 #include <algorithm>
+#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
+#include <mutex>
 #include <numeric>
+#include <pthread.h>
 #include <new>
 #include <thread>
 #include "b3r_plan.h"
@@ -64,15 +68,85 @@ int plan_threads() {
   return (int)std::max(1u, std::min(h ? h : 1u, 32u));
 }
 
-// fn(t, begin, end) over nt contiguous ranges of [0, n), one thread each (the first on the
-// calling thread).
+// The planner's worker threads, started once and kept for the process: plan_threads() - 1
+// workers plus the calling thread.  One parallel section at a time (plans built from several
+// host threads take turns); a section runs task(t) for t in [0, nt) with t = 0 on the caller.
+class PlanPool {
+ public:
+  // The pool is never destroyed (no join at exit).  A child process forked after the pool
+  // started has none of its workers: the fork handler drops the pointer and the child starts
+  // its own pool on first use.
+  static PlanPool& get() {
+    static std::once_flag once;
+    std::call_once(once, [] { pthread_atfork(nullptr, nullptr, [] { instance() = nullptr; }); });
+    static std::mutex mk;
+    std::lock_guard<std::mutex> lk(mk);
+    if (!instance()) instance() = new PlanPool(plan_threads() - 1);
+    return *instance();
+  }
+  int size() const { return (int)workers_.size() + 1; }
+  void run(int nt, const std::function<void(int)>& task) {
+    nt = std::max(1, std::min(nt, size()));
+    if (nt == 1) { task(0); return; }
+    std::lock_guard<std::mutex> section(section_);
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      task_ = &task;
+      n_active_ = nt;
+      pending_ = nt - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    task(0);
+    std::unique_lock<std::mutex> lk(m_);
+    done_.wait(lk, [&] { return pending_ == 0; });
+    task_ = nullptr;
+  }
+
+ private:
+  static PlanPool*& instance() {
+    static PlanPool* p = nullptr;
+    return p;
+  }
+  explicit PlanPool(int n) {
+    for (int w = 0; w < n; ++w) workers_.emplace_back([this, w] { loop(w + 1); });
+    for (auto& t : workers_) t.detach();
+  }
+  void loop(int id) {
+    uint64_t seen = 0;
+    for (;;) {
+      const std::function<void(int)>* task;
+      {
+        std::unique_lock<std::mutex> lk(m_);
+        cv_.wait(lk, [&] { return gen_ != seen; });
+        seen = gen_;
+        if (id >= n_active_) continue;
+        task = task_;
+      }
+      (*task)(id);
+      std::lock_guard<std::mutex> lk(m_);
+      if (--pending_ == 0) done_.notify_one();
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex section_, m_;
+  std::condition_variable cv_, done_;
+  const std::function<void(int)>* task_ = nullptr;
+  uint64_t gen_ = 0;
+  int n_active_ = 0, pending_ = 0;
+};
+
+// fn(t, begin, end) over nt contiguous ranges of [0, n) on the planner's threads (the first
+// range on the calling thread); at most one range per `grain` items, so that small plans (an
+// online window) stay on few threads.
+constexpr int64_t kPlanGrain = 1 << 14;
 template <typename F>
-void parallel_ranges(int64_t n, int nt, F&& fn) {
-  nt = (int)std::max<int64_t>(1, std::min<int64_t>(nt, n));
-  std::vector<std::thread> th;
-  for (int t = 1; t < nt; ++t) th.emplace_back([&, t] { fn(t, n * t / nt, n * (t + 1) / nt); });
-  fn(0, 0, n / nt);
-  for (auto& x : th) x.join();
+void parallel_ranges(int64_t n, int nt, F&& fn, int64_t grain = kPlanGrain) {
+  grain = std::max<int64_t>(grain, 1);
+  nt = (int)std::max<int64_t>(1, std::min<int64_t>(nt, (n + grain - 1) / grain));
+  nt = std::min(nt, PlanPool::get().size());
+  const std::function<void(int)> task = [&](int t) { fn(t, n * t / nt, n * (t + 1) / nt); };
+  PlanPool::get().run(nt, task);
 }
 
 }  // namespace
@@ -187,105 +261,173 @@ static inline bool img_live(const PlanBuild& B, int i) {
 }
 
 static int build_tracks(PlanBuild& B) {
+  // Every O(n_obs) step runs on the planner's threads (plan_threads()); the results are the
+  // same as one sequential pass: each track's observations end up in increasing o.
   const b3r_plan_desc& d = *B.d;
   const int T = d.n_tracks;
+  const int64_t n = d.n_obs;
+  const int nt = plan_threads();
   B.elim.assign(T, 0);
   if (!B.X.zero)
-    for (int t = 0; t < T; ++t) B.elim[t] = B.X.col[t] >= 0;
-  B.obs_live.resize(d.n_obs);
-  for (int64_t o = 0; o < d.n_obs; ++o) B.obs_live[o] = img_live(B, B.img_of[o]);
-  // CSR of observations per eliminated track (all tracks; stable in o)
+    parallel_ranges(T, nt, [&](int, int64_t a, int64_t b) {
+      for (int64_t t = a; t < b; ++t) B.elim[t] = B.X.col[t] >= 0;
+    });
+  B.obs_live.resize(n);
+  parallel_ranges(n, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t o = a; o < b; ++o) B.obs_live[o] = img_live(B, B.img_of[o]);
+  });
+  // CSR of observations per eliminated track (all tracks): counts by relaxed atomic
+  // increments, a prefix sum, an atomic fill, then each track's few observations sorted by o
   B.all_ptr.assign(T + 1, 0);
-  for (int64_t o = 0; o < d.n_obs; ++o)
-    if (B.elim[d.pids[o]]) B.all_ptr[d.pids[o] + 1]++;
+  int* cnt = B.all_ptr.data() + 1;
+  parallel_ranges(n, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t o = a; o < b; ++o) {
+      const int t = d.pids[o];
+      if (B.elim[t]) __atomic_fetch_add(cnt + t, 1, __ATOMIC_RELAXED);
+    }
+  });
   for (int t = 0; t < T; ++t) B.all_ptr[t + 1] += B.all_ptr[t];
   B.all_obs.resize(B.all_ptr[T]);
   {
     std::vector<int> fill(B.all_ptr.begin(), B.all_ptr.end() - 1);
-    for (int64_t o = 0; o < d.n_obs; ++o)
-      if (B.elim[d.pids[o]]) B.all_obs[fill[d.pids[o]]++] = (int)o;
+    parallel_ranges(n, nt, [&](int, int64_t a, int64_t b) {
+      for (int64_t o = a; o < b; ++o) {
+        const int t = d.pids[o];
+        if (B.elim[t]) B.all_obs[__atomic_fetch_add(&fill[t], 1, __ATOMIC_RELAXED)] = (int)o;
+      }
+    });
+    parallel_ranges(T, nt, [&](int, int64_t a, int64_t b) {
+      for (int64_t t = a; t < b; ++t) {
+        int* x = B.all_obs.data() + B.all_ptr[t];
+        const int L = B.all_ptr[t + 1] - B.all_ptr[t];
+        for (int i = 1; i < L; ++i)            // insertion sort: tracks are short
+          for (int j = i; j > 0 && x[j - 1] > x[j]; --j) std::swap(x[j - 1], x[j]);
+      }
+    });
   }
   // local tracks: eliminated, owned, non-empty; ordered by (first image, id)
-  for (int t = 0; t < T; ++t)
-    if (B.owned[t] && B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) B.loc_tracks.push_back(t);
   {
-    // stable counting sort by first image (tracks arrive in id order)
-    std::vector<int> cnt(d.n_imgs + 1, 0), sorted(B.loc_tracks.size());
-    for (int t : B.loc_tracks) cnt[B.img_of[B.all_obs[B.all_ptr[t]]] + 1]++;
-    for (int i = 0; i < d.n_imgs; ++i) cnt[i + 1] += cnt[i];
-    for (int t : B.loc_tracks) sorted[cnt[B.img_of[B.all_obs[B.all_ptr[t]]]]++] = t;
-    B.loc_tracks.swap(sorted);
+    // stable counting sort by first image (tracks in id order within an image)
+    std::vector<int> first(T, -1);
+    parallel_ranges(T, nt, [&](int, int64_t a, int64_t b) {
+      for (int64_t t = a; t < b; ++t)
+        if (B.owned[t] && B.elim[t] && B.all_ptr[t + 1] > B.all_ptr[t]) first[t] = B.img_of[B.all_obs[B.all_ptr[t]]];
+    });
+    std::vector<int> icnt(d.n_imgs + 1, 0);
+    int64_t nloc = 0;
+    for (int t = 0; t < T; ++t)
+      if (first[t] >= 0) { icnt[first[t] + 1]++; ++nloc; }
+    for (int i = 0; i < d.n_imgs; ++i) icnt[i + 1] += icnt[i];
+    B.loc_tracks.resize(nloc);
+    for (int t = 0; t < T; ++t)
+      if (first[t] >= 0) B.loc_tracks[icnt[first[t]]++] = t;
   }
   const int nT = (int)B.loc_tracks.size();
   B.trk_col.resize(nT);
-  for (int tl = 0; tl < nT; ++tl) B.trk_col[tl] = B.X.col[B.loc_tracks[tl]];
-  int64_t n_loc = 0;
-  for (int t : B.loc_tracks) n_loc += B.all_ptr[t + 1] - B.all_ptr[t];
+  B.trk_ptr.assign(nT + 1, 0);
+  parallel_ranges(nT, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t tl = a; tl < b; ++tl) {
+      const int t = B.loc_tracks[tl];
+      B.trk_col[tl] = B.X.col[t];
+      B.trk_ptr[tl + 1] = B.all_ptr[t + 1] - B.all_ptr[t];
+    }
+  });
+  for (int tl = 0; tl < nT; ++tl) B.trk_ptr[tl + 1] += B.trk_ptr[tl];
+  const int64_t n_loc = nT ? B.trk_ptr[nT] : 0;
   B.perm_t.resize(n_loc);
   B.trk_t.resize(n_loc);
   B.img_t.resize(n_loc);
-  B.kof.assign(d.n_obs, -1);
+  B.kof.assign(n, -1);
+  parallel_ranges(nT, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t tl = a; tl < b; ++tl) {
+      const int t = B.loc_tracks[tl];
+      int64_t k = B.trk_ptr[tl];
+      for (int j = B.all_ptr[t]; j < B.all_ptr[t + 1]; ++j, ++k) {
+        const int o = B.all_obs[j];
+        B.perm_t[k] = o;
+        B.trk_t[k] = (int)tl;
+        B.img_t[k] = B.img_of[o];
+        B.kof[o] = (int)k;
+      }
+    }
+  });
   // Point tasks: whole tracks packed greedily into <= 32 observations (one warp); a track
   // longer than 32 gets a task of its own, which the kernels process in rounds.
-  B.trk_ptr.assign(nT + 1, 0);
-  for (int tl = 0; tl < nT; ++tl)
-    B.trk_ptr[tl + 1] = B.trk_ptr[tl] + (B.all_ptr[B.loc_tracks[tl] + 1] - B.all_ptr[B.loc_tracks[tl]]);
-  int64_t k = 0;
-  int cur = 0;          // observations in the open task
-  bool open = false, open_long = false;
-  for (int tl = 0; tl < nT; ++tl) {
-    const int t = B.loc_tracks[tl];
-    const int L = B.all_ptr[t + 1] - B.all_ptr[t];
-    if (open && (open_long || L > kPointTask || cur + L > kPointTask)) open = false;
-    if (!open) {
-      B.pt_task.push_back((int)k);
-      open = true;
-      open_long = false;
-      cur = 0;
+  {
+    int cur = 0;          // observations in the open task
+    bool open = false, open_long = false;
+    for (int tl = 0; tl < nT; ++tl) {
+      const int L = B.trk_ptr[tl + 1] - B.trk_ptr[tl];
+      if (open && (open_long || L > kPointTask || cur + L > kPointTask)) open = false;
+      if (!open) {
+        B.pt_task.push_back(B.trk_ptr[tl]);
+        open = true;
+        open_long = false;
+        cur = 0;
+      }
+      cur += L;
+      open_long = L > kPointTask;
     }
-    for (int j = B.all_ptr[t]; j < B.all_ptr[t + 1]; ++j) {
-      const int o = B.all_obs[j];
-      B.perm_t[k] = o;
-      B.trk_t[k] = tl;
-      B.img_t[k] = B.img_of[o];
-      B.kof[o] = (int)k;
-      ++k;
-    }
-    cur += L;
-    open_long = L > kPointTask;
+    if (nT > 0) B.pt_task.push_back((int)n_loc);
   }
-  if (nT > 0) B.pt_task.push_back((int)k);
-  // image-major chunks over the observations this rank owns (pid in the track range)
-  int last_img = -1, in_chunk = 0;
-  for (int64_t o = 0; o < d.n_obs; ++o) {
-    const int t = d.pids[o];
-    if (!B.owned[t]) continue;
-    if (!B.obs_live[o]) {                  // evaluated for the objective only
-      B.rest_idx.push_back(make_int4((int)o, B.img_of[o], t, 0));
-      continue;
+  // image-major chunks over the observations this rank owns: each thread takes a range of
+  // images (an image's observations are contiguous in o), the ranges are joined in order
+  {
+    struct Part {
+      std::vector<int> obs, k, pid, chunk, img;
+      std::vector<int4> rest;
+    };
+    const int I = d.n_imgs;
+    const int ni = (int)std::max<int64_t>(1, std::min<int64_t>(nt, I));
+    std::vector<Part> part(ni);
+    parallel_ranges(I, ni, [&](int th, int64_t i0, int64_t i1) {
+      Part& P = part[th];
+      for (int64_t i = i0; i < i1; ++i) {
+        const int64_t o0 = i ? d.infos[i - 1] : 0, o1 = d.infos[i];
+        int in_chunk = kDiagChunk;            // a new chunk at the image's first live observation
+        for (int64_t o = o0; o < o1; ++o) {
+          const int t = d.pids[o];
+          if (!B.owned[t]) continue;
+          if (!B.obs_live[o]) {                // evaluated for the objective only
+            P.rest.push_back(make_int4((int)o, (int)i, t, 0));
+            continue;
+          }
+          if (in_chunk == kDiagChunk) {
+            P.chunk.push_back((int)P.obs.size());
+            P.img.push_back((int)i);
+            in_chunk = 0;
+          }
+          P.obs.push_back((int)o);
+          P.k.push_back(B.kof[o]);
+          P.pid.push_back(t);
+          ++in_chunk;
+        }
+      }
+    });
+    for (const Part& P : part) {
+      const int base = (int)B.c1_obs.size();
+      for (int c : P.chunk) B.c1_chunk.push_back(base + c);
+      B.c1_img.insert(B.c1_img.end(), P.img.begin(), P.img.end());
+      B.c1_obs.insert(B.c1_obs.end(), P.obs.begin(), P.obs.end());
+      B.c1_k.insert(B.c1_k.end(), P.k.begin(), P.k.end());
+      B.c1_pid.insert(B.c1_pid.end(), P.pid.begin(), P.pid.end());
+      B.rest_idx.insert(B.rest_idx.end(), P.rest.begin(), P.rest.end());
     }
-    const int i = B.img_of[o];
-    if (i != last_img || in_chunk == kDiagChunk) {
-      B.c1_chunk.push_back((int)B.c1_obs.size());
-      B.c1_img.push_back(i);
-      last_img = i;
-      in_chunk = 0;
-    }
-    B.c1_obs.push_back((int)o);
-    B.c1_k.push_back(B.kof[o]);
-    B.c1_pid.push_back(t);
-    ++in_chunk;
+    B.c1_chunk.push_back((int)B.c1_obs.size());
   }
-  B.c1_chunk.push_back((int)B.c1_obs.size());
   // packed per-observation indices (one 16-byte load per observation in the kernels)
   B.t_idx.resize(B.perm_t.size());
-  for (size_t kk = 0; kk < B.perm_t.size(); ++kk)
-    B.t_idx[kk] = make_int4(B.img_t[kk], B.loc_tracks[B.trk_t[kk]], B.trk_t[kk], B.perm_t[kk]);
+  parallel_ranges((int64_t)B.perm_t.size(), nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t kk = a; kk < b; ++kk)
+      B.t_idx[kk] = make_int4(B.img_t[kk], B.loc_tracks[B.trk_t[kk]], B.trk_t[kk], B.perm_t[kk]);
+  });
   B.c1_idx.resize(B.c1_obs.size());
-  for (size_t e = 0; e < B.c1_obs.size(); ++e) {
-    const int kk = B.c1_k[e];
-    B.c1_idx[e] = make_int4(B.c1_obs[e], kk, B.c1_pid[e], kk >= 0 ? B.trk_t[kk] : -1);
-  }
+  parallel_ranges((int64_t)B.c1_obs.size(), nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t e = a; e < b; ++e) {
+      const int kk = B.c1_k[e];
+      B.c1_idx[e] = make_int4(B.c1_obs[e], kk, B.c1_pid[e], kk >= 0 ? B.trk_t[kk] : -1);
+    }
+  });
   return B3R_OK;
 }
 
@@ -303,6 +445,7 @@ static int build_segments(PlanBuild& B) {
   // each thread takes a contiguous range of row images; per image its partners, sorted
   const int nt = plan_threads();
   std::vector<std::vector<int>> part_col(nt), part_cnt(nt);
+  const int64_t grain = std::max<int64_t>(1, (int64_t)I * 4096 / std::max<int64_t>(d.n_obs, 1));
   parallel_ranges(I, nt, [&](int t, int64_t i0, int64_t i1) {
     std::vector<int> stamp(I, -1), partners;
     std::vector<int>& col = part_col[t];
@@ -324,7 +467,7 @@ static int build_segments(PlanBuild& B) {
       col.insert(col.end(), partners.begin(), partners.end());
       cnt.push_back((int)partners.size());
     }
-  });
+  }, grain);
   B.seg_row_ptr.assign(I + 1, 0);
   B.seg_col.clear();
   int i = 0;
@@ -345,6 +488,9 @@ static inline int64_t seg_lookup(const PlanBuild& B, int i, int i2) {
 
 // This rank's observation pairs, bucketed by segment (stable in local track order), and
 // the pair tasks.
+// tracks per planner thread in the pair passes (a track's pairs grow with its length squared)
+constexpr int64_t kPairGrain = 512;
+
 static int build_pairs(PlanBuild& B) {
   const int64_t S = (int64_t)B.seg_col.size();
   const int64_t nT = (int64_t)B.loc_tracks.size();
@@ -379,7 +525,7 @@ static int build_pairs(PlanBuild& B) {
   parallel_ranges(nT, nt, [&](int t, int64_t a, int64_t b) {
     int64_t* c = cnt.data() + (size_t)t * S;
     for_pairs(a, b, [&](int64_t sg, int, int) { if (sg < 0) ++bad[t]; else c[sg]++; });
-  });
+  }, kPairGrain);
   for (int t = 0; t < nt; ++t) B3R_REQUIRE(bad[t] == 0, "internal: %lld pairs without a segment", (long long)bad[t]);
   B.seg_cnt.assign(S + 1, 0);
   for (int64_t sg = 0; sg < S; ++sg) {
@@ -413,7 +559,7 @@ static int build_pairs(PlanBuild& B) {
       if (pr.x < 0 || pr.y < 0) ++missing[t];
       B.pairs[fill[sg]++] = pr;
     });
-  });
+  }, kPairGrain);
   for (int t = 0; t < nt; ++t)
     B3R_REQUIRE(missing[t] == 0, "internal: pair observation without an image-major slot");
   // Tasks: segments cut into <= kPairTask pairs, in segment order (row image major) so that
