@@ -548,6 +548,7 @@ def lm_iterations(cfg, n_iter, warm, dev, n_tracks=None):
     e1.record()
     torch.cuda.synchronize(dev)
     return {'ms': e0.elapsed_time(e1) / done, 'wall_ms': 1e3 * (time.perf_counter() - tw) / done,
+            'plan_ms': plan_time_ms(sc, dev),
             'iterations': done, 'loss_first': [float(first.init_loss), float(first.new_loss)],
             'loss_last': float(last.new_loss),
             'what': 'engine.lm_step: residual op, fused linearization, PCG on S (tol 1e-6, <= 300 iterations), '
@@ -562,6 +563,7 @@ def latency_record(cfg, dev, n=1000):
     sc = cached_scene(cfg)
     o = sc.options
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in sc.lm_inputs().items()}
+    plan_ms = plan_time_ms(sc, dev)
     plan = BAPlan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
                   optim_P=o['optim_P'], device=dev)
     p = plan.params(t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'], t['pix2d_std'],
@@ -597,7 +599,29 @@ def latency_record(cfg, dev, n=1000):
     dev_ms = e0.elapsed_time(e1) / 100
     del graph
     return {'workload': f'configs[{cfg}]', 'n_obs': sc.n_obs, 'unit': 'ms', 'n': n, 'direct': pct(direct),
-            'cuda_graph': pct(replay), 'device_ms_per_replay': round(dev_ms, 4)}
+            'cuda_graph': pct(replay), 'device_ms_per_replay': round(dev_ms, 4),
+            'plan_ms': plan_ms}
+
+
+def plan_time_ms(sc, dev, reps=3):
+    """Median time of a plan for the scene's structure (BAPlan: the structure read back from the
+    device, b3r_plan_create's host planning and the upload of the plan), synchronised: what a
+    change of the problem structure costs before the first linearization."""
+    import torch
+    from blast3r_b200.plan import BAPlan
+    o = sc.options
+    infos = torch.from_numpy(np.ascontiguousarray(sc.infos)).to(dev)     # device structure tensors, as the
+    pids = torch.from_numpy(np.ascontiguousarray(sc.pids)).to(dev)       # reference's pipeline holds them
+    ts = []
+    for _ in range(reps):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        plan = BAPlan(infos, pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, optim_K=o['optim_K'],
+                      optim_P=o['optim_P'], optim_Z=o['optim_Z'], optim_X=o['optim_X'], device=dev)
+        torch.cuda.synchronize(dev)
+        ts.append(1e3 * (time.perf_counter() - t0))
+        del plan
+    return round(float(np.median(ts)), 2)
 
 
 # ------------------------------------------------------------------------------------------

@@ -1771,7 +1771,8 @@ extern "C" int b3r_linearize_schur_noalloc(b3r_plan* plan, const b3r_params* par
   void* ws = nullptr;
   {
     // The array's host-side name is not a device address: take the real address once per
-    // device, with that device current (check_device above guarantees it).
+    // device, with that device current (check_device above guarantees it).  It stays valid
+    // for the life of the process unless the device is reset (documented in the header).
     std::lock_guard<std::mutex> lock(g_static_ws_mutex);
     if (!g_static_ws_ptr[plan->device]) {
       void* p = nullptr;

@@ -277,7 +277,9 @@ int b3r_linearize_schur(b3r_plan* plan, const b3r_params* params, const b3r_lin_
  * b3r_plan_info.workspace_bytes exceed it are rejected with B3R_E_INVALID (enough for
  * an online window of ~150k observations).  The caller still passes the plan, the
  * parameters and the outputs.  The first call on a device looks up the array's device
- * address (make that first call before any stream capture).  All calls on a device share
+ * address (make that first call before any stream capture); the address is kept for the
+ * life of the process, so do not use this entry point after a cudaDeviceReset of that
+ * device (the library's module, and the array's address, may change).  All calls on a device share
  * the one array, so calls that overlap on the GPU (other streams, other threads) race:
  * serialise them.  Back-substitution after this call is not available (it needs the
  * caller's workspace). */
