@@ -18,7 +18,7 @@
 
 namespace b3r {
 
-constexpr int kPairTask = 2048;    // max observation pairs per pair task
+constexpr int kPairTask = 1024;    // max observation pairs per pair task
 constexpr int kDiagChunk = 1024;   // max observations per per-image diagonal chunk
 constexpr int kPointTask = 32;     // max observations per point task (one warp)
 constexpr int kImgRecFloats = 32;  // floats per per-image camera record

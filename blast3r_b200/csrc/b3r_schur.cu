@@ -15,7 +15,7 @@
 //             its image, reduced per image chunk, one atomic per value per chunk; also
 //             diag(Hcc) for the damping and preconditioner
 //   pairs     segment-major: for every image pair (i, i') the sum over shared tracks of
-//             -Y_o^T Y_o', one CTA per <= 2048-pair task, lane per observation pair, packed
+//             -Y_o^T Y_o', one CTA per <= 1024-pair task, lane per observation pair, packed
 //             float2 FMAs, records staged through shared memory by coalesced cp.async,
 //             one atomic per value per task
 //   finalize  per-type adaptive damping of diag(S) (ba_solver.py:510-517, 572-582) and
