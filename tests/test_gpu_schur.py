@@ -268,3 +268,89 @@ def test_linearization_objective_outputs(cfg, edit):
     assert rel_err(s.residuals.cpu().numpy(), full[:, :3].t().cpu().numpy()) < TOL_OBS
     want = float(full[:, 3:6].double().sum())
     assert abs(float(s.loss_sum) - want) <= 1e-6 * abs(want)
+
+
+def test_schur_entrywise_full_size_against_reference_jacobians():
+    """configs[2] at full size (1,000 images, 1 M tracks, 5.84 M observations), S compared entry
+    by entry (all 11,002 x 11,002 scalars) and b element by element with a float64 system built
+    in torch from the reference's OWN compiled kernels: its residual/weight kernel and its
+    float64 Jacobian kernel (oracle/_ref), then the Schur complement exactly as the reference
+    solver forms it (ba_solver.py:123-188): W clamped, A = J_c^T W J_c, D = Hpp + lambda_p I,
+    S = A - sum over same-track observation pairs Hpc_o^T D^-1 Hpc_o', b = g_c - Hpc^T D^-1 g_p.
+    Nothing of this library's linearization is used on the reference side."""
+    from oracle import build_ref
+    ext = build_ref.load_built()
+    if ext is None:
+        pytest.skip('reference extension not built (oracle/_ref)')
+    sc = make_scene(2)
+    inp, opts = scene_inputs(sc), dict(sc.options)
+    plan, s = run_plan(inp, opts)
+    S_ours = s.to_dense()
+    t = to_cuda(inp)
+    del inp
+    res = ext.residuals_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'], t['pts3d'],
+                                  t['pids'], t['pix2d'], t['pix2d_std'], t['pix2d_dep'], True, opts['weight_z'],
+                                  opts['pnorm'], opts['clip_pix_err'], opts['huber_delta'], 1e-16)
+    r, _, w = [x.contiguous() for x in res.view(-1, 3, 3).unbind(dim=1)]
+    Jc8, Jz, Jp = ext.jacobians_with_rigs(t['infos'], t['K'], t['P_rig2cam'], t['P_w2rig'], t['z_coefs'],
+                                          t['pts3d'], t['pids'], t['pix2d_std'], t['pix2d_dep'], True, True)
+    n, C = Jz.shape[0], Jz.shape[2]
+    Wd = w.clamp(1e-6, 1e6).double()
+    sW = Wd.sqrt()
+    Jc = torch.zeros(n, 3, 8 + C, dtype=torch.float64, device='cuda')
+    Jc[:, :, :8] = Jc8
+    Jc[:, 2, 8:] = Jz[:, 0]
+    Jcw = Jc * sW[:, :, None]
+    Jpw = Jp * sW[:, :, None]
+    del Jc, Jc8, Jz, Jp, res
+    img = torch.searchsorted(t['infos'][0].long(), torch.arange(n, device='cuda'), right=True)
+    cam, node = t['infos'][2].long()[img], t['infos'][1].long()[img]
+    ncp = plan.n_cam_params
+    cols = torch.cat([2 * cam[:, None] + torch.arange(2, device='cuda'),
+                      plan.info.off_P + 6 * node[:, None] + torch.arange(6, device='cuda'),
+                      plan.info.off_Z + C * img[:, None] + torch.arange(C, device='cuda')], 1)     # [n, 13]
+    pid = t['pids'].long()
+    T = sc.n_tracks
+    Hpp = torch.zeros(T, 3, 3, dtype=torch.float64, device='cuda').index_add_(0, pid, torch.einsum('nki,nkj->nij', Jpw, Jpw))
+    lam_p = 1e-12 * torch.diagonal(Hpp, dim1=1, dim2=2).max()
+    Dinv = torch.linalg.inv(Hpp + lam_p * torch.eye(3, dtype=torch.float64, device='cuda'))
+    del Hpp
+    Hpc = torch.einsum('nki,nkj->nij', Jpw, Jcw)                                   # [n, 3, 13]
+    sWr = sW * r.double()
+    g_c = torch.zeros(ncp, dtype=torch.float64, device='cuda').index_add_(
+        0, cols.reshape(-1), torch.einsum('nkj,nk->nj', Jcw, sWr).reshape(-1))
+    g_p = torch.zeros(T, 3, dtype=torch.float64, device='cuda').index_add_(0, pid, torch.einsum('nkj,nk->nj', Jpw, sWr))
+    Dg = torch.einsum('tij,tj->ti', Dinv, g_p)
+    b_ref = g_c - torch.zeros_like(g_c).index_add_(0, cols.reshape(-1), torch.einsum('nij,ni->nj', Hpc, Dg[pid]).reshape(-1))
+    err_b = rel_err(s.b.cpu().numpy(), b_ref.cpu().numpy())
+    assert err_b < TOL_B, err_b
+    del g_c, g_p, Dg, b_ref, Jpw
+    S_ref = torch.zeros(ncp * ncp, dtype=torch.float64, device='cuda')
+    W13 = cols.shape[1]
+
+    def scatter(rows, colsb, vals):          # S_ref[rows_i, cols_j] += vals_ij (flattened)
+        S_ref.index_add_(0, (rows[..., :, None] * ncp + colsb[..., None, :]).reshape(-1), vals.reshape(-1))
+    for a in range(0, n, 1 << 20):         # A = sum_o J_c^T W J_c
+        sl = slice(a, a + (1 << 20))
+        scatter(cols[sl], cols[sl], torch.einsum('nki,nkj->nij', Jcw[sl], Jcw[sl]))
+    del Jcw
+    Z = torch.einsum('nij,njk->nik', Dinv[pid], Hpc)                                # D^-1 Hpc
+    del Dinv
+    order = torch.argsort(pid, stable=True)
+    cnt = torch.bincount(pid, minlength=T)
+    start = torch.cumsum(cnt, 0) - cnt
+    for L in torch.unique(cnt).tolist():   # fill-in: every same-track pair (o, o'), o == o' included
+        if L == 0:
+            continue
+        trk = torch.nonzero(cnt == L).squeeze(1)
+        step = max(1, (1 << 26) // (L * L * W13 * W13))
+        for c0 in range(0, len(trk), step):
+            idx = order[start[trk[c0:c0 + step]][:, None] + torch.arange(L, device='cuda')]   # [m, L]
+            P = torch.einsum('mari,mbrj->mabij', Hpc[idx], Z[idx])                          # [m, L, L, 13, 13]
+            ci = cols[idx]
+            S_ref.index_add_(0, (ci[:, :, None, :, None] * ncp + ci[:, None, :, None, :]).reshape(-1), -P.reshape(-1))
+    S_ref = S_ref.view(ncp, ncp)
+    S_ref += torch.diag(s.precond.double() - s.diagA.double())      # the per-type damping lambda on diag(S)
+    err = float((S_ours - S_ref).abs().max() / S_ref.abs().max())
+    print(f'configs[2] full size: S max|diff| / max|S| = {err:.2e}, b {err_b:.2e}')
+    assert err < TOL_ACC, err
