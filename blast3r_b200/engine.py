@@ -1,8 +1,8 @@
-"""Levenberg-Marquardt step on the B200 solver: the reference's ``lm_step``
+"""Levenberg-Marquardt on the B200 solver: the reference's ``lm_step``
 (inference/engine.py:206-334) with the same arguments, update rules, line search and return
-values, running ``blast3r_b200.ba_solver`` and the library's residual op.  The reference's
-phase loop ``bundle_adjustment`` (engine.py:405-503) calls ``lm_step`` and is not mirrored
-here.
+values, running ``blast3r_b200.ba_solver`` and the library's residual op, and its phase loop
+``bundle_adjustment`` (engine.py:405-503) on top of it, taking the reference's own rig and
+track objects.
 
 The dense tangent prior (``weight_tan > 0``, engine.py:15-158, 253-299) runs on the
 library's ``b3r_tangent_prior`` kernel (``blast3r_b200.prior``).  With
@@ -190,3 +190,106 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
                                                   delta_zcf, delta_pts, init_loss, init_residuals, min_reproj,
                                                   min_loss_delta, verbose)
     return update, BA_Status(init_loss, init_residuals, new_loss, new_residuals)
+
+
+def iter_on(*iterators):
+    """The reference's phase schedule (engine.py:364-383): every argument is a scalar or a list;
+    lists of length one are broadcast, the others must share one length; yields one tuple of
+    values per phase."""
+    iterable = lambda it: isinstance(it, (tuple, list))   # noqa: E731
+    max_len = max([len(it) for it in iterators if iterable(it)] + [1])
+    its = []
+    for it in iterators:
+        if iterable(it):
+            assert len(it) in (1, max_len), f'missing {max_len - len(it)} values for parameter={it}'
+            its.append(it[0] if len(it) == 1 else it)
+        else:
+            its.append(it)
+    for step in range(max_len):
+        yield tuple(it[step] if iterable(it) else it for it in its)
+
+
+def _todevice(x, device):
+    if x is None:
+        return None
+    if isinstance(x, (list, tuple)):
+        return type(x)(_todevice(v, device) for v in x)
+    return x.to(device) if isinstance(x, torch.Tensor) else x
+
+
+def bundle_adjustment(rigs_data, track_data, pts3d=None, z_coefs=None, max_iters=1000, pnorm=0.5, optim_P=True,
+                      optim_Z=True, optim_Z0=True, optim_K=True, optim_X=True, weight_z=0.1, dense_depth=None,
+                      dense_conf=None, dense_pts3d_ref=None, tangent_reg=0.0, tan_stride=4, normalize_tangents=True,
+                      n_zcfs=None, no_Jfz=False, max_n_phases=-1, device='cuda', verbose=True, **other_lm_kwargs):
+    """The reference's main bundle-adjustment loop (engine.py:405-503) on this library's
+    ``lm_step``: the same arguments, phase schedule (scalars or per-phase lists, ``iter_on``),
+    per-phase depth-channel changes (``n_zcfs``: coefficients dropped or zero-padded, the first
+    log-depth channel kept and frozen unless 2 or all channels are used), the same stopping
+    rule (each phase iterates until a step does not lower the loss or ``max_iters``) and the
+    same return value (``rigs_data.update(K, P_rig2cam, P_w2rig, z_coefs)``, ``pts3d``).
+
+    ``rigs_data`` and ``track_data`` are the reference's ``RigsData`` and ``ObservedTracks``
+    (any objects with their attributes: ``to``, ``infos``, ``K``, ``P_rig2cam``, ``P_w2rig``,
+    ``depth_mode``, ``n_imgs``, ``update``, ``z_coefs_from_scale``; ``pids``, ``pix2d``,
+    ``pix2d_std``, ``pix2d_dep``).  Each phase's LM iterations run in float64 solves with
+    adaptive damping 1e-12, as in the reference."""
+    trk = track_data.to(device)
+    rig = rigs_data.to(device)
+    dense_depth = _todevice(dense_depth, device)
+    dense_conf = _todevice(dense_conf, device)
+    dense_pts3d_ref = _todevice(dense_pts3d_ref, device)
+    if z_coefs is None:
+        z_coefs = rig.z_coefs_from_scale(trk)
+    original_pix2d_dep = trk.pix2d_dep
+    pts3d = _todevice(pts3d, device)
+    assert pts3d is not None, 'the 3D points must be initialized before bundle adjustment'
+    variables = dict(K=rig.K, P_rig2cam=rig.P_rig2cam, P_w2rig=rig.P_w2rig, z_coefs=z_coefs, pts3d=pts3d)
+    phase_num = 0
+    for pnorm, max_iters, optim_K, optim_P, optim_Z, optim_X, weight_z, n_zcfs, tangent_reg in \
+            iter_on(pnorm, max_iters, optim_K, optim_P, optim_Z, optim_X, weight_z, n_zcfs, tangent_reg):
+        phase_num += 1
+        if phase_num > (max_n_phases % 1000):
+            break
+        dense_depth_use = dense_depth
+        if n_zcfs is not None:               # remove or add depth coefficients for this phase
+            z_coefs = variables['z_coefs']
+            optim_Z0 = True
+            if rig.depth_mode[:3] == 'log':
+                optim_Z0 = (n_zcfs == 2) or (n_zcfs == original_pix2d_dep.shape[1])
+                n_zcfs += not optim_Z0       # the first channel stays in, unoptimized
+            trk.pix2d_dep = original_pix2d_dep[:, :n_zcfs].contiguous()
+            if dense_depth is not None:
+                assert len(dense_depth) == rig.n_imgs, 'log_depth_maps must be n_imgs x (H, W, C)'
+                assert all(d.shape[-1] >= n_zcfs for d in dense_depth), \
+                    'not enough dense depth channels for the requested n_zcfs'
+                dense_depth_use = [d[..., :n_zcfs] for d in dense_depth]
+            if n_zcfs < z_coefs.shape[1]:
+                assert n_zcfs >= 1
+                variables['z_coefs'] = z_coefs[:, :n_zcfs].contiguous()
+            elif n_zcfs > z_coefs.shape[1]:
+                assert trk.pix2d_dep.shape[1] == n_zcfs, 'not enough multi-depthmaps in the original data'
+                variables['z_coefs'] = torch.cat((z_coefs, z_coefs.new_zeros((len(z_coefs), n_zcfs - z_coefs.shape[1]))),
+                                                 dim=1).contiguous()
+        if verbose:
+            print(f"Starting phase {phase_num}, with {variables['z_coefs'].shape[1]} z-coefs.")
+        it = 0
+        while it < max_iters:
+            update, status = lm_step(rig.infos(trk), trk.pids, trk.pix2d, trk.pix2d_std, trk.pix2d_dep, **variables,
+                                     log_depth_maps=dense_depth_use, conf=dense_conf, pts3d_ref=dense_pts3d_ref,
+                                     weight_tan=tangent_reg, tan_stride=tan_stride,
+                                     normalize_tangents=normalize_tangents, optim_K=optim_K, optim_Z=optim_Z,
+                                     optim_P=optim_P, optim_X=optim_X, optim_Z0=optim_Z0, pnorm=pnorm,
+                                     weight_z=weight_z, no_grad_f_from_rz=no_Jfz, depth_mode=rig.depth_mode,
+                                     dampen=1e-12, adaptive_dampen=True, dtype=torch.float64, **other_lm_kwargs)
+            if verbose:
+                before, after = float(reproj_score(status.init_residuals)), float(reproj_score(status.new_residuals))
+                avg_focal = float((update['K'][:, 0, 0].mean() + update['K'][:, 1, 1].mean()) / 2)
+                print(f'Loss at iter={it}: {float(status.init_loss):.3f} --> {float(status.new_loss):.3f}, '
+                      f'reproj_score: {before:.3f} --> {after:.3f}, avg_focal={avg_focal:.2f}')
+            if status.new_loss >= status.init_loss:
+                break
+            variables.update(update)
+            it += 1
+    trk.pix2d_dep = original_pix2d_dep       # restore
+    pts3d = variables.pop('pts3d')
+    return rigs_data.update(**variables), pts3d
