@@ -600,7 +600,44 @@ def latency_record(cfg, dev, n=1000):
     del graph
     return {'workload': f'configs[{cfg}]', 'n_obs': sc.n_obs, 'unit': 'ms', 'n': n, 'direct': pct(direct),
             'cuda_graph': pct(replay), 'device_ms_per_replay': round(dev_ms, 4),
-            'plan_ms': plan_ms}
+            'plan_ms': plan_ms, 'online_planning': online_plan_record(cfg, dev)}
+
+
+def online_plan_record(cfg, dev):
+    """Planning cost of the online loop's track merges (inference/pipeline.py:196-224) over the
+    configuration's frames: each frame's problem (the earlier frames' tracks, then the new
+    frame's, ObservedTracks.__or__ layout) planned from scratch (b3r_plan_create) and appended to
+    the previous frame's plan (b3r_plan_append).  Each plan is timed from the device structure
+    tensors to the uploaded plan, synchronised."""
+    import torch
+    from blast3r_b200.plan import BAPlan
+    from blast3r_b200.synthetic import OnlineSequence
+    seq = OnlineSequence(cached_scene(cfg))
+    frames = []
+    for q in range(1, seq.sc.n_imgs):
+        s = seq.frame(q)
+        frames.append((torch.from_numpy(np.ascontiguousarray(s.infos)).to(dev),
+                       torch.from_numpy(np.ascontiguousarray(s.pids)).to(dev), s.n_cams, s.n_nodes, s.n_tracks,
+                       s.n_zcf, s.n_obs))
+
+    def run(incremental):
+        prev, ts = None, []
+        for infos, pids, nc, nn, nt, C, _ in frames:
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            plan = BAPlan(infos, pids, nc, nn, nt, C, device=dev, retain=incremental,
+                          base=prev if incremental else None)
+            torch.cuda.synchronize(dev)
+            ts.append(1e3 * (time.perf_counter() - t0))
+            prev = plan if incremental else None
+        return ts
+    run(True)
+    full, inc = run(False), run(True)
+    return {'frames': len(frames), 'unit': 'ms',
+            'last_frame': {'n_obs': frames[-1][6], 'create_ms': round(full[-1], 2), 'append_ms': round(inc[-1], 2)},
+            'all_frames': {'create_ms': round(sum(full), 1), 'append_ms': round(sum(inc), 1)},
+            'what': 'plan of each online frame (old | new): b3r_plan_create from scratch vs b3r_plan_append to the '
+                    'previous frame\'s plan, structure read back from the device, plan uploaded'}
 
 
 def plan_time_ms(sc, dev, reps=3):

@@ -29,7 +29,7 @@ class PlanDesc(C.Structure):
                 ('mode_K', _i32), ('mode_P', _i32), ('mode_Z', _i32), ('mode_X', _i32),
                 ('mask_K', _pu8), ('mask_P', _pu8), ('mask_Z', _pu8), ('mask_X', _pu8),
                 ('track_begin', _i32), ('track_end', _i32), ('device', _i32), ('obs_local', _i32),
-                ('track_owner', _pi32), ('rank', _i32)]
+                ('track_owner', _pi32), ('rank', _i32), ('retain', _i32)]
 
 
 class PlanInfo(C.Structure):
@@ -82,6 +82,7 @@ _SIGS = {
     'b3r_fused_einsum_bki_bkj': (C.c_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, C.c_int,
                                            C.c_int, C.c_int, C.c_int, _vp]),
     'b3r_plan_create': (C.c_int, [C.POINTER(_vp), C.POINTER(PlanDesc)]),
+    'b3r_plan_append': (C.c_int, [C.POINTER(_vp), _vp, C.POINTER(PlanDesc)]),
     'b3r_plan_destroy': (C.c_int, [_vp]),
     'b3r_plan_get_info': (C.c_int, [_vp, C.POINTER(PlanInfo)]),
     'b3r_plan_get_pattern': (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),

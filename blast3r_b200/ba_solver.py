@@ -18,6 +18,7 @@ it they read the ``residuals`` / ``w_pts`` handed to ``solve_delta``, as the ref
 """
 import torch
 
+from . import _lib as L
 from .plan import BAPlan
 
 N_FOC = 2
@@ -42,6 +43,11 @@ class Linearization:
 
 _PLAN_CACHE = []        # (key, structure tensors, plan), most recent last
 _PLAN_CACHE_MAX = 8
+# Plans of at most this many observations keep their host-side lists, so that the next
+# structure of an online loop (the merge old | new of inference/pipeline.py:196-224) is planned
+# incrementally (b3r_plan_append); the host memory they hold is about 40 B per observation plus
+# 8 B per observation pair.
+INCREMENTAL_MAX_OBS = 1 << 22
 
 
 def _structure(rigs, pids, modes):
@@ -53,13 +59,29 @@ def _same(a, b):
     return a.shape == b.shape and a.dtype == b.dtype and a.device == b.device and torch.equal(a, b)
 
 
+def _append_candidate(key, n_imgs, n_obs, n_cams, n_nodes, n_tracks, C):
+    """The most recently used cached plan that kept its host state, if the new structure can
+    extend it (sizes only grow, same C and enable flags); b3r_plan_append checks the rest."""
+    if not _PLAN_CACHE:
+        return None
+    k, _, plan = _PLAN_CACHE[-1]
+    if not getattr(plan, 'retained', False) or k[5] != C or k[6] != key[6]:
+        return None
+    if (plan.n_imgs <= n_imgs and plan.n_obs <= n_obs and plan.n_cams <= n_cams and plan.n_nodes <= n_nodes
+            and plan.n_tracks <= n_tracks):
+        return plan
+    return None
+
+
 def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=True, optim_Z=True,
              optim_X=True, device=None):
     """Plan for this structure, reused while the structure tensors hold the same values.
 
     A cached plan is returned only when ``rigs``, ``pids`` and every bool mask are equal,
     element by element, to the copies taken when it was built (one device comparison per
-    call), so a reordering or an in-place edit of the structure always gets a new plan."""
+    call), so a reordering or an in-place edit of the structure always gets a new plan.  A
+    structure that extends the last plan's the way the online loop merges tracks gets its plan
+    by b3r_plan_append (incremental: only the new tracks are planned)."""
     modes = (optim_K, optim_P, optim_Z, optim_X)
     key = (tuple(rigs.shape), tuple(pids.shape), n_cams, n_nodes, n_tracks, C,
            tuple(m if isinstance(m, bool) else ('mask', tuple(m.shape)) for m in modes))
@@ -68,8 +90,18 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
         if k == key and len(saved) == len(cur) and all(_same(a, b) for a, b in zip(cur, saved)):
             _PLAN_CACHE.append(_PLAN_CACHE.pop(j))
             return plan
-    plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
-                  optim_Z=optim_Z, optim_X=optim_X, device=device)
+    retain = len(pids) <= INCREMENTAL_MAX_OBS
+    plan = None
+    base = _append_candidate(key, rigs.shape[1], len(pids), n_cams, n_nodes, n_tracks, C) if retain else None
+    if base is not None:
+        try:
+            plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
+                          optim_Z=optim_Z, optim_X=optim_X, device=device, retain=True, base=base)
+        except L.B3RError:     # not an extension of the last plan (tracks removed, reordered...)
+            plan = None
+    if plan is None:
+        plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
+                      optim_Z=optim_Z, optim_X=optim_X, device=device, retain=retain)
     if len(_PLAN_CACHE) >= _PLAN_CACHE_MAX:
         _PLAN_CACHE.pop(0)
     _PLAN_CACHE.append((key, [t.detach().clone() for t in cur], plan))

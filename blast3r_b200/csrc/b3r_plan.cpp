@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <numeric>
 #include <pthread.h>
@@ -260,6 +261,47 @@ static inline bool img_live(const PlanBuild& B, int i) {
   return B.img_bk[3 * i] >= 0 || B.img_bk[3 * i + 1] >= 0 || B.img_bk[3 * i + 2] >= 0;
 }
 
+static void build_image_major(PlanBuild& B);
+static void pack_indices(PlanBuild& B);
+
+// Eliminated tracks (point type enabled) and live observations (their image has an active
+// block).
+static void build_flags(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int nt = plan_threads();
+  B.elim.assign(d.n_tracks, 0);
+  if (!B.X.zero)
+    parallel_ranges(d.n_tracks, nt, [&](int, int64_t a, int64_t b) {
+      for (int64_t t = a; t < b; ++t) B.elim[t] = B.X.col[t] >= 0;
+    });
+  B.obs_live.resize(d.n_obs);
+  parallel_ranges(d.n_obs, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t o = a; o < b; ++o) B.obs_live[o] = img_live(B, B.img_of[o]);
+  });
+}
+
+// Point tasks of local tracks [tl0, nT): whole tracks packed greedily into <= 32
+// observations (one warp); a track longer than 32 gets a task of its own, which the kernels
+// process in rounds.  Appends to pt_task, then its end sentinel.
+static void pack_point_tasks(PlanBuild& B, int tl0) {
+  const int nT = (int)B.loc_tracks.size();
+  int cur = 0;          // observations in the open task
+  bool open = false, open_long = false;
+  for (int tl = tl0; tl < nT; ++tl) {
+    const int L = B.trk_ptr[tl + 1] - B.trk_ptr[tl];
+    if (open && (open_long || L > kPointTask || cur + L > kPointTask)) open = false;
+    if (!open) {
+      B.pt_task.push_back(B.trk_ptr[tl]);
+      open = true;
+      open_long = false;
+      cur = 0;
+    }
+    cur += L;
+    open_long = L > kPointTask;
+  }
+  if (nT > 0) B.pt_task.push_back(B.trk_ptr[nT]);
+}
+
 static int build_tracks(PlanBuild& B) {
   // Every O(n_obs) step runs on the planner's threads (plan_threads()); the results are the
   // same as one sequential pass: each track's observations end up in increasing o.
@@ -267,15 +309,7 @@ static int build_tracks(PlanBuild& B) {
   const int T = d.n_tracks;
   const int64_t n = d.n_obs;
   const int nt = plan_threads();
-  B.elim.assign(T, 0);
-  if (!B.X.zero)
-    parallel_ranges(T, nt, [&](int, int64_t a, int64_t b) {
-      for (int64_t t = a; t < b; ++t) B.elim[t] = B.X.col[t] >= 0;
-    });
-  B.obs_live.resize(n);
-  parallel_ranges(n, nt, [&](int, int64_t a, int64_t b) {
-    for (int64_t o = a; o < b; ++o) B.obs_live[o] = img_live(B, B.img_of[o]);
-  });
+  build_flags(B);
   // CSR of observations per eliminated track (all tracks): counts by relaxed atomic
   // increments, a prefix sum, an atomic fill, then each track's few observations sorted by o
   B.all_ptr.assign(T + 1, 0);
@@ -351,27 +385,20 @@ static int build_tracks(PlanBuild& B) {
       }
     }
   });
-  // Point tasks: whole tracks packed greedily into <= 32 observations (one warp); a track
-  // longer than 32 gets a task of its own, which the kernels process in rounds.
-  {
-    int cur = 0;          // observations in the open task
-    bool open = false, open_long = false;
-    for (int tl = 0; tl < nT; ++tl) {
-      const int L = B.trk_ptr[tl + 1] - B.trk_ptr[tl];
-      if (open && (open_long || L > kPointTask || cur + L > kPointTask)) open = false;
-      if (!open) {
-        B.pt_task.push_back(B.trk_ptr[tl]);
-        open = true;
-        open_long = false;
-        cur = 0;
-      }
-      cur += L;
-      open_long = L > kPointTask;
-    }
-    if (nT > 0) B.pt_task.push_back((int)n_loc);
-  }
-  // image-major chunks over the observations this rank owns: each thread takes a range of
-  // images (an image's observations are contiguous in o), the ranges are joined in order
+  pack_point_tasks(B, 0);
+  build_image_major(B);
+  pack_indices(B);
+  return B3R_OK;
+}
+
+// Image-major chunks over the observations this rank owns (c1_*, rest_idx), from the track
+// side's kof: each thread takes a range of images (an image's observations are contiguous
+// in o), the ranges are joined in order.
+static void build_image_major(PlanBuild& B) {
+  const b3r_plan_desc& d = *B.d;
+  const int nt = plan_threads();
+  B.c1_obs.clear(); B.c1_k.clear(); B.c1_pid.clear(); B.c1_chunk.clear(); B.c1_img.clear();
+  B.rest_idx.clear();
   {
     struct Part {
       std::vector<int> obs, k, pid, chunk, img;
@@ -415,7 +442,11 @@ static int build_tracks(PlanBuild& B) {
     }
     B.c1_chunk.push_back((int)B.c1_obs.size());
   }
-  // packed per-observation indices (one 16-byte load per observation in the kernels)
+}
+
+// Packed per-observation indices (one 16-byte load per observation in the kernels).
+static void pack_indices(PlanBuild& B) {
+  const int nt = plan_threads();
   B.t_idx.resize(B.perm_t.size());
   parallel_ranges((int64_t)B.perm_t.size(), nt, [&](int, int64_t a, int64_t b) {
     for (int64_t kk = a; kk < b; ++kk)
@@ -428,7 +459,6 @@ static int build_tracks(PlanBuild& B) {
       B.c1_idx[e] = make_int4(B.c1_obs[e], kk, B.c1_pid[e], kk >= 0 ? B.trk_t[kk] : -1);
     }
   });
-  return B3R_OK;
 }
 
 }  // namespace b3r
@@ -490,6 +520,8 @@ static inline int64_t seg_lookup(const PlanBuild& B, int i, int i2) {
 // the pair tasks.
 // tracks per planner thread in the pair passes (a track's pairs grow with its length squared)
 constexpr int64_t kPairGrain = 512;
+
+static void build_tasks(PlanBuild& B);
 
 static int build_pairs(PlanBuild& B) {
   const int64_t S = (int64_t)B.seg_col.size();
@@ -562,10 +594,17 @@ static int build_pairs(PlanBuild& B) {
   }, kPairGrain);
   for (int t = 0; t < nt; ++t)
     B3R_REQUIRE(missing[t] == 0, "internal: pair observation without an image-major slot");
-  // Tasks: segments cut into <= kPairTask pairs, in segment order (row image major) so that
-  // the records of a row image and of its window of partner images stay in L2 while its
-  // tasks run; within one row image the longest tasks go first so the short ones fill in
-  // behind them.  The pair lists stay in segment order; a task is a (segment, range).
+  build_tasks(B);
+  return B3R_OK;
+}
+
+// Tasks: segments cut into <= kPairTask pairs, in segment order (row image major) so that
+// the records of a row image and of its window of partner images stay in L2 while its
+// tasks run; within one row image the longest tasks go first so the short ones fill in
+// behind them.  The pair lists stay in segment order; a task is a (segment, range).
+static void build_tasks(PlanBuild& B) {
+  const int64_t S = (int64_t)B.seg_col.size();
+  const int64_t P = B.seg_cnt[S];
   std::vector<std::pair<int64_t, int64_t>> cuts;   // (first pair, segment)
   for (int64_t s = 0; s < S; ++s)
     for (int64_t p = B.seg_cnt[s]; p < B.seg_cnt[s + 1]; p += kPairTask) cuts.emplace_back(p, s);
@@ -588,7 +627,6 @@ static int build_pairs(PlanBuild& B) {
     B.task_seg[t] = (int)cuts[ord[t]].second;
   }
   B.task_pb[cuts.size()] = P;
-  return B3R_OK;
 }
 
 static inline int pat_lookup(const PlanBuild& B, int p, int q) {
@@ -908,25 +946,309 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 using namespace b3r;
 
-extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
-  B3R_REQUIRE(out != nullptr && desc != nullptr, "NULL argument");
-  *out = nullptr;
-  PlanBuild B;
+namespace b3r {
+
+// Host state a plan built with b3r_plan_desc.retain keeps for b3r_plan_append: the old
+// problem's structure and the parts of its build that an appended problem reuses.
+struct PlanState {
+  b3r_plan_desc desc{};                   // the problem's sizes and modes (pointers cleared)
+  std::vector<int32_t> infos, pids;       // copies of its structure arrays
+  std::vector<char> elim, img_live;       // [n_tracks] eliminated, [n_imgs] has an active block
+  std::vector<int> loc_tracks, trk_ptr, perm_t, trk_t, img_t, pt_task, kof;
+  std::vector<int> seg_row_ptr, seg_col;
+  std::vector<int64_t> seg_cnt;
+  std::vector<int2> pairs;
+};
+
+}  // namespace b3r
+
+// retain (and b3r_plan_append) cover single-rank plans: every track owned, global inputs.
+static int check_retain(const b3r_plan_desc& d) {
+  B3R_REQUIRE(d.retain == 0 || d.retain == 1, "retain must be 0 or 1");
+  if (d.retain)
+    B3R_REQUIRE(d.track_owner == nullptr && d.track_begin == 0 && d.track_end == d.n_tracks && !d.obs_local,
+                "retain needs a single-rank plan (every track owned, obs_local 0)");
+  return B3R_OK;
+}
+
+static int retain_state(PlanBuild& B, b3r_plan* P) {
+  try {
+    std::unique_ptr<PlanState> S(new PlanState());
+    const b3r_plan_desc& d = *B.d;
+    S->desc = d;
+    S->desc.infos = S->desc.pids = S->desc.track_owner = nullptr;
+    S->desc.mask_K = S->desc.mask_P = S->desc.mask_Z = S->desc.mask_X = nullptr;
+    S->infos.assign(d.infos, d.infos + 3 * (size_t)d.n_imgs);
+    S->pids.assign(d.pids, d.pids + d.n_obs);
+    S->img_live.resize(d.n_imgs);
+    for (int i = 0; i < d.n_imgs; ++i) S->img_live[i] = img_live(B, i);
+    S->elim = std::move(B.elim);
+    S->loc_tracks = std::move(B.loc_tracks); S->trk_ptr = std::move(B.trk_ptr);
+    S->perm_t = std::move(B.perm_t); S->trk_t = std::move(B.trk_t); S->img_t = std::move(B.img_t);
+    S->pt_task = std::move(B.pt_task); S->kof = std::move(B.kof);
+    S->seg_row_ptr = std::move(B.seg_row_ptr); S->seg_col = std::move(B.seg_col);
+    S->seg_cnt = std::move(B.seg_cnt); S->pairs = std::move(B.pairs);
+    P->state = S.release();
+    return B3R_OK;
+  } catch (const std::bad_alloc&) {
+    return fail(B3R_E_NOMEM, "host allocation failed while keeping the plan's host state");
+  }
+}
+
+// The local track, image-major, segment and pair lists of the merged problem B.d (old | new,
+// as ObservedTracks.__or__ builds it, inference/tracks.py:96-117) from the old plan's
+// retained state.  Old tracks keep their local order, point tasks and pair lists (their
+// observation indices and image-major slots shifted by the new observations inserted before
+// them); the new tracks follow, ordered by (first image, id) among themselves.
+static int build_appended(PlanBuild& B, const PlanState& O) {
+  const b3r_plan_desc& d = *B.d;
+  const b3r_plan_desc& d0 = O.desc;
+  const int I = d.n_imgs, I0 = d0.n_imgs, T = d.n_tracks, T0 = d0.n_tracks;
+  const int nt = plan_threads();
+  B3R_REQUIRE(d.C == d0.C, "not an extension: C=%d, the old plan's %d", d.C, d0.C);
+  B3R_REQUIRE(I >= I0 && T >= T0 && d.n_cams >= d0.n_cams && d.n_nodes >= d0.n_nodes,
+              "not an extension: fewer images, tracks, cameras or nodes than the old plan");
+  const int32_t* cum = d.infos;
+  const int32_t* cum0 = O.infos.data();
+  build_flags(B);
+  for (int t = 0; t < T0; ++t)
+    B3R_REQUIRE(B.elim[t] == O.elim[t], "not an extension: track %d changes its point status", t);
+  // every old image's observations come first in its range, unchanged
+  std::vector<int64_t> s_new(I + 1, 0), n_old(I, 0), add_o(I0, 0);
+  for (int i = 0; i < I; ++i) s_new[i + 1] = cum[i];
+  for (int i = 0; i < I0; ++i) {
+    const int64_t s0 = i ? cum0[i - 1] : 0;
+    n_old[i] = cum0[i] - s0;
+    B3R_REQUIRE(cum[I + i] == cum0[I0 + i] && cum[2 * I + i] == cum0[2 * I0 + i],
+                "not an extension: image %d changes its node or camera", i);
+    B3R_REQUIRE(img_live(B, i) == (bool)O.img_live[i], "not an extension: image %d changes its active blocks", i);
+    B3R_REQUIRE(s_new[i + 1] - s_new[i] >= n_old[i], "not an extension: image %d has fewer observations", i);
+    B3R_REQUIRE(std::equal(d.pids + s_new[i], d.pids + s_new[i] + n_old[i], O.pids.data() + s0),
+                "not an extension: image %d does not start with the old plan's observations", i);
+    add_o[i] = s_new[i] - s0;
+  }
+  // observations after them belong to new tracks: their per-track lists, in increasing o
+  const int nN = T - T0;
+  std::vector<int> nptr(nN + 1, 0);
+  for (int i = 0; i < I; ++i)
+    for (int64_t o = s_new[i] + n_old[i]; o < s_new[i + 1]; ++o) {
+      const int t = d.pids[o];
+      B3R_REQUIRE(t >= T0, "not an extension: new observation %lld of image %d has old track %d", (long long)o, i, t);
+      if (B.elim[t]) nptr[t - T0 + 1]++;
+    }
+  for (int j = 0; j < nN; ++j) nptr[j + 1] += nptr[j];
+  std::vector<int> nobs(nptr[nN]);
+  {
+    std::vector<int> fill(nptr.begin(), nptr.end() - 1);
+    for (int i = 0; i < I; ++i)
+      for (int64_t o = s_new[i] + n_old[i]; o < s_new[i + 1]; ++o) {
+        const int t = d.pids[o];
+        if (B.elim[t]) nobs[fill[t - T0]++] = (int)o;
+      }
+  }
+  // new local tracks (eliminated, non-empty), ordered by (first image, id)
+  std::vector<int> new_loc;
+  {
+    std::vector<int> icnt(I + 1, 0), first(nN, -1);
+    for (int j = 0; j < nN; ++j)
+      if (nptr[j + 1] > nptr[j]) { first[j] = B.img_of[nobs[nptr[j]]]; icnt[first[j] + 1]++; }
+    for (int i = 0; i < I; ++i) icnt[i + 1] += icnt[i];
+    new_loc.resize(icnt[I]);
+    for (int j = 0; j < nN; ++j)
+      if (first[j] >= 0) new_loc[icnt[first[j]]++] = T0 + j;
+  }
+  const int nT0 = (int)O.loc_tracks.size();
+  const int64_t nloc0 = (int64_t)O.perm_t.size();
+  const int nT = nT0 + (int)new_loc.size();
+  B.loc_tracks.resize(nT);
+  std::copy(O.loc_tracks.begin(), O.loc_tracks.end(), B.loc_tracks.begin());
+  std::copy(new_loc.begin(), new_loc.end(), B.loc_tracks.begin() + nT0);
+  B.trk_col.resize(nT);
+  for (int tl = 0; tl < nT; ++tl) B.trk_col[tl] = B.X.col[B.loc_tracks[tl]];
+  B.trk_ptr.assign(nT + 1, 0);
+  std::copy(O.trk_ptr.begin(), O.trk_ptr.begin() + nT0 + 1, B.trk_ptr.begin());
+  for (int j = 0; j < (int)new_loc.size(); ++j) {
+    const int jn = new_loc[j] - T0;
+    B.trk_ptr[nT0 + j + 1] = B.trk_ptr[nT0 + j] + (nptr[jn + 1] - nptr[jn]);
+  }
+  const int64_t n_loc = B.trk_ptr[nT];
+  B.perm_t.resize(n_loc);
+  B.trk_t.resize(n_loc);
+  B.img_t.resize(n_loc);
+  parallel_ranges(nloc0, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t k = a; k < b; ++k) {
+      B.perm_t[k] = (int)(O.perm_t[k] + add_o[O.img_t[k]]);
+      B.trk_t[k] = O.trk_t[k];
+      B.img_t[k] = O.img_t[k];
+    }
+  });
+  B.kof.assign(d.n_obs, -1);
+  for (int i = 0; i < I0; ++i)
+    std::copy(O.kof.begin() + (s_new[i] - add_o[i]), O.kof.begin() + (s_new[i] - add_o[i] + n_old[i]),
+              B.kof.begin() + s_new[i]);
+  for (int j = 0; j < (int)new_loc.size(); ++j) {
+    const int jn = new_loc[j] - T0;
+    int64_t k = B.trk_ptr[nT0 + j];
+    for (int q = nptr[jn]; q < nptr[jn + 1]; ++q, ++k) {
+      const int o = nobs[q];
+      B.perm_t[k] = o;
+      B.trk_t[k] = nT0 + j;
+      B.img_t[k] = B.img_of[o];
+      B.kof[o] = (int)k;
+    }
+  }
+  B.pt_task = O.pt_task;
+  if (!B.pt_task.empty()) B.pt_task.pop_back();   // the old end sentinel
+  pack_point_tasks(B, nT0);
+  build_image_major(B);
+  pack_indices(B);
+  // image-major slot of each image's first observation (every observation of an image with an
+  // active block has one, in o order: every track is this rank's), merged and old
+  std::vector<int64_t> c1s(I + 1, 0), c1s0(I0 + 1, 0);
+  for (int i = 0; i < I; ++i) c1s[i + 1] = c1s[i] + (img_live(B, i) ? s_new[i + 1] - s_new[i] : 0);
+  for (int i = 0; i < I0; ++i) c1s0[i + 1] = c1s0[i] + (O.img_live[i] ? n_old[i] : 0);
+  B3R_REQUIRE(c1s[I] == (int64_t)B.c1_obs.size(), "internal: image-major entries of the merged plan");
+  // pairs (a < b) of live observations of the new local tracks
+  auto for_new_pairs = [&](auto&& fn) {
+    for (int tl = nT0; tl < nT; ++tl)
+      for (int64_t ka = B.trk_ptr[tl]; ka < B.trk_ptr[tl + 1]; ++ka) {
+        if (!B.obs_live[B.perm_t[ka]]) continue;
+        for (int64_t kb = ka + 1; kb < B.trk_ptr[tl + 1]; ++kb)
+          if (B.obs_live[B.perm_t[kb]]) fn(B.img_t[ka], B.img_t[kb], ka, kb);
+      }
+  };
+  // segments: each row image's old partners merged with the new tracks' partners
+  std::vector<uint64_t> keys;
+  for_new_pairs([&](int ia, int ib, int64_t, int64_t) { keys.push_back((uint64_t)ia * (uint64_t)I + (uint64_t)ib); });
+  std::sort(keys.begin(), keys.end());
+  keys.erase(std::unique(keys.begin(), keys.end()), keys.end());
+  B.seg_row_ptr.assign(I + 1, 0);
+  B.seg_col.clear();
+  std::vector<int64_t> old_seg;   // old segment of each merged segment, -1: new
+  {
+    size_t kk = 0;
+    for (int i = 0; i < I; ++i) {
+      const int ob = i < I0 ? O.seg_row_ptr[i] : 0, oe = i < I0 ? O.seg_row_ptr[i + 1] : 0;
+      int ia = ob;
+      for (;;) {
+        const bool has_new = kk < keys.size() && keys[kk] / (uint64_t)I == (uint64_t)i;
+        if (ia == oe && !has_new) break;
+        const int ca = ia < oe ? O.seg_col[ia] : I;
+        const int cb = has_new ? (int)(keys[kk] % (uint64_t)I) : I;
+        if (ca <= cb) {
+          B.seg_col.push_back(ca);
+          old_seg.push_back(ia);
+          ++ia;
+          if (ca == cb) ++kk;
+        } else {
+          B.seg_col.push_back(cb);
+          old_seg.push_back(-1);
+          ++kk;
+        }
+      }
+      B.seg_row_ptr[i + 1] = (int)B.seg_col.size();
+    }
+  }
+  const int64_t S = (int64_t)B.seg_col.size();
+  std::vector<int64_t> ncnt(S, 0);
+  int64_t bad = 0;
+  for_new_pairs([&](int ia, int ib, int64_t, int64_t) {
+    const int64_t sg = seg_lookup(B, ia, ib);
+    if (sg < 0) ++bad; else ncnt[sg]++;
+  });
+  B3R_REQUIRE(bad == 0, "internal: %lld new pairs without a segment", (long long)bad);
+  B.seg_cnt.assign(S + 1, 0);
+  std::vector<int> row_of_seg(S);
+  for (int i = 0; i < I; ++i)
+    for (int sg = B.seg_row_ptr[i]; sg < B.seg_row_ptr[i + 1]; ++sg) row_of_seg[sg] = i;
+  auto old_cnt = [&](int64_t sg) { return old_seg[sg] < 0 ? 0 : O.seg_cnt[old_seg[sg] + 1] - O.seg_cnt[old_seg[sg]]; };
+  for (int64_t sg = 0; sg < S; ++sg) B.seg_cnt[sg + 1] = B.seg_cnt[sg] + old_cnt(sg) + ncnt[sg];
+  B.pairs.resize(B.seg_cnt[S]);
+  // old pairs, their image-major slots shifted by the new entries before them
+  parallel_ranges(S, nt, [&](int, int64_t a, int64_t b) {
+    for (int64_t sg = a; sg < b; ++sg) {
+      const int64_t os = old_seg[sg];
+      if (os < 0) continue;
+      const int i = row_of_seg[sg], i2 = B.seg_col[sg];
+      const int ex = (int)(c1s[i] - c1s0[i]), ey = (int)(c1s[i2] - c1s0[i2]);
+      int2* dst = B.pairs.data() + B.seg_cnt[sg];
+      for (int64_t p = O.seg_cnt[os]; p < O.seg_cnt[os + 1]; ++p, ++dst)
+        *dst = make_int2(O.pairs[p].x + ex, O.pairs[p].y + ey);
+    }
+  }, 256);
+  // new pairs after them, in local track order
+  std::vector<int> e_of_k(n_loc - nloc0, -1);
+  for (int i = 0; i < I; ++i) {
+    if (!img_live(B, i)) continue;
+    for (int64_t o = s_new[i] + n_old[i]; o < s_new[i + 1]; ++o) {
+      const int k = B.kof[o];
+      const int64_t e = c1s[i] + (o - s_new[i]);
+      B3R_REQUIRE(B.c1_obs[e] == (int)o, "internal: image-major slot of observation %lld", (long long)o);
+      if (k >= nloc0) e_of_k[k - nloc0] = (int)e;
+    }
+  }
+  std::vector<int64_t> fill(S);
+  for (int64_t sg = 0; sg < S; ++sg) fill[sg] = B.seg_cnt[sg] + old_cnt(sg);
+  for_new_pairs([&](int ia, int ib, int64_t ka, int64_t kb) {
+    B.pairs[fill[seg_lookup(B, ia, ib)]++] = make_int2(e_of_k[ka - nloc0], e_of_k[kb - nloc0]);
+  });
+  build_tasks(B);
+  return B3R_OK;
+}
+
+static void init_build(PlanBuild& B, const b3r_plan_desc* desc) {
   B.d = desc;
   if (desc->device >= 0) {
     int n_sm = 0;
     if (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, desc->device) == cudaSuccess && n_sm > 0)
       B.pcg_target_groups = n_sm;
   }
+}
+
+static int finish_plan(PlanBuild& B, b3r_plan** out);
+
+extern "C" int b3r_plan_append(b3r_plan** out, const b3r_plan* old, const b3r_plan_desc* desc) {
+  B3R_REQUIRE(out != nullptr && old != nullptr && desc != nullptr, "NULL argument");
+  *out = nullptr;
+  B3R_REQUIRE(old->state != nullptr,
+              "the old plan keeps no host state to append to (build it with b3r_plan_desc.retain = 1)");
+  B3R_REQUIRE(desc->track_owner == nullptr && desc->track_begin == 0 && desc->track_end == desc->n_tracks &&
+              !desc->obs_local, "b3r_plan_append builds single-rank plans (every track owned, obs_local 0)");
+  B3R_TRY(check_retain(*desc));
+  PlanBuild B;
+  init_build(B, desc);
+  try {
+    B3R_TRY(build_maps(B));
+    B3R_TRY(build_appended(B, *old->state));
+    B3R_TRY(build_pattern(B));
+    return finish_plan(B, out);
+  } catch (const std::bad_alloc&) {
+    return fail(B3R_E_NOMEM, "host allocation failed while planning");
+  }
+}
+
+extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
+  B3R_REQUIRE(out != nullptr && desc != nullptr, "NULL argument");
+  *out = nullptr;
+  PlanBuild B;
+  init_build(B, desc);
+  B3R_TRY(check_retain(*desc));
   try {
     B3R_TRY(build_maps(B));
     B3R_TRY(build_tracks(B));
     B3R_TRY(build_segments(B));
     B3R_TRY(build_pairs(B));
     B3R_TRY(build_pattern(B));
+    return finish_plan(B, out);
   } catch (const std::bad_alloc&) {
     return fail(B3R_E_NOMEM, "host allocation failed while planning");
   }
+}
+
+// Everything after the build_* steps: the device copy of the plan, the workspace layout and
+// the info record; keeps the host state for b3r_plan_append when the desc asks for it.
+static int finish_plan(PlanBuild& B, b3r_plan** out) {
+  const b3r_plan_desc* desc = B.d;
   const bool host_only = desc->device < 0;   // planning only: pattern/info queries, no kernels
   int prev_dev = 0;
   if (!host_only) {
@@ -1051,6 +1373,10 @@ extern "C" int b3r_plan_create(b3r_plan** out, const b3r_plan_desc* desc) {
   I.depth_stitch = d.zonly;
   I.pcg_row_groups = d.n_pcg_groups;
   I.pcg_resident = d.pcg_resident;
+  if (desc->retain) {
+    const int rc = retain_state(B, P);
+    if (rc != B3R_OK) { b3r_plan_destroy(P); return rc; }
+  }
   *out = P;
   return B3R_OK;
 }
@@ -1065,6 +1391,7 @@ extern "C" int b3r_plan_destroy(b3r_plan* plan) {
     e = cudaFree(plan->dev_mem);
     cudaSetDevice(prev);
   }
+  delete plan->state;
   delete plan;
   return check_cuda(e, "b3r_plan_destroy");
 }

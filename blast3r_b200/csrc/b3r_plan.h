@@ -152,6 +152,10 @@ struct HostPattern {
   std::vector<int> row_ptr, col_idx, val_off, bsize, boff;
 };
 
+// Host state a plan keeps for b3r_plan_append (b3r_plan.cpp); null unless the plan was built
+// with b3r_plan_desc.retain.
+struct PlanState;
+
 }  // namespace b3r
 
 struct b3r_plan {
@@ -169,4 +173,5 @@ struct b3r_plan {
   std::vector<int> in_obs;   // global observation of each input row (empty: the identity)
   bool staged = false;
   const void* staged_src[3] = {nullptr, nullptr, nullptr};
+  b3r::PlanState* state = nullptr;   // owned; freed by b3r_plan_destroy
 };

@@ -50,7 +50,15 @@ class SchurSystem:
 class BAPlan:
     def __init__(self, infos, pids, n_cams, n_nodes, n_tracks, n_zcf, optim_K=True, optim_P=True,
                  optim_Z=True, optim_X=True, track_range=None, device=None, obs_local=False, track_owner=None,
-                 rank=0):
+                 rank=0, retain=False, base=None):
+        """Plan one BA phase's structure.
+
+        ``retain`` keeps the host-side track, segment and pair lists so that a later plan can
+        be appended to this one.  ``base``: an earlier plan built with ``retain`` whose problem
+        this one extends the way the online loop merges tracks (``old | new``,
+        inference/tracks.py:96-117; images, tracks, cameras and nodes only added, every old
+        image's observations first in its range): the plan is then built incrementally by
+        ``b3r_plan_append`` (``B3RError`` if the structure does not extend ``base``)."""
         infos_h = np.ascontiguousarray(torch.as_tensor(infos).detach().cpu().numpy().astype(np.int32))
         pids_h = np.ascontiguousarray(torch.as_tensor(pids).detach().cpu().numpy().astype(np.int32))
         n_imgs = infos_h.shape[1]
@@ -85,9 +93,14 @@ class BAPlan:
                           track_begin=t0, track_end=t1,
                           device=device.index if device.type == 'cuda' else -1, obs_local=int(bool(obs_local)),
                           track_owner=owner.ctypes.data_as(C.POINTER(C.c_int32)) if owner is not None else None,
-                          rank=int(rank))
+                          rank=int(rank), retain=int(bool(retain)))
         self._h = C.c_void_p()
-        L.call('b3r_plan_create', C.byref(self._h), C.byref(desc))
+        if base is None:
+            L.call('b3r_plan_create', C.byref(self._h), C.byref(desc))
+        else:
+            L.call('b3r_plan_append', C.byref(self._h), base.handle, C.byref(desc))
+        self.retained = bool(retain)
+        self.appended = base is not None
         self.info = L.PlanInfo()
         L.call('b3r_plan_get_info', self._h, C.byref(self.info))
         i = self.info

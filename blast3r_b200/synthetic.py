@@ -270,3 +270,46 @@ def make_scene(cfg, seed=None, n_tracks=None, n_imgs=None, dtype_check=True):
                  truth=dict(K=K_true.astype(np.float32), P_w2rig=P_true.astype(np.float32),
                             pts3d=pts.astype(np.float32)),
                  meta=meta)
+
+
+class OnlineSequence:
+    """A scene as the online loop grows it, one frame at a time (inference/pipeline.py:196-224).
+
+    After frame q the problem holds images 0..q and every track whose last observation is in
+    an image <= q.  Each frame's tracks are appended after the earlier ones with the next ids
+    and, inside every image, their observations follow the earlier tracks' observations: the
+    layout ``ObservedTracks.__or__`` gives the merge ``old | new`` (inference/tracks.py:96-117).
+    ``frame(q)`` returns that problem as a ``Scene`` (initial parameters of the full scene).
+    """
+
+    def __init__(self, sc):
+        I, T = sc.n_imgs, sc.n_tracks
+        img = np.repeat(np.arange(I), np.diff(np.concatenate([[0], sc.infos[0]])))
+        last = np.full(T, -1)
+        np.maximum.at(last, sc.pids, img)
+        t_order = np.lexsort((np.arange(T), last))          # tracks by (last image, id)
+        new_id = np.empty(T, np.int64)
+        new_id[t_order] = np.arange(T)
+        pids = new_id[sc.pids]
+        self.rows = np.lexsort((pids, img))                  # image-major, then new track id
+        self.pids = pids[self.rows].astype(np.int32)
+        self.img = img[self.rows]
+        self.t_order = t_order
+        self.n_upto = np.searchsorted(last[t_order], np.arange(I), side='right')
+        self.sc = sc
+
+    def frame(self, q):
+        sc = self.sc
+        nt = int(self.n_upto[q])
+        keep = (self.img <= q) & (self.pids < nt)
+        rows = self.rows[keep]
+        nppi = np.bincount(self.img[keep], minlength=q + 1)
+        cam_ids = sc.infos[2, :q + 1]
+        n_cams = int(cam_ids.max()) + 1
+        infos = np.stack([np.cumsum(nppi), np.arange(q + 1), cam_ids]).astype(np.int32)
+        return Scene(name=f'{sc.name}-frame{q}', n_imgs=q + 1, n_cams=n_cams, n_nodes=q + 1, n_tracks=nt,
+                     infos=infos, pids=np.ascontiguousarray(self.pids[keep]),
+                     pix2d=sc.pix2d[rows], pix2d_std=sc.pix2d_std[rows], pix2d_dep=sc.pix2d_dep[rows],
+                     K=sc.K[:n_cams], P_rig2cam=sc.P_rig2cam[:n_cams], P_w2rig=sc.P_w2rig[:q + 1],
+                     z_coefs=sc.z_coefs[:q + 1], pts3d=sc.pts3d[self.t_order[:nt]],
+                     options=dict(sc.options), meta=dict(sc.meta, frame=q))

@@ -158,6 +158,11 @@ typedef struct {
                                          (any partition, e.g. by first image, so that a
                                          rank's tracks share images) instead of the range */
     int32_t rank;
+    int32_t retain;                   /* 1: the plan keeps its host-side track, segment and
+                                         pair lists so that b3r_plan_append can extend it
+                                         (single-rank plans: every track owned, obs_local 0);
+                                         costs host memory of about 40 B per observation
+                                         plus 8 B per observation pair */
 } b3r_plan_desc;
 
 typedef struct {
@@ -190,6 +195,23 @@ typedef struct {
  * Replaces the structure discovery the reference redoes every iteration inside
  * HStackMat.gram_matrix / OneBlockPerRow.__matmul__obpc_obpr (ba_solver.py:854-924). */
 int b3r_plan_create(b3r_plan** plan, const b3r_plan_desc* desc);
+
+/* Incremental planning for the online track merge.  `desc` describes the merged problem
+ * `old | new` the way ObservedTracks.__or__ (inference/tracks.py:96-117) builds it for the
+ * online loop (inference/pipeline.py:196-224): every image of `old` keeps its node, camera
+ * and observations, which come first in its range; observations after them, and all
+ * observations of images added at the end, belong to new tracks (ids >= old n_tracks);
+ * nodes, cameras, images and tracks are only added.  Builds the merged plan from the
+ * host state `old` retained (b3r_plan_desc.retain): old tracks keep their local order,
+ * point tasks and pair lists (observation and image-major indices shifted), only the new
+ * tracks are sorted, paired and bucketed, and the S pattern and solver tables are rebuilt.
+ * The result is a plan for `desc` like b3r_plan_create's (same S pattern, same systems up
+ * to summation order); it retains its own state when desc->retain is set.  `old` is not
+ * changed.  Returns B3R_E_INVALID, naming the first difference, when `desc` does not
+ * extend `old` (track removal, reordering, other rules), in which case the caller plans
+ * from scratch.  No counterpart in the reference, which rediscovers the structure every
+ * iteration (ba_solver.py:854-924). */
+int b3r_plan_append(b3r_plan** plan, const b3r_plan* old, const b3r_plan_desc* desc);
 int b3r_plan_destroy(b3r_plan* plan);
 int b3r_plan_get_info(const b3r_plan* plan, b3r_plan_info* info);
 
