@@ -957,22 +957,33 @@ def run_b200(args):
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=600), device_id=dev)
     peak, peak_kind = measured_peaks()
 
+    wall = {}                     # wall-clock seconds of each part of this run
+    t_run = time.perf_counter()
+
+    def lap(name, t0):
+        wall[name] = round(time.perf_counter() - t0, 1)
+        return time.perf_counter()
+    t0 = time.perf_counter()
     wl = Workload(args.config, args.tracks, world, rank, dev, obs_local=world > 1)
     head = measure_workload(wl, args.steps, args.warmup, peak, peak_kind, want_clocks=True,
                             e2e_steps=args.e2e_steps)
+    t0 = lap('headline', t0)
     sc = wl.sc
     extras = {}
     if not args.no_extras:
         if world == 1:
             extras['latency_per_linearization'] = latency_record(args.config, dev, n=200)
+            t0 = lap('latency', t0)
             extras['ms_per_lm_iteration'] = lm_iterations(args.config, 3, 3, dev, n_tracks=args.tracks)
         else:
             extras['ms_per_lm_iteration'] = sharded_lm_iteration(args, dev, world, rank)
+        t0 = lap('lm_iterations', t0)
     wl.release()
     del wl
     if not args.no_configs4:
         wl4 = Workload(4, args.configs4_tracks, world, rank, dev, obs_local=world > 1)
         r4 = measure_workload(wl4, args.configs4_steps, 3, peak, peak_kind, want_clocks=False, e2e_steps=4)
+        t0 = lap('configs4', t0)
         r4['note'] = ('the depth-stitch phase of configs[4] (scripts/xps/co3d_offline.sh:38 second phase): focal '
                       'and poses fixed, only depth-coefficient blocks in S; measured like the headline step')
         extras['configs4'] = r4
@@ -980,10 +991,13 @@ def run_b200(args):
         del wl4
     if world == 1 and not args.no_extras:
         extras['configs3_latency'] = latency_record(3, dev, n=1000)
+        t0 = lap('configs3', t0)
         extras['configs1_lm_iterations'] = lm_iterations(1, 10, 2, dev)
+        t0 = lap('configs1', t0)
         if not args.no_reference_gpu:
             extras['reference_gpu'] = reference_gpu_record(dev)
             extras['reference_gpu']['headline_workload'] = REFERENCE_GPU_UNAVAILABLE
+            t0 = lap('reference_gpu', t0)
 
     if rank == 0:
         line = {'metric': METRIC, 'value': head['value'], 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
@@ -1000,6 +1014,9 @@ def run_b200(args):
         line.update(extras)
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_baseline(args.config, args.cpu_sample_tracks)
+            t0 = lap('cpu_baseline', t0)
+        wall['total'] = round(time.perf_counter() - t_run, 1)
+        line['wall_s'] = wall
         sys.stdout.flush()
         os.write(json_fd, (json.dumps(line) + '\n').encode())
     if world > 1:

@@ -391,73 +391,80 @@ static int build_tracks(PlanBuild& B) {
   return B3R_OK;
 }
 
-// Image-major chunks over the observations this rank owns (c1_*, rest_idx), from the track
-// side's kof: each thread takes a range of images (an image's observations are contiguous
-// in o), the ranges are joined in order.
+// Image-major chunks over the observations this rank owns (c1_*, rest_idx, c1_idx), from the
+// track side's kof.  An observation's image decides whether it is live, so one count per image
+// (owned observations; all of them when every track is this rank's) places every image's
+// entries; the images are then filled in parallel, straight into the final arrays.
 static void build_image_major(PlanBuild& B) {
   const b3r_plan_desc& d = *B.d;
   const int nt = plan_threads();
-  B.c1_obs.clear(); B.c1_k.clear(); B.c1_pid.clear(); B.c1_chunk.clear(); B.c1_img.clear();
-  B.rest_idx.clear();
-  {
-    struct Part {
-      std::vector<int> obs, k, pid, chunk, img;
-      std::vector<int4> rest;
-    };
-    const int I = d.n_imgs;
-    const int ni = (int)std::max<int64_t>(1, std::min<int64_t>(nt, I));
-    std::vector<Part> part(ni);
-    parallel_ranges(I, ni, [&](int th, int64_t i0, int64_t i1) {
-      Part& P = part[th];
-      for (int64_t i = i0; i < i1; ++i) {
-        const int64_t o0 = i ? d.infos[i - 1] : 0, o1 = d.infos[i];
-        int in_chunk = kDiagChunk;            // a new chunk at the image's first live observation
+  const int I = d.n_imgs;
+  const int32_t* cum = d.infos;
+  const bool all_owned = !d.track_owner && d.track_begin == 0 && d.track_end == d.n_tracks;
+  std::vector<int64_t> own(I, 0);
+  parallel_ranges(I, nt, [&](int, int64_t i0, int64_t i1) {
+    for (int64_t i = i0; i < i1; ++i) {
+      const int64_t o0 = i ? cum[i - 1] : 0, o1 = cum[i];
+      if (all_owned) {
+        own[i] = o1 - o0;
+      } else {
+        int64_t c = 0;
+        for (int64_t o = o0; o < o1; ++o) c += B.owned[d.pids[o]];
+        own[i] = c;
+      }
+    }
+  }, std::max<int64_t>(1, (int64_t)I * kPlanGrain / std::max<int64_t>(d.n_obs, 1)));
+  std::vector<int64_t> e0(I + 1, 0), r0(I + 1, 0);
+  std::vector<int> ch0(I + 1, 0);
+  for (int i = 0; i < I; ++i) {
+    const bool live = img_live(B, i);
+    e0[i + 1] = e0[i] + (live ? own[i] : 0);
+    r0[i + 1] = r0[i] + (live ? 0 : own[i]);
+    ch0[i + 1] = ch0[i] + (live ? (int)((own[i] + kDiagChunk - 1) / kDiagChunk) : 0);
+  }
+  const int64_t n_c1 = e0[I];
+  B.c1_obs.resize(n_c1); B.c1_k.resize(n_c1); B.c1_pid.resize(n_c1); B.c1_idx.resize(n_c1);
+  B.c1_chunk.resize(ch0[I] + 1); B.c1_img.resize(ch0[I]);
+  B.rest_idx.resize(r0[I]);
+  parallel_ranges(I, nt, [&](int, int64_t i0, int64_t i1) {
+    for (int64_t i = i0; i < i1; ++i) {
+      const int64_t o0 = i ? cum[i - 1] : 0, o1 = cum[i];
+      if (!img_live(B, (int)i)) {            // evaluated for the objective only
+        int64_t r = r0[i];
         for (int64_t o = o0; o < o1; ++o) {
           const int t = d.pids[o];
-          if (!B.owned[t]) continue;
-          if (!B.obs_live[o]) {                // evaluated for the objective only
-            P.rest.push_back(make_int4((int)o, (int)i, t, 0));
-            continue;
-          }
-          if (in_chunk == kDiagChunk) {
-            P.chunk.push_back((int)P.obs.size());
-            P.img.push_back((int)i);
-            in_chunk = 0;
-          }
-          P.obs.push_back((int)o);
-          P.k.push_back(B.kof[o]);
-          P.pid.push_back(t);
-          ++in_chunk;
+          if (B.owned[t]) B.rest_idx[r++] = make_int4((int)o, (int)i, t, 0);
         }
+        continue;
       }
-    });
-    for (const Part& P : part) {
-      const int base = (int)B.c1_obs.size();
-      for (int c : P.chunk) B.c1_chunk.push_back(base + c);
-      B.c1_img.insert(B.c1_img.end(), P.img.begin(), P.img.end());
-      B.c1_obs.insert(B.c1_obs.end(), P.obs.begin(), P.obs.end());
-      B.c1_k.insert(B.c1_k.end(), P.k.begin(), P.k.end());
-      B.c1_pid.insert(B.c1_pid.end(), P.pid.begin(), P.pid.end());
-      B.rest_idx.insert(B.rest_idx.end(), P.rest.begin(), P.rest.end());
+      for (int c = ch0[i]; c < ch0[i + 1]; ++c) {
+        B.c1_chunk[c] = (int)(e0[i] + (int64_t)(c - ch0[i]) * kDiagChunk);
+        B.c1_img[c] = (int)i;
+      }
+      int64_t e = e0[i];
+      for (int64_t o = o0; o < o1; ++o) {
+        const int t = d.pids[o];
+        if (!all_owned && !B.owned[t]) continue;
+        const int kk = B.kof[o];
+        B.c1_obs[e] = (int)o;
+        B.c1_k[e] = kk;
+        B.c1_pid[e] = t;
+        B.c1_idx[e] = make_int4((int)o, kk, t, kk >= 0 ? B.trk_t[kk] : -1);
+        ++e;
+      }
     }
-    B.c1_chunk.push_back((int)B.c1_obs.size());
-  }
+  }, std::max<int64_t>(1, (int64_t)I * kPlanGrain / std::max<int64_t>(d.n_obs, 1)));
+  B.c1_chunk[ch0[I]] = (int)n_c1;
 }
 
-// Packed per-observation indices (one 16-byte load per observation in the kernels).
+// Packed per-observation indices of the track side (one 16-byte load per observation in the
+// kernels); the image-major side's (c1_idx) are written by build_image_major.
 static void pack_indices(PlanBuild& B) {
   const int nt = plan_threads();
   B.t_idx.resize(B.perm_t.size());
   parallel_ranges((int64_t)B.perm_t.size(), nt, [&](int, int64_t a, int64_t b) {
     for (int64_t kk = a; kk < b; ++kk)
       B.t_idx[kk] = make_int4(B.img_t[kk], B.loc_tracks[B.trk_t[kk]], B.trk_t[kk], B.perm_t[kk]);
-  });
-  B.c1_idx.resize(B.c1_obs.size());
-  parallel_ranges((int64_t)B.c1_obs.size(), nt, [&](int, int64_t a, int64_t b) {
-    for (int64_t e = a; e < b; ++e) {
-      const int kk = B.c1_k[e];
-      B.c1_idx[e] = make_int4(B.c1_obs[e], kk, B.c1_pid[e], kk >= 0 ? B.trk_t[kk] : -1);
-    }
   });
 }
 
@@ -922,19 +929,43 @@ struct Arena {
   void add(const std::vector<T>& v, const T** dst) { add_raw(v.data(), v.size() * sizeof(T), (void**)dst); }
   template <typename T>
   void add_mut(size_t count, T** dst) { add_raw(nullptr, count * sizeof(T), (void**)dst); }
-  void add_raw(const void* src, size_t bytes, void** dst) {
-    items.push_back({src, bytes, dst, total});
-    total += (bytes + 255) & ~size_t(255);
-  }
+  void add_raw(const void* src, size_t bytes, void** dst) { items.push_back({src, bytes, dst, 0}); }
+  // Layout: the small constant pieces first, packed into one host image and copied at once (an
+  // online plan has ~40 pieces of a few KB, whose separate synchronous copies cost more than
+  // their bytes), then the large constant pieces (one copy each, no host staging), then the
+  // pieces the kernels fill (nothing copied).
+  static constexpr size_t kSmall = size_t(1) << 20;
   int upload(void** base) {
+    auto pad = [](size_t b) { return (b + 255) & ~size_t(255); };
+    total = 0;
+    for (int pass = 0; pass < 3; ++pass)
+      for (auto& it : items) {
+        const int cls = !it.src ? 2 : (it.bytes < kSmall ? 0 : 1);
+        if (cls != pass) continue;
+        it.off = total;
+        total += pad(it.bytes);
+      }
+    size_t small_end = 0;
+    for (auto& it : items)
+      if (it.src && it.bytes < kSmall) small_end = std::max(small_end, it.off + it.bytes);
     if (total == 0) total = 256;
+    std::vector<char> img;
+    try {
+      img.assign(small_end, 0);
+    } catch (const std::bad_alloc&) {
+      return fail(B3R_E_NOMEM, "host allocation failed for the plan's upload image");
+    }
     B3R_TRY(check_cuda(cudaMalloc(base, total), "plan cudaMalloc"));
     for (auto& it : items) {
-      char* p = (char*)*base + it.off;
-      *it.dst = p;
-      if (it.src && it.bytes)
-        B3R_TRY(check_cuda(cudaMemcpy(p, it.src, it.bytes, cudaMemcpyHostToDevice), "plan upload"));
+      *it.dst = (char*)*base + it.off;
+      if (!it.src || !it.bytes) continue;
+      if (it.bytes < kSmall)
+        std::memcpy(img.data() + it.off, it.src, it.bytes);
+      else
+        B3R_TRY(check_cuda(cudaMemcpy(*it.dst, it.src, it.bytes, cudaMemcpyHostToDevice), "plan upload"));
     }
+    if (small_end)
+      B3R_TRY(check_cuda(cudaMemcpy(*base, img.data(), small_end, cudaMemcpyHostToDevice), "plan upload"));
     return B3R_OK;
   }
 };
@@ -1000,6 +1031,8 @@ static int retain_state(PlanBuild& B, b3r_plan* P) {
 // retained state.  Old tracks keep their local order, point tasks and pair lists (their
 // observation indices and image-major slots shifted by the new observations inserted before
 // them); the new tracks follow, ordered by (first image, id) among themselves.
+constexpr int kPlanFromScratch = 1;   // build_appended: the extension is planned in full
+
 static int build_appended(PlanBuild& B, const PlanState& O) {
   const b3r_plan_desc& d = *B.d;
   const b3r_plan_desc& d0 = O.desc;
@@ -1037,6 +1070,10 @@ static int build_appended(PlanBuild& B, const PlanState& O) {
       if (B.elim[t]) nptr[t - T0 + 1]++;
     }
   for (int j = 0; j < nN; ++j) nptr[j + 1] += nptr[j];
+  // the new tracks are planned on one thread: a merge that adds more than a quarter of the
+  // observations (many frames at once) is planned from scratch on all of them (the structure
+  // is an extension all the same)
+  if (4 * (d.n_obs - d0.n_obs) > d0.n_obs) return kPlanFromScratch;
   std::vector<int> nobs(nptr[nN]);
   {
     std::vector<int> fill(nptr.begin(), nptr.end() - 1);
@@ -1219,7 +1256,14 @@ extern "C" int b3r_plan_append(b3r_plan** out, const b3r_plan* old, const b3r_pl
   init_build(B, desc);
   try {
     B3R_TRY(build_maps(B));
-    B3R_TRY(build_appended(B, *old->state));
+    const int rc = build_appended(B, *old->state);
+    if (rc == kPlanFromScratch) {
+      B3R_TRY(build_tracks(B));
+      B3R_TRY(build_segments(B));
+      B3R_TRY(build_pairs(B));
+    } else if (rc != B3R_OK) {
+      return rc;
+    }
     B3R_TRY(build_pattern(B));
     return finish_plan(B, out);
   } catch (const std::bad_alloc&) {
