@@ -65,7 +65,10 @@ def _append_candidate(key, n_imgs, n_obs, n_cams, n_nodes, n_tracks, C):
     if not _PLAN_CACHE:
         return None
     k, _, plan = _PLAN_CACHE[-1]
-    if not getattr(plan, 'retained', False) or k[5] != C or k[6] != key[6]:
+    # bool masks grow with the problem: compare flag kinds (the library checks that every old
+    # image and track keeps its status)
+    kinds = [tuple(m if isinstance(m, bool) else 'mask' for m in kk[6]) for kk in (k, key)]
+    if not getattr(plan, 'retained', False) or k[5] != C or kinds[0] != kinds[1]:
         return None
     if (plan.n_imgs <= n_imgs and plan.n_obs <= n_obs and plan.n_cams <= n_cams and plan.n_nodes <= n_nodes
             and plan.n_tracks <= n_tracks):

@@ -221,3 +221,26 @@ def test_solver_plans_online_frames_incrementally():
     p = BS.get_plan(t['rigs'], pids, s.n_cams, s.n_nodes, s.n_tracks, s.n_zcf, device='cpu')
     assert p.retained and not p.appended
     BS._PLAN_CACHE.clear()
+
+
+def test_solver_appends_with_growing_masks():
+    """Bool-tensor enable masks grow with the problem (one entry per node / image): the cache
+    still appends, and the plan equals a fresh one."""
+    seq = OnlineSequence(make_scene(3, n_imgs=16, n_tracks=900))
+    BS._PLAN_CACHE.clear()
+    try:
+        for q in range(6, 9):
+            s = seq.frame(q)
+            t = _frame_tensors(s)
+            mP = torch.ones(s.n_nodes, dtype=torch.bool)
+            mP[2] = False
+            mZ = torch.ones(s.n_imgs, dtype=torch.bool)
+            mZ[[1, 4]] = False
+            p = BS.get_plan(t['rigs'], t['pids'], s.n_cams, s.n_nodes, s.n_tracks, s.n_zcf, optim_P=mP,
+                            optim_Z=mZ, device='cpu')
+            assert p.appended == (q > 6)
+            fresh = BAPlan(t['rigs'], t['pids'], s.n_cams, s.n_nodes, s.n_tracks, s.n_zcf, optim_P=mP, optim_Z=mZ,
+                           device='cpu')
+            _assert_same_plan(p.handle, fresh.handle)
+    finally:
+        BS._PLAN_CACHE.clear()
