@@ -125,7 +125,7 @@ class GaussNewtonSolver:
         self.dampen = dampen
         self.adaptive_dampen = adaptive_dampen
         self.no_grad_f_from_rz = no_grad_f_from_rz
-        self.last_solve = {}
+        self._pcg_result = None
 
     def compute_jacobians(self, rigs, K, P_rig2cam, P_w2rig, z_coefs, pts3d, pids, pix2d_std, pix2d_dep,
                           is_depth_log, optim_Z_1st_cam=True, optim_Z0=True, optim_K=True, optim_Z=True,
@@ -170,7 +170,20 @@ class GaussNewtonSolver:
         J.system = J.plan.linearize(p, opts, z_prior=z_prior, objective=objective)
         return J.system
 
-    def solve_delta(self, J, residuals, w_pts, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
+    @property
+    def last_solve(self):
+        """Iterations and convergence of the last solve: dict(iters, converged)."""
+        return self.check_solve()
+
+    def check_solve(self):
+        """Reads the last solve's PCG status (one synchronisation when the solve was queued
+        with ``wait=False``); raises if a grid-barrier wait of the PCG kernel ran out."""
+        if self._pcg_result is None:
+            return {}
+        it, conv = BAPlan.pcg_status(self._pcg_result)
+        return dict(iters=it, converged=conv)
+
+    def solve_delta(self, J, residuals, w_pts, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None, wait=True):
         """delta = [delta_c, delta_p] solving (J^T W J + damping) delta = J^T W r through the
         Schur complement (ba_solver.py:110-182); float32 like the reference."""
         assert residuals.shape == (self.n_kpts, 3)
@@ -190,25 +203,27 @@ class GaussNewtonSolver:
                     raise TypeError('z_prior with a partial depth-coefficient mask is not supported')
                 zp = (H_z, g_z)
         s = self.linearize(J, residuals, w_pts, clamp_w, lin_kw, z_prior=zp)
-        return self._solve(s)
+        return self._solve(s, wait)
 
-    def solve_with_objective(self, J, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None):
+    def solve_with_objective(self, J, clamp_w=(1e-6, 1e6), z_prior=None, lin_kw=None, wait=True):
         """solve_delta for a linearization that recomputes residuals in-kernel (compute_jacobians
         given pix2d), which also returns the objective at the linearization point from the same
         passes: (delta, loss, residuals) with loss the mean Huber error over the (n_obs, 3)
         errors (0-d float32, what lm_step's objective computes, engine.py:263-281) and residuals
-        an (n_obs, 3) view."""
+        an (n_obs, 3) view.  ``wait=False`` (also for solve_delta) returns without reading the
+        PCG's status back: the caller queues more work and calls ``check_solve`` later."""
         assert J.tensors['pix2d'] is not None, 'the objective needs in-kernel residuals (pix2d)'
         s = self.linearize(J, None, None, clamp_w, lin_kw, z_prior=z_prior, objective=True)
         loss = (s.loss_sum[0] / max(3 * self.n_kpts, 1)).to(torch.float32)
-        return self._solve(s), loss, s.residuals.transpose(0, 1)
+        return self._solve(s, wait), loss, s.residuals.transpose(0, 1)
 
-    def _solve(self, s):
+    def _solve(self, s, wait=True):
         dt = torch.float64 if self.dtype == torch.float64 else torch.float32
         # the reference's PCG (ba_solver.py:202, 1197-1238) as one device kernel on the explicit S
-        delta_c, niter, conv = s.plan.pcg(s.S_vals, s.precond, s.b.to(dt), tol=1e-6, maxiter=300)
+        delta_c, self._pcg_result = s.plan.pcg(s.S_vals, s.precond, s.b.to(dt), tol=1e-6, maxiter=300, wait=False)
+        if wait:
+            self.check_solve()
         delta_p = s.backsub(delta_c.to(torch.float32))
-        self.last_solve = dict(iters=niter, converged=conv)
         return torch.cat([delta_c.to(torch.float32), delta_p])
 
     def unpack_delta_inplace(self, delta):

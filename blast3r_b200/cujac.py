@@ -211,4 +211,27 @@ def hat_se3(xi):
 
 
 def exp_se3(xi):
-    return torch.matrix_exp(hat_se3(xi))
+    """exp(hat_se3(xi)), the matrix exponential the reference takes with torch.matrix_exp, in
+    closed form: with w = xi[:, :3] (angle th = |w|, W = [w]x) and v = xi[:, 3:],
+    R = I + A W + B W^2 and t = (I + B W + C W^2) v, A = sin(th)/th, B = (1 - cos th)/th^2,
+    C = (th - sin th)/th^3 (Rodrigues' formula and the left Jacobian of SE(3); Barfoot,
+    "State Estimation for Robotics", 2017, sec. 7.1.3), Taylor series below th = 1e-3, in
+    float64.  Batched torch.matrix_exp reads its squaring counts back to the host; this form
+    keeps the line search free of that synchronisation."""
+    x = xi.to(torch.float64)
+    w, v = x[:, :3], x[:, 3:]
+    th2 = (w * w).sum(-1)
+    small = th2 < 1e-6
+    th = torch.where(small, torch.ones_like(th2), th2).sqrt()
+    s, c = torch.sin(th), torch.cos(th)
+    A = torch.where(small, 1 - th2 / 6 + th2 * th2 / 120, s / th)
+    B = torch.where(small, 0.5 - th2 / 24 + th2 * th2 / 720, (1 - c) / (th * th))
+    Cc = torch.where(small, 1 / 6 - th2 / 120 + th2 * th2 / 5040, (th - s) / (th * th * th))
+    W = skew_symmetric(w, device=xi.device)
+    W2 = W @ W
+    eye = torch.eye(3, dtype=torch.float64, device=xi.device)
+    out = x.new_zeros((len(x), 4, 4))
+    out[:, :3, :3] = eye + A[:, None, None] * W + B[:, None, None] * W2
+    out[:, :3, 3] = ((eye + B[:, None, None] * W + Cc[:, None, None] * W2) @ v[:, :, None])[:, :, 0]
+    out[:, 3, 3] = 1
+    return out.to(xi.dtype)

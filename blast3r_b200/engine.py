@@ -175,20 +175,24 @@ def lm_step(rigs, pids, pix2d, pix2d_std, pix2d_dep, K, P_rig2cam, P_w2rig, z_co
                               optim_X=optim_X, is_depth_log=is_depth_log,
                               pix2d=pix2d if recompute_residuals else None)
     lin_kw = dict(weight_z=weight_z, pnorm=pnorm, max_pix_err=clip_pix_err, huber_delta=huber_delta)
+    # The solve is queued without reading its status back, so that the back-substitution and
+    # the first line-search trial are queued while the PCG kernel runs; its status is checked
+    # once the line search has synchronised anyway.
     if recompute_residuals:
         # the objective at the current parameters comes out of the linearization's own passes
         # (the same residuals and Huber errors the residual op computes)
-        delta, init_loss, init_residuals = jac.solve_with_objective(J, z_prior=z_prior, lin_kw=lin_kw)
+        delta, init_loss, init_residuals = jac.solve_with_objective(J, z_prior=z_prior, lin_kw=lin_kw, wait=False)
         if tan_loss0 is not None:
             init_loss = init_loss + tan_loss0.to(init_loss.dtype)
     else:
         init_loss, init_residuals, w_pts = objective(K, P_w2rig, pts3d, z_coefs, need_w=True)
-        delta = jac.solve_delta(J, init_residuals, w_pts, z_prior=z_prior, lin_kw=lin_kw)
+        delta = jac.solve_delta(J, init_residuals, w_pts, z_prior=z_prior, lin_kw=lin_kw, wait=False)
     delta_K, delta_P, delta_zcf, delta_pts = jac.unpack_delta_inplace(delta)
 
     update, new_loss, new_residuals = line_search(objective, K, P_w2rig, z_coefs, pts3d, delta, delta_K, delta_P,
                                                   delta_zcf, delta_pts, init_loss, init_residuals, min_reproj,
                                                   min_loss_delta, verbose)
+    jac.check_solve()
     return update, BA_Status(init_loss, init_residuals, new_loss, new_residuals)
 
 

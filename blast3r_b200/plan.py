@@ -254,11 +254,14 @@ class BAPlan:
         L.call(name, self._h, S_vals.data_ptr(), x.contiguous().data_ptr(), y.data_ptr(), s)
         return y
 
-    def pcg(self, S_vals, precond, b, tol=1e-6, maxiter=300, barrier_spin_limit=0, flags=0, raw=False):
+    def pcg(self, S_vals, precond, b, tol=1e-6, maxiter=300, barrier_spin_limit=0, flags=0, raw=False, wait=True):
         """Solve S x = b on the device (b3r_pcg_ex): the reference's PCG iteration and
         stopping rule, one cooperative kernel.  Returns (x, iterations, converged); raises if a
         grid-barrier wait ran out (with ``raw``, returns (x, iterations, converged, error)
-        instead).  ``barrier_spin_limit`` bounds every barrier wait (0: the library's default)."""
+        instead).  ``barrier_spin_limit`` bounds every barrier wait (0: the library's default).
+        With ``wait=False`` nothing is read back: returns (x, result), result the device int32
+        [iterations, converged, error, replacements] that ``pcg_status`` reads later, so that
+        the host can queue the work that follows while the solve runs."""
         assert b.dtype in (torch.float32, torch.float64)
         b = b.contiguous()
         x = torch.empty_like(b)
@@ -268,12 +271,23 @@ class BAPlan:
         L.call('b3r_pcg_ex', self._h, S_vals.data_ptr(), precond.contiguous().data_ptr(), b.data_ptr(), x.data_ptr(),
                dt, float(tol), int(maxiter), int(barrier_spin_limit), int(flags), work.data_ptr(), res.data_ptr(),
                torch.cuda.current_stream().cuda_stream)
+        if not wait:
+            return x, res
         it, conv, err = res[:3].tolist()
         if raw:
             return x, int(it), bool(conv), int(err)
         if err:
             raise L.B3RError('b3r_pcg: a grid barrier of the PCG kernel gave up')
         return x, int(it), bool(conv)
+
+    @staticmethod
+    def pcg_status(res):
+        """(iterations, converged) of a ``pcg(..., wait=False)`` result; raises if a grid-barrier
+        wait of that solve ran out."""
+        it, conv, err = res[:3].tolist()
+        if err:
+            raise L.B3RError('b3r_pcg: a grid barrier of the PCG kernel gave up')
+        return int(it), bool(conv)
 
     def backsub(self, params, opts, workspace_ptr, delta_c, delta_p=None):
         if delta_p is None:

@@ -207,7 +207,8 @@ int b3r_plan_create(b3r_plan** plan, const b3r_plan_desc* desc);
  * tracks are sorted, paired and bucketed, and the S pattern and solver tables are rebuilt.
  * The result is a plan for `desc` like b3r_plan_create's (same S pattern, same systems up
  * to summation order); it retains its own state when desc->retain is set.  `old` is not
- * changed.  Returns B3R_E_INVALID, naming the first difference, when `desc` does not
+ * changed.  A merge that adds more than a quarter of the observations (many frames at once)
+ * is planned in full inside the call.  Returns B3R_E_INVALID, naming the first difference, when `desc` does not
  * extend `old` (track removal, reordering, other rules), in which case the caller plans
  * from scratch.  No counterpart in the reference, which rediscovers the structure every
  * iteration (ba_solver.py:854-924). */

@@ -2,6 +2,7 @@
 compute_jacobians (host-only plan on CPU tensors), plan caching, column counts after
 enabling, and unpack_delta_inplace (ba_solver.py:72-108, 228-248)."""
 import numpy as np
+import pytest
 import torch
 
 from blast3r_b200 import ba_solver as BS
@@ -69,3 +70,15 @@ def test_plan_cache_sees_a_reordering_of_pids():
     t['pids'][i] = t['pids'][i + 1000003]      # an in-place edit of the tensor the plan was built from
     J4 = s.compute_jacobians(*args, t['pids'], t['pix2d_std'], t['pix2d_dep'], is_depth_log=True)
     assert J4.plan is not J.plan
+
+
+@pytest.mark.parametrize('scale', [0.0, 1e-7, 1e-4, 1e-3, 2e-3, 0.1, 1.0, 3.0])
+def test_exp_se3_equals_matrix_exponential(scale):
+    """cujac.exp_se3 (closed form) against the reference's torch.matrix_exp(hat_se3(xi))
+    (extensions/cujac/__init__.py:56-58), float64, across the small-angle series threshold."""
+    from blast3r_b200.cujac import exp_se3, hat_se3
+    g = torch.Generator().manual_seed(7)
+    xi = torch.randn(300, 6, dtype=torch.float64, generator=g) * scale
+    want = torch.matrix_exp(hat_se3(xi))
+    assert (exp_se3(xi) - want).abs().max().item() < 1e-13
+    assert exp_se3(xi.float()).dtype == torch.float32
