@@ -679,13 +679,15 @@ __global__ void __launch_bounds__(kDiagThreads, 6) k_diag(Ctx c, float* __restri
     for (int j = 0; j < NGL; ++j) {
       const int g = lane + 32 * j;
       if (g < NG) {                 // columns 4g..4g+3 (those >= N are never emitted)
-        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        // packed float2 adds: the same sums, in the same order, in half the instructions
+        float2 t01 = make_float2(0.f, 0.f), t23 = make_float2(0.f, 0.f);
 #pragma unroll 8
         for (int l = 0; l < 32; ++l) {
           const float4 x = *reinterpret_cast<const float4*>(rw + l * RS + 4 * g);
-          t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+          t01 = __fadd2_rn(t01, make_float2(x.x, x.y));
+          t23 = __fadd2_rn(t23, make_float2(x.z, x.w));
         }
-        run[j].x += t.x; run[j].y += t.y; run[j].z += t.z; run[j].w += t.w;
+        run[j].x += t01.x; run[j].y += t01.y; run[j].z += t23.x; run[j].w += t23.y;
       }
     }
     __syncwarp();
