@@ -16,6 +16,8 @@ running a matrix-free PCG on the implicit Schur complement (ba_solver.py:184-206
 residuals and weights in-kernel (identical values: one shared device function); without
 it they read the ``residuals`` / ``w_pts`` handed to ``solve_delta``, as the reference does.
 """
+import weakref
+
 import torch
 
 from . import _lib as L
@@ -59,6 +61,34 @@ def _same(a, b):
     return a.shape == b.shape and a.dtype == b.dtype and a.device == b.device and torch.equal(a, b)
 
 
+def _version(t):
+    """The tensor's in-place modification counter (None for inference tensors, which keep none)."""
+    try:
+        return t._version
+    except RuntimeError:
+        return None
+
+
+def _saved(cur):
+    """What the cache keeps of a plan's structure tensors: a copy of each, a weak reference to
+    the caller's tensor and its modification counter."""
+    return [(t.detach().clone(), weakref.ref(t), _version(t)) for t in cur]
+
+
+def _matches(cur, saved):
+    """The structure tensors hold the saved values: each is the very tensor the plan was built
+    from, not modified in place since (its counter unchanged: no device comparison, no
+    synchronisation), or equal element by element to the saved copy."""
+    if len(cur) != len(saved):
+        return False
+    for a, (copy, ref, ver) in zip(cur, saved):
+        if ver is not None and ref() is a and _version(a) == ver:
+            continue
+        if not _same(a, copy):
+            return False
+    return True
+
+
 def _append_candidate(key, n_imgs, n_obs, n_cams, n_nodes, n_tracks, C):
     """The most recently used cached plan that kept its host state, if the new structure can
     extend it (sizes only grow, same C and enable flags); b3r_plan_append checks the rest."""
@@ -80,9 +110,10 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
              optim_X=True, device=None):
     """Plan for this structure, reused while the structure tensors hold the same values.
 
-    A cached plan is returned only when ``rigs``, ``pids`` and every bool mask are equal,
-    element by element, to the copies taken when it was built (one device comparison per
-    call), so a reordering or an in-place edit of the structure always gets a new plan.  A
+    A cached plan is returned only when ``rigs``, ``pids`` and every bool mask are the tensors
+    it was built from, unmodified since, or equal element by element to the copies taken then
+    (one device comparison), so a reordering or an in-place edit of the structure always gets a
+    new plan.  A
     structure that extends the last plan's the way the online loop merges tracks gets its plan
     by b3r_plan_append (incremental: only the new tracks are planned)."""
     modes = (optim_K, optim_P, optim_Z, optim_X)
@@ -90,7 +121,7 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
            tuple(m if isinstance(m, bool) else ('mask', tuple(m.shape)) for m in modes))
     cur = _structure(rigs, pids, modes)
     for j, (k, saved, plan) in enumerate(_PLAN_CACHE):
-        if k == key and len(saved) == len(cur) and all(_same(a, b) for a, b in zip(cur, saved)):
+        if k == key and _matches(cur, saved):
             _PLAN_CACHE.append(_PLAN_CACHE.pop(j))
             return plan
     retain = len(pids) <= INCREMENTAL_MAX_OBS
@@ -107,7 +138,7 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
                       optim_Z=optim_Z, optim_X=optim_X, device=device, retain=retain)
     if len(_PLAN_CACHE) >= _PLAN_CACHE_MAX:
         _PLAN_CACHE.pop(0)
-    _PLAN_CACHE.append((key, [t.detach().clone() for t in cur], plan))
+    _PLAN_CACHE.append((key, _saved(cur), plan))
     return plan
 
 

@@ -82,3 +82,27 @@ def test_exp_se3_equals_matrix_exponential(scale):
     want = torch.matrix_exp(hat_se3(xi))
     assert (exp_se3(xi) - want).abs().max().item() < 1e-13
     assert exp_se3(xi.float()).dtype == torch.float32
+
+
+def test_plan_cache_sees_in_place_edits_of_the_same_tensor():
+    """The same structure tensors, unmodified, reuse the plan without a comparison; an in-place
+    edit of them (here two observations of an image swapped) gets a new plan, and so does an
+    edit inside inference mode, whose tensors keep no modification counter."""
+    sc = make_scene(0, n_imgs=8, n_tracks=100)
+    orig = sc.pids.copy()
+    t = _t(sc)                       # shares memory with sc's arrays
+    BS._PLAN_CACHE.clear()
+    try:
+        p1 = BS.get_plan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, device='cpu')
+        assert BS.get_plan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, device='cpu') is p1
+        t['pids'][[0, 1]] = t['pids'][[1, 0]].clone()
+        p2 = BS.get_plan(t['rigs'], t['pids'], sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, device='cpu')
+        assert p2 is not p1
+        with torch.inference_mode():
+            pids = torch.from_numpy(orig.copy())
+            p3 = BS.get_plan(t['rigs'], pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, device='cpu')
+            assert p3 is p1
+            pids[[0, 1]] = pids[[1, 0]].clone()
+            assert BS.get_plan(t['rigs'], pids, sc.n_cams, sc.n_nodes, sc.n_tracks, sc.n_zcf, device='cpu') is p2
+    finally:
+        BS._PLAN_CACHE.clear()
