@@ -44,7 +44,10 @@ class Linearization:
 
 
 _PLAN_CACHE = []        # (key, structure tensors, plan), most recent last
-_PLAN_CACHE_MAX = 8
+# The online loop (inference/pipeline.py:212-224) runs a global BA every gba_step = 8 frames and
+# a frozen single-frame BA on the others: 16 plans keep the last global BA's plans (one per
+# phase) in the cache for the next global BA to extend.
+_PLAN_CACHE_MAX = 16
 # Plans of at most this many observations keep their host-side lists, so that the next
 # structure of an online loop (the merge old | new of inference/pipeline.py:196-224) is planned
 # incrementally (b3r_plan_append); the host memory they hold is about 40 B per observation plus
@@ -90,19 +93,18 @@ def _matches(cur, saved):
 
 
 def _append_candidate(key, n_imgs, n_obs, n_cams, n_nodes, n_tracks, C):
-    """The most recently used cached plan that kept its host state, if the new structure can
-    extend it (sizes only grow, same C and enable flags); b3r_plan_append checks the rest."""
-    if not _PLAN_CACHE:
-        return None
-    k, _, plan = _PLAN_CACHE[-1]
-    # bool masks grow with the problem: compare flag kinds (the library checks that every old
-    # image and track keeps its status)
-    kinds = [tuple(m if isinstance(m, bool) else 'mask' for m in kk[6]) for kk in (k, key)]
-    if not getattr(plan, 'retained', False) or k[5] != C or kinds[0] != kinds[1]:
-        return None
-    if (plan.n_imgs <= n_imgs and plan.n_obs <= n_obs and plan.n_cams <= n_cams and plan.n_nodes <= n_nodes
-            and plan.n_tracks <= n_tracks):
-        return plan
+    """The most recently used cached plan that kept its host state and that the new structure
+    may extend (sizes only grow, same C and enable flags; b3r_plan_append checks the rest).
+    The whole cache is searched: in the online loop the plans of the frozen single-frame BAs
+    come between two global BAs."""
+    def kinds(k):           # bool masks grow with the problem: compare flag kinds (the library
+        return tuple(m if isinstance(m, bool) else 'mask' for m in k[6])   # checks each old status)
+    for k, _, plan in reversed(_PLAN_CACHE):
+        if not getattr(plan, 'retained', False) or k[5] != C or kinds(k) != kinds(key):
+            continue
+        if (plan.n_imgs <= n_imgs and plan.n_obs <= n_obs and plan.n_cams <= n_cams and plan.n_nodes <= n_nodes
+                and plan.n_tracks <= n_tracks and plan.n_obs > 0):
+            return plan
     return None
 
 

@@ -244,3 +244,32 @@ def test_solver_appends_with_growing_masks():
             _assert_same_plan(p.handle, fresh.handle)
     finally:
         BS._PLAN_CACHE.clear()
+
+
+def test_solver_appends_across_frozen_single_frame_plans():
+    """The online loop's pattern (inference/pipeline.py:212-224): a global BA on the merged
+    problem every few frames and, between them, frozen BAs of the new frame alone (one image,
+    points fixed).  The next global BA's plan is appended to the last global one, not planned
+    from scratch, although other plans were built in between; under inference mode, as the
+    reference's online loop runs."""
+    seq = OnlineSequence(make_scene(3, n_imgs=24, n_tracks=1500))
+    BS._PLAN_CACHE.clear()
+    try:
+        with torch.inference_mode():
+            for q in (12, 16, 20):
+                s = seq.frame(q)
+                t = _frame_tensors(s)
+                p = BS.get_plan(t['rigs'], t['pids'], s.n_cams, s.n_nodes, s.n_tracks, s.n_zcf, device='cpu')
+                assert p.appended == (q > 12)
+                fresh = BAPlan(t['rigs'], t['pids'], s.n_cams, s.n_nodes, s.n_tracks, s.n_zcf, device='cpu')
+                _assert_same_plan(p.handle, fresh.handle)
+                for f in range(q + 1, q + 4):        # frozen BAs of the next frames alone
+                    sf = seq.frame(f)
+                    img = np.repeat(np.arange(sf.n_imgs), np.diff(np.concatenate([[0], sf.infos[0]])))
+                    sel = img == f
+                    pids = np.unique(sf.pids[sel], return_inverse=True)[1].astype(np.int32)
+                    rigs = torch.tensor([[int(sel.sum())], [0], [0]], dtype=torch.int32)
+                    BS.get_plan(rigs, torch.from_numpy(pids), 1, 1, int(pids.max()) + 1, s.n_zcf, optim_X=False,
+                                device='cpu')
+    finally:
+        BS._PLAN_CACHE.clear()
