@@ -116,7 +116,7 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
     it was built from, unmodified since, or equal element by element to the copies taken then
     (one device comparison), so a reordering or an in-place edit of the structure always gets a
     new plan.  A
-    structure that extends the last plan's the way the online loop merges tracks gets its plan
+    structure that extends a cached plan's the way the online loop merges tracks gets its plan
     by b3r_plan_append (incremental: only the new tracks are planned)."""
     modes = (optim_K, optim_P, optim_Z, optim_X)
     key = (tuple(rigs.shape), tuple(pids.shape), n_cams, n_nodes, n_tracks, C,
@@ -133,7 +133,7 @@ def get_plan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=True, optim_P=Tru
         try:
             plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
                           optim_Z=optim_Z, optim_X=optim_X, device=device, retain=True, base=base)
-        except L.B3RError:     # not an extension of the last plan (tracks removed, reordered...)
+        except L.B3RError:     # not an extension of that plan (tracks removed, reordered...)
             plan = None
     if plan is None:
         plan = BAPlan(rigs, pids, n_cams, n_nodes, n_tracks, C, optim_K=optim_K, optim_P=optim_P,
