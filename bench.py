@@ -194,7 +194,7 @@ def channel_subset(sc, C):
 
 
 # ------------------------------------------------------------------------------------------
-# roofline bookkeeping
+# roofline bookkeeping: compulsory fp32 bytes of one linearization
 # ------------------------------------------------------------------------------------------
 def algorithmic_bytes(n_obs, n_tracks, plan_info, block_size):
     """Compulsory bytes of one linearization (fp32): per observation pix2d 8 + std 8 +
@@ -466,7 +466,7 @@ def measure_workload(wl, steps, warmup, peak, peak_kind, want_clocks, e2e_steps)
     sc, plan = wl.sc, wl.plan
     passes = pass_times(wl)
     dom = max((k for k in passes if k not in ('prep', 'finalize')), key=lambda k: passes[k]['ms'])
-    # SURVEY 8(d) bytes of what this rank processes: its observations and tracks, and S, b
+    # compulsory bytes of what this rank processes: its observations and tracks, and S, b
     B, nnz_upper = algorithmic_bytes(wl.n_local, wl.tracks_local, plan.info, plan.block_size)
     dom_ms = passes[dom]['ms']
     R = int(plan.info.record_floats)
