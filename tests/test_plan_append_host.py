@@ -273,3 +273,32 @@ def test_solver_appends_across_frozen_single_frame_plans():
                                 device='cpu')
     finally:
         BS._PLAN_CACHE.clear()
+
+
+def test_append_refuses_status_changes_of_old_images_and_tracks():
+    """Old images keep their node, camera and active blocks, old tracks their point status:
+    a change of any of them is refused (the old lists would no longer describe them)."""
+    seq = OnlineSequence(make_scene(3, n_imgs=16, n_tracks=800))
+    s6, s7 = seq.frame(6), seq.frame(7)
+    base = _create(s6, masks=dict(Z=np.ones(s6.n_imgs, bool)))
+    try:
+        infos = s7.infos.copy()
+        infos[2, 3] = 5                               # image 3 now uses camera 5
+        with pytest.raises(L.B3RError, match='node or camera'):
+            _append(base, _variant(s7, infos=infos), masks=dict(Z=np.ones(s7.n_imgs, bool)))
+        mZ = np.ones(s7.n_imgs, bool)
+        mZ[2] = False                                 # image 2's depth coefficients switched off ...
+        keep = []
+        d = _desc(s7, keep, masks=dict(Z=mZ))
+        d.mode_K = d.mode_P = L.ENABLE_ZERO           # ... and its focal and pose too: image 2 has no block
+        h = C.c_void_p()
+        with pytest.raises(L.B3RError, match='active blocks'):
+            L.call('b3r_plan_append', C.byref(h), base, C.byref(d))
+        mX = np.ones(s7.n_tracks, bool)
+        mX[0] = False                                 # track 0's point no longer optimised
+        with pytest.raises(L.B3RError, match='point status'):
+            _append(base, s7, masks=dict(Z=np.ones(s7.n_imgs, bool), X=mX))
+        ok = _append(base, s7, masks=dict(Z=np.ones(s7.n_imgs, bool)))
+        L.call('b3r_plan_destroy', ok)
+    finally:
+        L.call('b3r_plan_destroy', base)
