@@ -302,3 +302,20 @@ def test_append_refuses_status_changes_of_old_images_and_tracks():
         L.call('b3r_plan_destroy', ok)
     finally:
         L.call('b3r_plan_destroy', base)
+
+
+def test_online_sequence_matches_the_reference_merge():
+    """synthetic.OnlineSequence builds, frame by frame, exactly the problems the reference's own
+    ObservedTracks.__or__ produces in its online loop (golden vectors from
+    tests/golden/make_golden_merge.py: observations per image, track ids, keypoints)."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden', 'refmerge_online.npz'))
+    sc = make_scene(3, n_imgs=12, n_tracks=400, seed=301)
+    assert np.array_equal(sc.pids, z['scene_pids']) and np.array_equal(sc.pix2d, z['scene_pix2d'])
+    seq = OnlineSequence(sc)
+    for q in range(sc.n_imgs):
+        f = seq.frame(q)
+        assert f.n_tracks == int(z[f'f{q}_n_tracks'])
+        assert np.array_equal(np.diff(np.concatenate([[0], f.infos[0]])), z[f'f{q}_nppi'])
+        assert np.array_equal(f.pids, z[f'f{q}_pids'])
+        assert np.array_equal(f.pix2d, z[f'f{q}_pix2d'])
