@@ -319,3 +319,27 @@ def test_online_sequence_matches_the_reference_merge():
         assert np.array_equal(np.diff(np.concatenate([[0], f.infos[0]])), z[f'f{q}_nppi'])
         assert np.array_equal(f.pids, z[f'f{q}_pids'])
         assert np.array_equal(f.pix2d, z[f'f{q}_pix2d'])
+
+
+def test_append_edge_cases_empty_problems_and_empty_frames():
+    """Appending to an empty problem (frame 0 holds no track yet), and a merge that adds an
+    image without any observation (a frame whose tracks all continue later): both give the
+    fresh plan."""
+    seq = OnlineSequence(make_scene(3, n_imgs=10, n_tracks=500))
+    s0, s1, s2 = seq.frame(0), seq.frame(1), seq.frame(2)
+    assert s0.n_obs == 0 and s0.n_tracks == 0
+    h0 = _create(s0)
+    h1 = _append(h0, s1)
+    f1 = _create(s1, retain=0)
+    _assert_same_plan(h1, f1)
+    h2 = _append(h1, s2)
+    f2 = _create(s2, retain=0)
+    _assert_same_plan(h2, f2)
+    # one more image with no observation, same tracks
+    infos = np.concatenate([s2.infos, np.array([[s2.infos[0, -1]], [s2.n_imgs], [s2.n_imgs]], np.int32)], 1)
+    s3 = _variant(s2, infos=infos, n_imgs=s2.n_imgs + 1, n_nodes=s2.n_nodes + 1, n_cams=s2.n_cams + 1)
+    h3 = _append(h2, s3)
+    f3 = _create(s3, retain=0)
+    _assert_same_plan(h3, f3)
+    for h in (h0, h1, f1, h2, f2, h3, f3):
+        L.call('b3r_plan_destroy', h)
